@@ -1,0 +1,31 @@
+/* mpkmeans_debug.h -- test hooks of libmpkmeans_b200.  No counterpart in the
+ * reference: they expose engine internals to the parity tests. */
+#ifndef MPKMEANS_B200_DEBUG_H
+#define MPKMEANS_B200_DEBUG_H
+
+#include "mpkmeans.h"
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* While dOut4 is non-NULL, every assignment of engine e writes, per row, the
+ * tensor-core best and runner-up distances and their centroids as
+ * (v0, v1, j0 bits, j1 bits) to dOut4 (n float4 on the device). */
+mpkStatus mpkDebugSetAssignTrace(mpkEngine e, float* dOut4);
+
+/* Operand scale s, subnormal floor eta = 2^-25/s, fixed-point fraction bits,
+ * and the two error-bound constants of the assignment filter. */
+mpkStatus mpkDebugEngineInfo(mpkEngine e, float* scale, float* eta, int* frac, float* c1, float* c2);
+
+#ifdef __cplusplus
+}
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#endif /* MPKMEANS_B200_DEBUG_H */

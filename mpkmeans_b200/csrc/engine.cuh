@@ -1,0 +1,92 @@
+/* engine.cuh -- internal interfaces of the B200 k-means engine.
+ *
+ * HBM layout of one engine (one GPU, one shard of rows):
+ *   P      n x d FP32, row major, caller owned, never modified
+ *   Xs     2 x n x dp FP16: plane 0 = hi, plane 1 = lo of s*P, dp = d rounded
+ *          up to 64 (zero padded); split once per fit
+ *   xnorm  n FP32: ||p_i|| (only feeds the error bound)
+ *   Cs     2 x k x dp FP16: hi/lo of s*C, re-split every iteration
+ *   cn     kpad FP32: ||c_j||^2 in the reference's tree order; +inf past k
+ *   list   refinement entries (row + up to 4 candidates), capacity n
+ *   sums   k*d int64 fixed-point coordinate sums, then k int64 counts
+ *   prm    DevParams (scales, status word, counters)
+ */
+#pragma once
+
+#include "common.cuh"
+
+namespace mpk {
+
+struct DevParams {
+    float pmax;          /* max |P| over the whole problem (all shards)        */
+    float c0max;         /* max |C0| at the start of the fit                   */
+    float scale;         /* FP16 operand scale s (a power of two)              */
+    float neg2_inv_s2;   /* -2 / s^2, folds the scale out of the products      */
+    float eta;           /* 2^-25 / s: absolute floor of a subnormal FP16 word */
+    int   frac;          /* fractional bits of the fixed-point update          */
+    int   status;        /* MPK_DEV_* bits                                     */
+    unsigned int nflag;  /* refinement entries written by the last assign      */
+    unsigned long long nflag_total;  /* refinement entries over the run       */
+    unsigned long long ncand_total;  /* candidate centroids refined, over run */
+    unsigned long long novf_total;   /* rows refined against all k centroids  */
+};
+
+struct RefineEntry {
+    int row;
+    int ovf;             /* 1: candidate list may be incomplete, scan all k */
+    int c[4];            /* candidate centroids, -1 when unused             */
+};
+
+/* Error-bound constants of the assignment filter (host computed). */
+struct BoundConsts {
+    float c1;            /* multiplies ||x|| * max_j ||c_j||                */
+    float c2;            /* multiplies eta * (||x|| + max_j ||c_j||)        */
+};
+
+/* ---- prep (kernels.cu) ---- */
+void launch_maxabs(const float* A, long long count, float* out, cudaStream_t s);
+void launch_set_scale(DevParams* prm, long long n_total, cudaStream_t s);
+void launch_split_rows(const float* src, long long rows, int d, int dp, const DevParams* prm,
+                       __half* planes, long long plane_stride, float* norms, cudaStream_t s);
+void launch_prep_c(const float* C, int k, int kpad, int d, int dp, DevParams* prm,
+                   __half* planes, float* cn, cudaStream_t s);
+
+/* ---- assign (assign_tc.cu) ---- */
+struct AssignArgs {
+    const CUtensorMap* tmX;   /* host copies, passed by value to the kernel */
+    const CUtensorMap* tmC;
+    long long n;
+    int k, d, dp;
+    const float* xnorm;
+    const float* cn;
+    const DevParams* prm_ro;
+    DevParams* prm;
+    int* labels;
+    RefineEntry* list;
+    int refine;               /* 0: trust the emulated argmin outright      */
+    BoundConsts bc;
+    int num_sms;
+    float4* dbg;              /* optional: (v0, v1, j0, j1) per row, test hook */
+};
+int  assign_bn_for(int k);                   /* N tile width chosen for k     */
+int  assign_supported(int d);                /* 1 when d fits the kernel      */
+cudaError_t launch_assign(const AssignArgs& a, cudaStream_t s);
+
+/* ---- refine / update (kernels.cu) ---- */
+void launch_refine(const float* P, const float* C, const float* cn, int d, int k,
+                   const RefineEntry* list, DevParams* prm, int* labels, long long n_cap,
+                   unsigned long long* hist_slot, int num_sms, cudaStream_t s);
+void launch_accum_fixed(const float* P, long long n, int d, const int* labels, int k,
+                        DevParams* prm, long long* sums, long long* counts, int num_sms, cudaStream_t s);
+void launch_finalize_fixed(const long long* sums, const long long* counts, int k, int d,
+                           const DevParams* prm, float* C, float* moved2, cudaStream_t s);
+void launch_inertia(const float* P, const float* C, const int* labels, long long n, int d,
+                    double* out, cudaStream_t s);
+void launch_count_diff(const int* a, const int* b, long long n, unsigned long long* out, cudaStream_t s);
+void launch_add_const(float* p, long long count, float c, cudaStream_t s);
+void launch_standardize(float* P, int n, int d, cudaStream_t s);
+
+/* ---- tensor maps (engine host code) ---- */
+bool make_tmap_planes(CUtensorMap* map, const __half* base, long long rows, int dp, int box_rows);
+
+}  /* namespace mpk */

@@ -1,0 +1,455 @@
+/* kernels.cu -- SIMT kernels of the B200 k-means engine: operand preparation,
+ * near-tie refinement, the fixed-point centroid update and bookkeeping.
+ *
+ * All FP32 arithmetic whose result must match the reference bit for bit is
+ * written with explicit fmaf() and compiled with -fmad=false, so no other
+ * operation is contracted.
+ */
+#include "engine.cuh"
+
+#include <cmath>
+
+namespace mpk {
+namespace {
+
+constexpr unsigned FULL = 0xffffffffu;
+
+/* ------------------------------------------------------------- max |A| --- */
+
+__global__ void k_maxabs(const float* __restrict__ A, long long count, float* out) {
+    float m = 0.f;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long n4 = (((uintptr_t)A & 15) == 0) ? count / 4 : 0;
+    const float4* A4 = reinterpret_cast<const float4*>(A);
+    for (long long t = i; t < n4; t += stride) {
+        const float4 v = A4[t];
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+    for (long long t = 4 * n4 + i; t < count; t += stride) m = fmaxf(m, fabsf(A[t]));
+    m = warp_max(m);   /* NaN entries are dropped by fmaxf */
+    if ((threadIdx.x & 31) == 0 && m > 0.f) atomicMax(reinterpret_cast<unsigned int*>(out), __float_as_uint(m));
+}
+
+/* Operand scale and update precision, from the maxima, on the device (no host
+ * round trip):
+ *   scale s = largest power of two with s * max|P, C0| <= 4096, the rule of
+ *             gemm-emulation/src/split_fp16.cu:255-262, so hi words sit well
+ *             inside FP16's normal range and lo words keep 11 bits;
+ *   frac    = 62 - E - ceil(log2 n) with max|P| < 2^E, so that n quantised
+ *             coordinates of magnitude < 2^(E+frac) sum below 2^62. */
+__global__ void k_set_scale(DevParams* prm, long long n_total) {
+    const float m = fmaxf(prm->pmax, prm->c0max);
+    float s = 1.f;
+    if (m > 0.f && isfinite(m)) {
+        int e = 0;
+        frexpf(4096.0f / m, &e);
+        s = ldexpf(1.0f, e - 1);
+        if (!(s > 0.f) || !isfinite(s)) s = 1.f;
+    }
+    prm->scale = s;
+    prm->neg2_inv_s2 = -2.0f / (s * s);
+    prm->eta = ldexpf(1.0f, -25) / s;
+    int E = 0;
+    if (prm->pmax > 0.f && isfinite(prm->pmax)) frexpf(prm->pmax, &E);
+    int lg = 0;
+    while ((1ll << lg) < n_total && lg < 62) ++lg;
+    int frac = 62 - E - lg;
+    if (frac > 200) frac = 200;
+    prm->frac = frac;
+}
+
+/* ------------------------------------------------------------- splits ---- */
+
+/* One warp per row: hi = fp16(s*x), lo = fp16(s*x - hi); both planes row major
+ * with leading dimension dp (zero padded past d).  norms[i] = ||x_i|| (FP32,
+ * any order: it only feeds the error bound, which inflates it). */
+__global__ void k_split_rows(const float* __restrict__ src, long long rows, int d, int dp,
+                             const DevParams* __restrict__ prm, __half* __restrict__ planes,
+                             long long plane_stride, float* __restrict__ norms) {
+    const int lane = threadIdx.x & 31;
+    const long long wstride = (long long)gridDim.x * (blockDim.x >> 5);
+    const float s = prm->scale;
+    for (long long i = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < rows; i += wstride) {
+        const float* x = src + (size_t)i * d;
+        __half* hi = planes + (size_t)i * dp;
+        __half* lo = hi + plane_stride;
+        float acc = 0.f;
+        for (int t = lane; t < dp; t += 32) {
+            const float v = t < d ? x[t] : 0.f;
+            acc = fmaf(v, v, acc);
+            const float a = v * s;
+            const __half h = __float2half_rn(a);
+            const float r = a - __half2float(h);
+            hi[t] = h;
+            lo[t] = __float2half_rn(r);
+        }
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(FULL, acc, o);
+        if (norms && lane == 0) norms[i] = sqrtf(acc);
+    }
+}
+
+/* Centroid preparation, one 256-thread block per centroid row:
+ *   cn[j]   = ||c_j||^2 in exactly the order of the reference's k_row_norms
+ *             (kmeans/src/kernels.cu:83-92): thread t runs an fmaf chain over
+ *             t, t+256, ..., then the shared-memory halving tree;
+ *   planes  = hi/lo FP16 of s*c_j, as for the points.
+ * Blocks j in [k, kpad) write cn[j] = +inf so the assignment epilogue can read
+ * whole 32-wide column groups without a bounds test. */
+__global__ void k_prep_c(const float* __restrict__ C, int k, int d, int dp, DevParams* __restrict__ prm,
+                         __half* __restrict__ planes, long long plane_stride, float* __restrict__ cn) {
+    __shared__ float sh[256];
+    const int j = blockIdx.x;
+    const int t = threadIdx.x;
+    if (j >= k) {
+        if (t == 0) cn[j] = INFINITY;
+        return;
+    }
+    const float* c = C + (size_t)j * d;
+    const float s = prm->scale;
+    float acc = 0.f;
+    for (int f = t; f < d; f += 256) acc = fmaf(c[f], c[f], acc);
+    __half* hi = planes + (size_t)j * dp;
+    __half* lo = hi + plane_stride;
+    bool bad = false;
+    for (int f = t; f < dp; f += 256) {
+        const float v = f < d ? c[f] : 0.f;
+        const float a = v * s;
+        bad |= !(fabsf(a) <= 32768.f);
+        const __half h = __float2half_rn(a);
+        hi[f] = h;
+        lo[f] = __float2half_rn(a - __half2float(h));
+    }
+    if (bad) atomicOr(&prm->status, MPK_DEV_SCALE);
+    sh[t] = acc;
+    __syncthreads();
+    for (int off = 128; off > 0; off >>= 1) {
+        if (t < off) sh[t] = sh[t] + sh[t + off];
+        __syncthreads();
+    }
+    if (t == 0) cn[j] = sh[0];
+}
+
+/* ------------------------------------------------------------- refine ---- */
+
+/* FP32 dot in the order of the reference's refinement (kmeans/src/kernels.cu
+ * 582-602): lane l runs an fmaf chain over l, l+32, ...; shfl_down tree.  The
+ * total is valid in lane 0. */
+__device__ __forceinline__ float dot_warp(const float* __restrict__ p, const float* __restrict__ c, int d, int lane) {
+    float acc = 0.f;
+    for (int t = lane; t < d; t += 32) acc = fmaf(p[t], c[t], acc);
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_down_sync(FULL, acc, off);
+    return acc;
+}
+
+/* One warp per refinement entry: recompute each candidate's distance in FP32,
+ * D = fmaf(-2, dot, ||c||^2), and keep the smallest, the smaller index on a
+ * tie.  An overflow entry scans all k centroids. */
+__global__ void k_refine(const float* __restrict__ P, const float* __restrict__ C, const float* __restrict__ cn,
+                         int d, int k, const RefineEntry* __restrict__ list, DevParams* __restrict__ prm,
+                         int* __restrict__ labels, long long cap, unsigned long long* hist_slot) {
+    const int lane = threadIdx.x & 31;
+    const long long nf = prm->nflag < (unsigned long long)cap ? (long long)prm->nflag : cap;
+    const long long wstride = (long long)gridDim.x * (blockDim.x >> 5);
+    const long long w0 = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    unsigned long long ncand = 0, novf = 0;
+    for (long long e = w0; e < nf; e += wstride) {
+        const RefineEntry E = list[e];
+        const float* p = P + (size_t)E.row * d;
+        float bv = INFINITY;
+        int bj = k;
+        if (E.ovf) {
+            for (int j = 0; j < k; ++j) {
+                const float dot = dot_warp(p, C + (size_t)j * d, d, lane);
+                const float v = fmaf(-2.f, dot, cn[j]);
+                if (v < bv || (v == bv && j < bj)) { bv = v; bj = j; }
+            }
+            ncand += (unsigned long long)k;
+            ++novf;
+        } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int j = E.c[q];
+                if (j < 0) continue;
+                const float dot = dot_warp(p, C + (size_t)j * d, d, lane);
+                const float v = fmaf(-2.f, dot, cn[j]);
+                if (v < bv || (v == bv && j < bj)) { bv = v; bj = j; }
+                ++ncand;
+            }
+        }
+        if (lane == 0) labels[E.row] = bj;   /* lane 0 holds the reduced dot */
+    }
+    if (lane == 0 && ncand) {
+        atomicAdd(&prm->ncand_total, ncand);
+        if (novf) atomicAdd(&prm->novf_total, novf);
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        atomicAdd(&prm->nflag_total, (unsigned long long)nf);
+        if (hist_slot) *hist_slot = (unsigned long long)nf;
+    }
+}
+
+/* ------------------------------------------------------------- update ---- */
+
+/* Segmented fixed-point sum of the points per label.
+ *
+ * Each CTA owns a slice of F coordinates and a contiguous run of rows, and
+ * keeps a private k x F table of int64 sums (plus k counts for slice 0) in
+ * shared memory.  Every coordinate is quantised once, q = rint(x * 2^frac),
+ * so the sums are exact integers: order independent, identical on every run
+ * and on any number of GPUs, and within 2^-frac per point of the reference's
+ * FP64 accumulation (kmeans/src/kernels.cu:690-703).  The private tables are
+ * then added into the global int64 sums, one atomic per non-zero entry. */
+template <int F>
+__global__ void k_accum_fixed(const float* __restrict__ P, long long n, int d, const int* __restrict__ labels,
+                              int k, DevParams* __restrict__ prm, long long* __restrict__ sums,
+                              long long* __restrict__ counts, long long rows_per_cta) {
+    extern __shared__ __align__(16) unsigned char sm_raw[];
+    unsigned long long* acc = reinterpret_cast<unsigned long long*>(sm_raw);
+    unsigned int* cnt = reinterpret_cast<unsigned int*>(acc + (size_t)k * F);
+    const int slice = blockIdx.y;
+    const int f0 = slice * F;
+    const bool do_count = (slice == 0);
+    for (int e = threadIdx.x; e < k * F; e += blockDim.x) acc[e] = 0ull;
+    if (do_count) for (int e = threadIdx.x; e < k; e += blockDim.x) cnt[e] = 0u;
+    __syncthreads();
+
+    constexpr int RPW = 32 / F;                       /* rows per warp step */
+    const int lane = threadIdx.x & 31;
+    const int rs = lane / F, f = lane % F;
+    const int col = f0 + f;
+    const bool colok = col < d;
+    const double sc = ldexp(1.0, prm->frac);
+    const int nwarps = blockDim.x >> 5;
+    const long long r0 = (long long)blockIdx.x * rows_per_cta;
+    long long r1 = r0 + rows_per_cta;
+    if (r1 > n) r1 = n;
+    const long long step = (long long)nwarps * RPW;
+    bool badlab = false;
+
+    constexpr int U = 8;
+    long long i = r0 + (long long)(threadIdx.x >> 5) * RPW + rs;
+    for (; i + (U - 1) * step < r1; i += U * step) {
+        int a[U];
+        float x[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const long long ii = i + u * step;
+            a[u] = labels[ii];
+            x[u] = colok ? P[(size_t)ii * d + col] : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            if ((unsigned)a[u] >= (unsigned)k) { badlab = true; continue; }
+            const long long qv = __double2ll_rn((double)x[u] * sc);
+            if (qv) atomicAdd(&acc[(size_t)a[u] * F + f], (unsigned long long)qv);
+            if (do_count && f == 0) atomicAdd(&cnt[a[u]], 1u);
+        }
+    }
+    for (; i < r1; i += step) {
+        const int a = labels[i];
+        if ((unsigned)a >= (unsigned)k) { badlab = true; continue; }
+        const float x = colok ? P[(size_t)i * d + col] : 0.f;
+        const long long qv = __double2ll_rn((double)x * sc);
+        if (qv) atomicAdd(&acc[(size_t)a * F + f], (unsigned long long)qv);
+        if (do_count && f == 0) atomicAdd(&cnt[a], 1u);
+    }
+    if (badlab) atomicOr(&prm->status, MPK_DEV_LABEL_RANGE);
+    __syncthreads();
+    for (int e = threadIdx.x; e < k * F; e += blockDim.x) {
+        const unsigned long long v = acc[e];
+        const int c = f0 + (e % F);
+        if (v && c < d)
+            atomicAdd(reinterpret_cast<unsigned long long*>(&sums[(size_t)(e / F) * d + c]), v);
+    }
+    if (do_count)
+        for (int e = threadIdx.x; e < k; e += blockDim.x)
+            if (cnt[e]) atomicAdd(reinterpret_cast<unsigned long long*>(&counts[e]), (unsigned long long)cnt[e]);
+}
+
+/* C_j = (float)((S_j * 2^-frac) / count_j); an empty cluster keeps its old
+ * centroid; moved2[j] = ||c_new - c_old||^2 by the reference's 256-wide tree
+ * (kmeans/src/kernels.cu:705-723). */
+__global__ void k_finalize_fixed(const long long* __restrict__ sums, const long long* __restrict__ counts, int k,
+                                 int d, const DevParams* __restrict__ prm, float* __restrict__ C,
+                                 float* __restrict__ moved2) {
+    __shared__ float sh[256];
+    const int j = blockIdx.x;
+    const int t = threadIdx.x;
+    const long long cnt = counts[j];
+    const double inv = ldexp(1.0, -prm->frac);
+    float acc = 0.f;
+    for (int f = t; f < d; f += 256) {
+        const size_t o = (size_t)j * d + f;
+        const float old = C[o];
+        const float nv = cnt > 0 ? (float)(((double)sums[o] * inv) / (double)cnt) : old;
+        C[o] = nv;
+        const float dv = nv - old;
+        acc = fmaf(dv, dv, acc);
+    }
+    sh[t] = acc;
+    __syncthreads();
+    for (int off = 128; off > 0; off >>= 1) {
+        if (t < off) sh[t] = sh[t] + sh[t + off];
+        __syncthreads();
+    }
+    if (t == 0 && moved2) moved2[j] = sh[0];
+}
+
+/* inertia = sum_i ||p_i - c_a(i)||^2 in FP64, one warp per row. */
+__global__ void k_inertia(const float* __restrict__ P, const float* __restrict__ C, const int* __restrict__ labels,
+                          long long n, int d, double* out) {
+    const int lane = threadIdx.x & 31;
+    const long long wstride = (long long)gridDim.x * (blockDim.x >> 5);
+    double tot = 0.0;
+    for (long long i = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < n; i += wstride) {
+        const float* p = P + (size_t)i * d;
+        const float* c = C + (size_t)labels[i] * d;
+        for (int t = lane; t < d; t += 32) {
+            const double v = (double)p[t] - (double)c[t];
+            tot = fma(v, v, tot);
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(FULL, tot, o);
+    if (lane == 0 && tot != 0.0) atomicAdd(out, tot);
+}
+
+__global__ void k_count_diff(const int* __restrict__ a, const int* __restrict__ b, long long n,
+                             unsigned long long* out) {
+    unsigned long long c = 0;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) c += (a[i] != b[i]);
+    for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(FULL, c, o);
+    if ((threadIdx.x & 31) == 0 && c) atomicAdd(out, c);
+}
+
+__global__ void k_add_const(float* p, long long count, float c) {
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += stride) p[i] += c;
+}
+
+/* Per-feature z-score, FP64 two-pass (kmeans/src/kernels.cu:116-140 semantics):
+ * one block per feature; population variance; sd <= 1e-12 divides by 1. */
+__global__ void k_standardize(float* P, int n, int d) {
+    __shared__ double sh[256];
+    const int f = blockIdx.x, t = threadIdx.x;
+    double acc = 0.0;
+    for (int i = t; i < n; i += 256) acc += (double)P[(size_t)i * d + f];
+    sh[t] = acc;
+    __syncthreads();
+    for (int o = 128; o > 0; o >>= 1) { if (t < o) sh[t] += sh[t + o]; __syncthreads(); }
+    const double mean = sh[0] / (double)n;
+    __syncthreads();
+    acc = 0.0;
+    for (int i = t; i < n; i += 256) { const double v = (double)P[(size_t)i * d + f] - mean; acc = fma(v, v, acc); }
+    sh[t] = acc;
+    __syncthreads();
+    for (int o = 128; o > 0; o >>= 1) { if (t < o) sh[t] += sh[t + o]; __syncthreads(); }
+    const double sd = sqrt(sh[0] / (double)n);
+    const double inv = sd > 1e-12 ? 1.0 / sd : 1.0;
+    for (int i = t; i < n; i += 256) {
+        const size_t o = (size_t)i * d + f;
+        P[o] = (float)(((double)P[o] - mean) * inv);
+    }
+}
+
+inline int grid_for(long long items, int threads, int cap) {
+    long long b = (items + threads - 1) / threads;
+    if (b < 1) b = 1;
+    return (int)(b > cap ? cap : b);
+}
+
+}  /* namespace */
+
+/* ------------------------------------------------------------ launchers -- */
+
+void launch_maxabs(const float* A, long long count, float* out, cudaStream_t s) {
+    if (count <= 0) return;
+    k_maxabs<<<grid_for(count / 4 + 1, 256, 148 * 8), 256, 0, s>>>(A, count, out);
+}
+
+void launch_set_scale(DevParams* prm, long long n_total, cudaStream_t s) {
+    k_set_scale<<<1, 1, 0, s>>>(prm, n_total);
+}
+
+void launch_split_rows(const float* src, long long rows, int d, int dp, const DevParams* prm, __half* planes,
+                       long long plane_stride, float* norms, cudaStream_t s) {
+    if (rows <= 0) return;
+    k_split_rows<<<grid_for(rows, 8, 148 * 16), 256, 0, s>>>(src, rows, d, dp, prm, planes, plane_stride, norms);
+}
+
+void launch_prep_c(const float* C, int k, int kpad, int d, int dp, DevParams* prm, __half* planes, float* cn,
+                   cudaStream_t s) {
+    k_prep_c<<<kpad, 256, 0, s>>>(C, k, d, dp, prm, planes, (long long)k * dp, cn);
+}
+
+void launch_refine(const float* P, const float* C, const float* cn, int d, int k, const RefineEntry* list,
+                   DevParams* prm, int* labels, long long n_cap, unsigned long long* hist_slot, int num_sms,
+                   cudaStream_t s) {
+    k_refine<<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, list, prm, labels, n_cap, hist_slot);
+}
+
+/* Slice width F: the widest power of two (<= 32) whose k x F int64 table plus
+ * k counts fits in ~96 KB, so two or more CTAs share an SM. */
+static int accum_f_for(int k) {
+    int F = 32;
+    while (F > 1 && (size_t)k * F * 8 + (size_t)k * 4 > 96 * 1024) F >>= 1;
+    return F;
+}
+
+template <int F>
+static void launch_accum_f(const float* P, long long n, int d, const int* labels, int k, DevParams* prm,
+                           long long* sums, long long* counts, int num_sms, cudaStream_t s) {
+    const int slices = (d + F - 1) / F;
+    const size_t smem = (size_t)k * F * 8 + (size_t)k * 4;
+    static_assert(F >= 1 && F <= 32, "slice width");
+    cudaFuncSetAttribute(k_accum_fixed<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    /* about three resident CTAs per SM in total, split over the slices */
+    long long chunks = (3LL * num_sms + slices - 1) / slices;
+    if (chunks < 1) chunks = 1;
+    long long rows = (n + chunks - 1) / chunks;
+    if (rows < 1) rows = 1;
+    chunks = (n + rows - 1) / rows;
+    dim3 grid((unsigned)chunks, (unsigned)slices);
+    k_accum_fixed<F><<<grid, 512, smem, s>>>(P, n, d, labels, k, prm, sums, counts, rows);
+}
+
+void launch_accum_fixed(const float* P, long long n, int d, const int* labels, int k, DevParams* prm,
+                        long long* sums, long long* counts, int num_sms, cudaStream_t s) {
+    if (n <= 0) return;
+    switch (accum_f_for(k)) {
+        case 32: launch_accum_f<32>(P, n, d, labels, k, prm, sums, counts, num_sms, s); break;
+        case 16: launch_accum_f<16>(P, n, d, labels, k, prm, sums, counts, num_sms, s); break;
+        case 8: launch_accum_f<8>(P, n, d, labels, k, prm, sums, counts, num_sms, s); break;
+        case 4: launch_accum_f<4>(P, n, d, labels, k, prm, sums, counts, num_sms, s); break;
+        case 2: launch_accum_f<2>(P, n, d, labels, k, prm, sums, counts, num_sms, s); break;
+        default: launch_accum_f<1>(P, n, d, labels, k, prm, sums, counts, num_sms, s); break;
+    }
+}
+
+void launch_finalize_fixed(const long long* sums, const long long* counts, int k, int d, const DevParams* prm,
+                           float* C, float* moved2, cudaStream_t s) {
+    k_finalize_fixed<<<k, 256, 0, s>>>(sums, counts, k, d, prm, C, moved2);
+}
+
+void launch_inertia(const float* P, const float* C, const int* labels, long long n, int d, double* out,
+                    cudaStream_t s) {
+    if (n <= 0) return;
+    k_inertia<<<grid_for(n, 8, 148 * 16), 256, 0, s>>>(P, C, labels, n, d, out);
+}
+
+void launch_count_diff(const int* a, const int* b, long long n, unsigned long long* out, cudaStream_t s) {
+    if (n <= 0) return;
+    k_count_diff<<<grid_for(n, 256, 148 * 8), 256, 0, s>>>(a, b, n, out);
+}
+
+void launch_add_const(float* p, long long count, float c, cudaStream_t s) {
+    if (count <= 0) return;
+    k_add_const<<<grid_for(count, 256, 8192), 256, 0, s>>>(p, count, c);
+}
+
+void launch_standardize(float* P, int n, int d, cudaStream_t s) {
+    k_standardize<<<d, 256, 0, s>>>(P, n, d);
+}
+
+}  /* namespace mpk */

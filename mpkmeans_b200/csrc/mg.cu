@@ -1,0 +1,216 @@
+/* mg.cu -- single-process multi-GPU Lloyd over row shards (mpkMeansMixedMG).
+ *
+ * One engine per device holds its shard's split points.  Per iteration every
+ * device assigns its rows and adds its exact int64 fixed-point sums and
+ * counts; one NCCL allreduce (int64 sum, in place) combines them; every device
+ * then finalises the same centroids redundantly.  Integer sums make the result
+ * independent of the number of devices and of the reduction order.
+ *
+ * NCCL is resolved at run time (dlopen of libnccl.so.2, or the copy already
+ * loaded by the host process), so the library links without it and callers
+ * that never use this entry point never load it.
+ */
+#include "engine.cuh"
+#include "mpkmeans.h"
+
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+namespace {
+
+struct Nccl {
+    ncclResult_t (*commInitAll)(ncclComm_t*, int, const int*) = nullptr;
+    ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*allReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    ncclResult_t (*groupStart)() = nullptr;
+    ncclResult_t (*groupEnd)() = nullptr;
+    const char* (*errStr)(ncclResult_t) = nullptr;
+    bool ok = false;
+};
+
+const Nccl& nccl() {
+    static Nccl n;
+    static bool tried = false;
+    if (tried) return n;
+    tried = true;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+        fprintf(stderr, "mpkMeansMixedMG: cannot load NCCL: %s\n", dlerror());
+        return n;
+    }
+    n.commInitAll = (decltype(n.commInitAll))dlsym(h, "ncclCommInitAll");
+    n.commDestroy = (decltype(n.commDestroy))dlsym(h, "ncclCommDestroy");
+    n.allReduce = (decltype(n.allReduce))dlsym(h, "ncclAllReduce");
+    n.groupStart = (decltype(n.groupStart))dlsym(h, "ncclGroupStart");
+    n.groupEnd = (decltype(n.groupEnd))dlsym(h, "ncclGroupEnd");
+    n.errStr = (decltype(n.errStr))dlsym(h, "ncclGetErrorString");
+    n.ok = n.commInitAll && n.commDestroy && n.allReduce && n.groupStart && n.groupEnd && n.errStr;
+    return n;
+}
+
+__global__ void k_max_abs_host_visible(const float* A, long long count, float* out) {
+    float m = 0.f;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < count;
+         i += (long long)gridDim.x * blockDim.x)
+        m = fmaxf(m, fabsf(A[i]));
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0 && m > 0.f) atomicMax(reinterpret_cast<unsigned int*>(out), __float_as_uint(m));
+}
+
+float device_maxabs(const float* A, long long count, cudaStream_t s) {
+    float* d = nullptr;
+    float h = 0.f;
+    if (count <= 0 || cudaMalloc(&d, sizeof(float)) != cudaSuccess) return 0.f;
+    cudaMemsetAsync(d, 0, sizeof(float), s);
+    long long blocks = (count + 255) / 256;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    k_max_abs_host_visible<<<(int)blocks, 256, 0, s>>>(A, count, d);
+    cudaMemcpyAsync(&h, d, sizeof(float), cudaMemcpyDeviceToHost, s);
+    cudaStreamSynchronize(s);
+    cudaFree(d);
+    return h;
+}
+
+}  /* namespace */
+
+extern "C" mpkStatus mpkMeansMixedMG(int ngpu, const int* devices, const float* const* dPshard, const int* nshard,
+                                     int d, int k, float* const* dC, int* const* dAssign, const mpkParams* params,
+                                     mpkStats* stats) {
+    if (ngpu < 1 || !devices || !dPshard || !nshard || !dC || !dAssign || d <= 0 || k <= 0) return MPK_ERR_INVALID;
+    long long n_total = 0;
+    for (int g = 0; g < ngpu; ++g) {
+        if (nshard[g] < 0 || (nshard[g] > 0 && (!dPshard[g] || !dAssign[g])) || !dC[g]) return MPK_ERR_INVALID;
+        n_total += nshard[g];
+    }
+    if (n_total < k) return MPK_ERR_INVALID;
+    const Nccl& N = nccl();
+    if (!N.ok) return MPK_ERR_INVALID;
+    mpkParams P;
+    if (params) P = *params; else mpkParamsInit(&P);
+    mpkStats local;
+    mpkStats* S = stats ? stats : &local;
+    std::memset(S, 0, sizeof(*S));
+    const int refine = (P.use_cond3 || P.use_cond6) ? 1 : 0;
+    int prev_dev = 0;
+    cudaGetDevice(&prev_dev);
+
+    std::vector<cudaStream_t> st(ngpu, nullptr);
+    std::vector<mpkEngine> eng(ngpu, nullptr);
+    std::vector<long long*> sums(ngpu, nullptr);
+    std::vector<float*> moved(ngpu, nullptr);
+    std::vector<ncclComm_t> comm(ngpu, nullptr);
+    float* h_moved = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    mpkStatus rc = MPK_OK;
+    const long long len = (long long)k * d + k;
+    int it = 0;
+
+    /* one global operand scale: max |P| over every shard and the start C */
+    float pmax = 0.f;
+    for (int g = 0; g < ngpu; ++g) {
+        cudaSetDevice(devices[g]);
+        if (cudaStreamCreateWithFlags(&st[g], cudaStreamNonBlocking) != cudaSuccess) { rc = MPK_ERR_CUDA; goto done; }
+        pmax = fmaxf(pmax, device_maxabs(dPshard[g], (long long)nshard[g] * d, st[g]));
+        if (g == 0) pmax = fmaxf(pmax, device_maxabs(dC[g], (long long)k * d, st[g]));
+    }
+    for (int g = 0; g < ngpu; ++g) {
+        cudaSetDevice(devices[g]);
+        rc = mpkEngineCreate(&eng[g], dPshard[g], nshard[g], d, k, nullptr, pmax > 0.f ? pmax : 1.f, n_total, st[g]);
+        if (rc != MPK_OK) goto done;
+        if (cudaMalloc(&sums[g], (size_t)len * sizeof(long long)) != cudaSuccess ||
+            cudaMalloc(&moved[g], (size_t)k * sizeof(float)) != cudaSuccess) { rc = MPK_ERR_ALLOC; goto done; }
+    }
+    {
+        const ncclResult_t r = N.commInitAll(comm.data(), ngpu, devices);
+        if (r != ncclSuccess) {
+            fprintf(stderr, "mpkMeansMixedMG: ncclCommInitAll: %s\n", N.errStr(r));
+            rc = MPK_ERR_CUDA;
+            goto done;
+        }
+    }
+    if (cudaMallocHost(&h_moved, (size_t)k * sizeof(float)) != cudaSuccess) { rc = MPK_ERR_ALLOC; goto done; }
+    cudaSetDevice(devices[0]);
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventRecord(e0, st[0]);
+    for (it = 0; it < P.max_iter; ++it) {
+        for (int g = 0; g < ngpu; ++g) {
+            cudaSetDevice(devices[g]);
+            if ((rc = mpkEngineAssign(eng[g], dC[g], dAssign[g], refine)) != MPK_OK) goto done;
+            if ((rc = mpkEngineAccumulate(eng[g], dAssign[g], sums[g])) != MPK_OK) goto done;
+        }
+        N.groupStart();
+        for (int g = 0; g < ngpu; ++g)
+            N.allReduce(sums[g], sums[g], (size_t)len, ncclInt64, ncclSum, comm[g], st[g]);
+        {
+            const ncclResult_t r = N.groupEnd();
+            if (r != ncclSuccess) {
+                fprintf(stderr, "mpkMeansMixedMG: ncclAllReduce: %s\n", N.errStr(r));
+                rc = MPK_ERR_CUDA;
+                goto done;
+            }
+        }
+        for (int g = 0; g < ngpu; ++g) {
+            cudaSetDevice(devices[g]);
+            if ((rc = mpkEngineFinalize(eng[g], sums[g], dC[g], moved[g])) != MPK_OK) goto done;
+        }
+        S->hp_baseline += n_total * k;
+        S->tested += n_total * (k - 1);
+        if (P.tol > 0.f || P.verbose) {
+            cudaSetDevice(devices[0]);
+            cudaMemcpyAsync(h_moved, moved[0], (size_t)k * sizeof(float), cudaMemcpyDeviceToHost, st[0]);
+            if (cudaStreamSynchronize(st[0]) != cudaSuccess) { rc = MPK_ERR_CUDA; goto done; }
+            double fro2 = 0.0;
+            for (int j = 0; j < k; ++j) fro2 += (double)h_moved[j];
+            if (P.verbose) fprintf(stderr, "[mg] iter %3d  ||dC||_F^2 %.6e\n", it, fro2);
+            if (P.tol > 0.f && fro2 < (double)P.tol * (double)P.tol) { ++it; break; }
+        }
+    }
+    S->iters = it;
+    cudaSetDevice(devices[0]);
+    cudaEventRecord(e1, st[0]);
+    for (int g = 0; g < ngpu; ++g) {
+        cudaSetDevice(devices[g]);
+        if (cudaStreamSynchronize(st[g]) != cudaSuccess) { rc = MPK_ERR_CUDA; goto done; }
+    }
+    {
+        float ms = 0.f;
+        cudaSetDevice(devices[0]);
+        cudaEventElapsedTime(&ms, e0, e1);
+        S->t_total_ms = ms;
+        for (int g = 0; g < ngpu; ++g) {
+            cudaSetDevice(devices[g]);
+            long long rows = 0, cands = 0, full = 0;
+            int status = 0;
+            double ine = 0.0;
+            mpkEngineCounters(eng[g], &rows, &cands, &full, &status);
+            if (status) { rc = MPK_ERR_CUDA; goto done; }
+            S->hp_update += cands;
+            if (nshard[g] > 0 && mpkEngineInertia(eng[g], dC[g], dAssign[g], &ine) != MPK_OK) { rc = MPK_ERR_CUDA; goto done; }
+            S->inertia += ine;
+        }
+    }
+done:
+    for (int g = 0; g < ngpu; ++g) {
+        cudaSetDevice(devices[g]);
+        if (st[g]) cudaStreamSynchronize(st[g]);
+        if (comm[g]) N.commDestroy(comm[g]);
+        if (eng[g]) mpkEngineDestroy(eng[g]);
+        cudaFree(sums[g]);
+        cudaFree(moved[g]);
+        if (st[g]) cudaStreamDestroy(st[g]);
+    }
+    cudaSetDevice(devices[0]);
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    cudaFreeHost(h_moved);
+    cudaSetDevice(prev_dev);
+    return rc;
+}

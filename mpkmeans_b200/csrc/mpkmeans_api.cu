@@ -1,0 +1,757 @@
+/* mpkmeans_api.cu -- the C ABI of libmpkmeans_b200: engine handle, Lloyd
+ * drivers and data helpers.  Declarations and the reference interface each one
+ * replaces are in include/mpkmeans.h.
+ */
+#include "engine.cuh"
+#include "mpkmeans.h"
+#include "mpkmeans_debug.h"
+
+#include <cublas_v2.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <climits>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <random>
+#include <string>
+#include <vector>
+
+using namespace mpk;
+
+/* ----------------------------------------------------------- helpers ---- */
+
+#define MPK_TRY(call)                                                                    \
+    do {                                                                                 \
+        cudaError_t e_ = (call);                                                         \
+        if (e_ != cudaSuccess) {                                                         \
+            fprintf(stderr, "mpkmeans_b200 %s:%d CUDA: %s\n", __FILE__, __LINE__,         \
+                    cudaGetErrorString(e_));                                             \
+            return MPK_ERR_CUDA;                                                         \
+        }                                                                                \
+    } while (0)
+
+namespace {
+
+constexpr double U16 = 1.0 / 2048.0;
+constexpr double U24 = 1.0 / 16777216.0;
+constexpr double U22 = 1.0 / 4194304.0;
+
+cudaStream_t stream_of(cublasHandle_t blas) {
+    cudaStream_t s = nullptr;
+    if (blas) cublasGetStream(blas, &s);
+    return s;
+}
+
+long long round_up(long long a, long long b) { return (a + b - 1) / b * b; }
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+/* Error-bound constants of the assignment filter, for inner dimension d (dp
+ * padded).  A pair (i, j) is excluded only when
+ *     D~_j - D~_best > c1 ||x|| cmax + c2 eta (||x|| + cmax) + 2^-22 (|D~_j| + |D~_best|)
+ * where D~ is the tensor-core distance.  The terms:
+ *   split    3 * 2^-22 ||x|| ||c||: the lo words carry the residual to 2^-22
+ *            relative and the dropped lo*lo product is below 2^-22;
+ *   accum    (3 dp / 16 + 16) * 2^-22 ||x|| ||c||: one truncating FP32 add per
+ *            16-deep MMA step of the three-product chain, plus slack;
+ *   fp32     gamma_d ||x|| ||c||: the FP32 evaluation the labels must agree
+ *            with (any summation order);
+ *   floor    2^-25/s per coordinate for lo words that fall subnormal (c2);
+ * each appears once for the best and once for the candidate (factor 2) and as
+ * a distance (factor 2 on the dot).  The norms ||x||, ||c|| are FP32 values,
+ * inflated here by their own rounding. */
+BoundConsts bound_consts(int d, int dp) {
+    const double eps_split = 3.2 * U22;
+    const double eps_acc = (3.0 * dp / 16.0 + 16.0) * U22;
+    const double g = d * U24;
+    const double gamma_d = g / (1.0 - g);
+    const double infl = 1.0 + 4.0 * d * U24 + 1.0 / 65536.0;
+    BoundConsts bc;
+    bc.c1 = (float)(4.0 * (eps_split + eps_acc + gamma_d) * infl);
+    bc.c2 = (float)(4.0 * std::sqrt((double)d) * 1.01);
+    return bc;
+}
+
+int current_sm_count(int* dev_out, int* cc_major) {
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (cc_major) cudaDeviceGetAttribute(cc_major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (dev_out) *dev_out = dev;
+    return sms;
+}
+
+}  /* namespace */
+
+/* ------------------------------------------------------------ engine ---- */
+
+struct mpkEngine_s {
+    int dev = 0, num_sms = 0;
+    cudaStream_t s = nullptr;
+    const float* P = nullptr;
+    long long n = 0;
+    int d = 0, k = 0, dp = 0, kpad = 0;
+    bool can_assign = false;
+    __half* Xs = nullptr;
+    float* xnorm = nullptr;
+    __half* Cs = nullptr;
+    float* cn = nullptr;
+    RefineEntry* list = nullptr;
+    DevParams* prm = nullptr;
+    double* dInertia = nullptr;
+    unsigned long long* hist = nullptr;   /* MPK_MAX_HIST slots */
+    CUtensorMap tmX, tmC;
+    BoundConsts bc;
+    float4* dbg = nullptr;                /* test hook, set by mpkDebugAssignTop */
+};
+
+static void engine_free(mpkEngine e) {
+    if (!e) return;
+    cudaFree(e->Xs);
+    cudaFree(e->xnorm);
+    cudaFree(e->Cs);
+    cudaFree(e->cn);
+    cudaFree(e->list);
+    cudaFree(e->prm);
+    cudaFree(e->dInertia);
+    cudaFree(e->hist);
+    delete e;
+}
+
+static mpkStatus engine_create(mpkEngine* out, const float* dP, long long n, int d, int k, const float* dC0,
+                               float pmax_global, long long n_global, cudaStream_t s, bool need_assign) {
+    if (!out || n < 0 || d <= 0 || k <= 0 || (n > 0 && !dP)) return MPK_ERR_INVALID;
+    if (n > INT_MAX) {
+        fprintf(stderr, "mpkmeans_b200: a shard holds at most %d rows (got %lld)\n", INT_MAX, n);
+        return MPK_ERR_INVALID;
+    }
+    *out = nullptr;
+    int cc = 0;
+    mpkEngine e = new mpkEngine_s();
+    e->num_sms = current_sm_count(&e->dev, &cc);
+    if (cc != 10) {
+        fprintf(stderr, "mpkmeans_b200: needs an sm_100 GPU (B200); device %d is compute capability %d.x\n",
+                e->dev, cc);
+        delete e;
+        return MPK_ERR_CUDA;
+    }
+    if (need_assign && !assign_supported(d)) {
+        fprintf(stderr, "mpkmeans_b200: d = %d is above the assignment kernel's limit of 256\n", d);
+        delete e;
+        return MPK_ERR_INVALID;
+    }
+    e->s = s;
+    e->P = dP;
+    e->n = n;
+    e->d = d;
+    e->k = k;
+    e->dp = (int)round_up(d, 64);
+    e->kpad = (int)round_up(k, 256);
+    e->can_assign = need_assign;
+    e->bc = bound_consts(d, e->dp);
+    const long long ng = n_global > 0 ? n_global : (n > 0 ? n : 1);
+
+#define ALLOC(ptr, bytes)                                                      \
+    if (cudaMalloc((void**)&(ptr), (size_t)(bytes)) != cudaSuccess) {          \
+        fprintf(stderr, "mpkmeans_b200: cudaMalloc of %lld bytes failed\n", (long long)(bytes)); \
+        engine_free(e);                                                        \
+        return MPK_ERR_ALLOC;                                                  \
+    }
+    ALLOC(e->prm, sizeof(DevParams));
+    ALLOC(e->dInertia, sizeof(double));
+    ALLOC(e->hist, sizeof(unsigned long long) * MPK_MAX_HIST);
+    if (need_assign) {
+        ALLOC(e->Xs, (size_t)2 * (n > 0 ? n : 1) * e->dp * sizeof(__half));
+        ALLOC(e->xnorm, (size_t)(n > 0 ? n : 1) * sizeof(float));
+        ALLOC(e->Cs, (size_t)2 * k * e->dp * sizeof(__half));
+        ALLOC(e->cn, (size_t)e->kpad * sizeof(float));
+        ALLOC(e->list, (size_t)(n > 0 ? n : 1) * sizeof(RefineEntry));
+    }
+#undef ALLOC
+    cudaMemsetAsync(e->prm, 0, sizeof(DevParams), s);
+    cudaMemsetAsync(e->hist, 0, sizeof(unsigned long long) * MPK_MAX_HIST, s);
+    if (pmax_global > 0.f) {
+        DevParams h{};
+        h.pmax = pmax_global;
+        h.c0max = 0.f;
+        cudaMemcpyAsync(e->prm, &h, sizeof(float) * 2, cudaMemcpyHostToDevice, s);
+        cudaStreamSynchronize(s);   /* h is on the stack */
+    } else {
+        launch_maxabs(dP, n * d, &e->prm->pmax, s);
+        if (dC0) launch_maxabs(dC0, (long long)k * d, &e->prm->c0max, s);
+    }
+    launch_set_scale(e->prm, ng, s);
+    if (need_assign) {
+        if (n > 0) launch_split_rows(dP, n, d, e->dp, e->prm, e->Xs, n * e->dp, e->xnorm, s);
+        auto fn = encode_fn();
+        if (!fn) {
+            fprintf(stderr, "mpkmeans_b200: cuTensorMapEncodeTiled is unavailable\n");
+            engine_free(e);
+            return MPK_ERR_CUDA;
+        }
+        if ((n > 0 && !make_tmap_planes(&e->tmX, e->Xs, n, e->dp, 128)) ||
+            !make_tmap_planes(&e->tmC, e->Cs, k, e->dp, assign_bn_for(k))) {
+            fprintf(stderr, "mpkmeans_b200: tensor map encoding failed\n");
+            engine_free(e);
+            return MPK_ERR_CUDA;
+        }
+    }
+    if (cudaGetLastError() != cudaSuccess) {
+        engine_free(e);
+        return MPK_ERR_CUDA;
+    }
+    *out = e;
+    return MPK_OK;
+}
+
+namespace mpk {
+bool make_tmap_planes(CUtensorMap* map, const __half* base, long long rows, int dp, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn || rows <= 0) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)dp, (cuuint64_t)rows, 2};
+    cuuint64_t strides[2] = {(cuuint64_t)dp * 2, (cuuint64_t)rows * (cuuint64_t)dp * 2};
+    cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  /* namespace mpk */
+
+static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int refine, int hist_it) {
+    if (!e->can_assign) return MPK_ERR_INVALID;
+    cudaMemsetAsync(&e->prm->nflag, 0, sizeof(unsigned int), e->s);
+    launch_prep_c(dC, e->k, e->kpad, e->d, e->dp, e->prm, e->Cs, e->cn, e->s);
+    if (e->n == 0) return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
+    AssignArgs a;
+    a.tmX = &e->tmX;
+    a.tmC = &e->tmC;
+    a.n = e->n;
+    a.k = e->k;
+    a.d = e->d;
+    a.dp = e->dp;
+    a.xnorm = e->xnorm;
+    a.cn = e->cn;
+    a.prm_ro = e->prm;
+    a.prm = e->prm;
+    a.labels = dAssign;
+    a.list = e->list;
+    a.refine = refine;
+    a.bc = e->bc;
+    a.num_sms = e->num_sms;
+    a.dbg = e->dbg;
+    cudaError_t err = launch_assign(a, e->s);
+    if (err != cudaSuccess) {
+        fprintf(stderr, "mpkmeans_b200: assignment launch failed: %s\n", cudaGetErrorString(err));
+        return MPK_ERR_CUDA;
+    }
+    if (refine)
+        launch_refine(e->P, dC, e->cn, e->d, e->k, e->list, e->prm, dAssign, e->n,
+                      (hist_it >= 0 && hist_it < MPK_MAX_HIST) ? e->hist + hist_it : nullptr, e->num_sms, e->s);
+    return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
+}
+
+static mpkStatus engine_accumulate(mpkEngine e, const int* dAssign, long long* dSums) {
+    const long long len = (long long)e->k * e->d + e->k;
+    cudaMemsetAsync(dSums, 0, (size_t)len * sizeof(long long), e->s);
+    launch_accum_fixed(e->P, e->n, e->d, dAssign, e->k, e->prm, dSums, dSums + (long long)e->k * e->d,
+                       e->num_sms, e->s);
+    return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
+}
+
+static mpkStatus engine_finalize(mpkEngine e, const long long* dSums, float* dC, float* dMoved2) {
+    launch_finalize_fixed(dSums, dSums + (long long)e->k * e->d, e->k, e->d, e->prm, dC, dMoved2, e->s);
+    return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
+}
+
+extern "C" {
+
+mpkStatus mpkEngineCreate(mpkEngine* out, const float* dP, long long n, int d, int k, const float* dC0,
+                          float pmax_global, long long n_global, cudaStream_t stream) {
+    return engine_create(out, dP, n, d, k, dC0, pmax_global, n_global, stream, true);
+}
+
+mpkStatus mpkEngineDestroy(mpkEngine e) {
+    if (!e) return MPK_ERR_INVALID;
+    cudaStreamSynchronize(e->s);
+    engine_free(e);
+    return MPK_OK;
+}
+
+mpkStatus mpkEngineAssign(mpkEngine e, const float* dC, int* dAssign, int refine) {
+    if (!e || !dC || (e->n > 0 && !dAssign)) return MPK_ERR_INVALID;
+    return engine_assign(e, dC, dAssign, refine, -1);
+}
+
+mpkStatus mpkEngineAccumulate(mpkEngine e, const int* dAssign, long long* dSums) {
+    if (!e || !dSums || (e->n > 0 && !dAssign)) return MPK_ERR_INVALID;
+    return engine_accumulate(e, dAssign, dSums);
+}
+
+mpkStatus mpkEngineFinalize(mpkEngine e, const long long* dSums, float* dC, float* dMoved2) {
+    if (!e || !dSums || !dC) return MPK_ERR_INVALID;
+    return engine_finalize(e, dSums, dC, dMoved2);
+}
+
+mpkStatus mpkEngineInertia(mpkEngine e, const float* dC, const int* dAssign, double* out) {
+    if (!e || !dC || !out) return MPK_ERR_INVALID;
+    MPK_TRY(cudaMemsetAsync(e->dInertia, 0, sizeof(double), e->s));
+    launch_inertia(e->P, dC, dAssign, e->n, e->d, e->dInertia, e->s);
+    MPK_TRY(cudaMemcpyAsync(out, e->dInertia, sizeof(double), cudaMemcpyDeviceToHost, e->s));
+    MPK_TRY(cudaStreamSynchronize(e->s));
+    return MPK_OK;
+}
+
+int mpkEngineFracBits(mpkEngine e) {
+    if (!e) return -1;
+    int f = 0;
+    cudaMemcpyAsync(&f, &e->prm->frac, sizeof(int), cudaMemcpyDeviceToHost, e->s);
+    cudaStreamSynchronize(e->s);
+    return f;
+}
+
+mpkStatus mpkEngineCounters(mpkEngine e, long long* rows_refined, long long* cand_refined, long long* rows_full_scan,
+                            int* status) {
+    if (!e) return MPK_ERR_INVALID;
+    DevParams h;
+    MPK_TRY(cudaMemcpyAsync(&h, e->prm, sizeof(DevParams), cudaMemcpyDeviceToHost, e->s));
+    MPK_TRY(cudaStreamSynchronize(e->s));
+    if (rows_refined) *rows_refined = (long long)h.nflag_total;
+    if (cand_refined) *cand_refined = (long long)h.ncand_total;
+    if (rows_full_scan) *rows_full_scan = (long long)h.novf_total;
+    if (status) *status = h.status;
+    return MPK_OK;
+}
+
+long long mpkEngineSumsLength(mpkEngine e) { return e ? (long long)e->k * e->d + e->k : 0; }
+
+/* Test hook: while set, every assignment writes (v0, v1, j0, j1) per row --
+ * the emulated best and runner-up distances and their centroids -- to dOut4
+ * (n float4, device).  Pass NULL to stop.  No reference counterpart. */
+mpkStatus mpkDebugSetAssignTrace(mpkEngine e, float* dOut4) {
+    if (!e) return MPK_ERR_INVALID;
+    e->dbg = reinterpret_cast<float4*>(dOut4);
+    return MPK_OK;
+}
+
+/* Test hook: the operand scale, eta, fixed-point bits and bound constants. */
+mpkStatus mpkDebugEngineInfo(mpkEngine e, float* scale, float* eta, int* frac, float* c1, float* c2) {
+    if (!e) return MPK_ERR_INVALID;
+    DevParams h;
+    MPK_TRY(cudaMemcpyAsync(&h, e->prm, sizeof(DevParams), cudaMemcpyDeviceToHost, e->s));
+    MPK_TRY(cudaStreamSynchronize(e->s));
+    if (scale) *scale = h.scale;
+    if (eta) *eta = h.eta;
+    if (frac) *frac = h.frac;
+    if (c1) *c1 = e->bc.c1;
+    if (c2) *c2 = e->bc.c2;
+    return MPK_OK;
+}
+
+/* ------------------------------------------------------------ params ---- */
+
+void mpkParamsInit(mpkParams* p) {
+    if (!p) return;
+    std::memset(p, 0, sizeof(*p));
+    p->max_iter = 100;
+    p->tol = 0.f;
+    p->use_cond3 = 1;
+    p->use_cond6 = 1;
+    p->accum = MPK_ACCUM_FP32;
+    p->mw_macs = 3;
+}
+
+double mpkEpsilon(int d, int accum) {
+    const double u = (accum == MPK_ACCUM_FP16) ? U16 : U24;
+    const double g = (double)d * u;
+    if (g >= 1.0) return -1.0;
+    return 2.0 * U16 + g / (1.0 - g);
+}
+
+double mpkMultiwordEpsilon(int d, int macs) {
+    if (macs < 1 || macs > 3) return -1.0;
+    const int m = d + (macs == 1 ? 0 : (macs == 2 ? 1 : 3));
+    const double g = (double)m * U24;
+    if (g >= 1.0) return -1.0;
+    const double gamma = g / (1.0 - g);
+    const double dropped = macs == 1 ? 2.0 * U16 + U16 * U16 : (macs == 2 ? U16 + U16 * U16 : 3.0 * U16 * U16);
+    const double eps = (1.0 + dropped) * (1.0 + gamma) - 1.0;
+    return eps >= 1.0 ? -1.0 : eps;
+}
+
+/* ------------------------------------------------------- preprocessing -- */
+
+mpkStatus mpkShiftNonNegative(float* dP, int n, int d, float* out_shift) {
+    if (!dP || n <= 0 || d <= 0) return MPK_ERR_INVALID;
+    float* dmax = nullptr;
+    if (cudaMalloc(&dmax, sizeof(float)) != cudaSuccess) return MPK_ERR_ALLOC;
+    cudaMemset(dmax, 0, sizeof(float));
+    launch_maxabs(dP, (long long)n * d, dmax, nullptr);
+    float M = 0.f;
+    cudaError_t e = cudaMemcpy(&M, dmax, sizeof(float), cudaMemcpyDeviceToHost);
+    cudaFree(dmax);
+    if (e != cudaSuccess) return MPK_ERR_CUDA;
+    launch_add_const(dP, (long long)n * d, M, nullptr);
+    MPK_TRY(cudaGetLastError());
+    if (out_shift) *out_shift = M;
+    return MPK_OK;
+}
+
+mpkStatus mpkStandardize(float* dP, int n, int d) {
+    if (!dP || n <= 0 || d <= 0) return MPK_ERR_INVALID;
+    launch_standardize(dP, n, d, nullptr);
+    MPK_TRY(cudaGetLastError());
+    return MPK_OK;
+}
+
+mpkStatus mpkShiftCentroids(float* dC, int k, int d, float delta) {
+    if (!dC || k <= 0 || d <= 0) return MPK_ERR_INVALID;
+    launch_add_const(dC, (long long)k * d, delta, nullptr);
+    MPK_TRY(cudaGetLastError());
+    return MPK_OK;
+}
+
+/* ------------------------------------------------------------ drivers --- */
+
+static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k, float* dC, int* dAssign,
+                       const mpkParams* params, mpkStats* stats, bool force_refine, const char* tag) {
+    if (n <= 0 || d <= 0 || k <= 0 || k > n || !dP || !dC || !dAssign) return MPK_ERR_INVALID;
+    mpkParams P;
+    if (params) P = *params; else mpkParamsInit(&P);
+    mpkStats local;
+    mpkStats* S = stats ? stats : &local;
+    std::memset(S, 0, sizeof(*S));
+    const int refine = (force_refine || P.use_cond3 || P.use_cond6) ? 1 : 0;
+    cudaStream_t s = stream_of(blas);
+
+    cudaEvent_t ev_all0, ev_all1, ev_x;
+    cudaEventCreate(&ev_all0);
+    cudaEventCreate(&ev_all1);
+    cudaEventCreate(&ev_x);
+    cudaEventRecord(ev_all0, s);
+
+    mpkEngine e = nullptr;
+    mpkStatus st = engine_create(&e, dP, n, d, k, dC, 0.f, n, s, true);
+    if (st != MPK_OK) {
+        cudaEventDestroy(ev_all0); cudaEventDestroy(ev_all1); cudaEventDestroy(ev_x);
+        return st;
+    }
+    cudaEventRecord(ev_x, s);
+    long long* sums = nullptr;
+    float* moved2 = nullptr;
+    float* h_moved = nullptr;
+    const int iters_cap = P.max_iter > 0 ? P.max_iter : 0;
+    std::vector<cudaEvent_t> ev((size_t)iters_cap * 4, nullptr);
+    int it = 0;
+    if (cudaMalloc(&sums, ((size_t)k * d + k) * sizeof(long long)) != cudaSuccess ||
+        cudaMalloc(&moved2, (size_t)k * sizeof(float)) != cudaSuccess ||
+        cudaMallocHost(&h_moved, (size_t)k * sizeof(float)) != cudaSuccess) {
+        st = MPK_ERR_ALLOC;
+        goto done;
+    }
+    for (auto& x : ev) cudaEventCreate(&x);
+
+    for (it = 0; it < iters_cap; ++it) {
+        cudaEventRecord(ev[4 * it + 0], s);
+        if ((st = engine_assign(e, dC, dAssign, refine, it)) != MPK_OK) goto done;
+        cudaEventRecord(ev[4 * it + 1], s);
+        if ((st = engine_accumulate(e, dAssign, sums)) != MPK_OK) goto done;
+        if ((st = engine_finalize(e, sums, dC, moved2)) != MPK_OK) goto done;
+        cudaEventRecord(ev[4 * it + 2], s);
+        S->hp_baseline += (long long)n * k;
+        S->tested += (long long)n * (k - 1);
+        if (P.tol > 0.f || P.verbose) {
+            cudaMemcpyAsync(h_moved, moved2, (size_t)k * sizeof(float), cudaMemcpyDeviceToHost, s);
+            if (cudaStreamSynchronize(s) != cudaSuccess) { st = MPK_ERR_CUDA; goto done; }
+            double fro2 = 0.0;
+            for (int j = 0; j < k; ++j) fro2 += (double)h_moved[j];
+            if (P.verbose) fprintf(stderr, "[%s] iter %3d  ||dC||_F^2 %.6e\n", tag, it, fro2);
+            if (P.tol > 0.f && fro2 < (double)P.tol * (double)P.tol) { ++it; break; }
+        }
+    }
+    S->iters = it;
+    cudaEventRecord(ev_all1, s);
+    if (cudaStreamSynchronize(s) != cudaSuccess) { st = MPK_ERR_CUDA; goto done; }
+    {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, ev_all0, ev_all1);
+        S->t_total_ms = ms;
+        double prep_x = 0.0;
+        cudaEventElapsedTime(&ms, ev_all0, ev_x);
+        prep_x = ms;
+        for (int t = 0; t < it; ++t) {
+            cudaEventElapsedTime(&ms, ev[4 * t + 0], ev[4 * t + 1]);
+            S->t_gemm_lo_ms += ms;
+            cudaEventElapsedTime(&ms, ev[4 * t + 1], ev[4 * t + 2]);
+            S->t_update_ms += ms;
+        }
+        S->t_dist_ms = prep_x + S->t_gemm_lo_ms;
+        long long rows = 0, cands = 0, full = 0;
+        int status = 0;
+        mpkEngineCounters(e, &rows, &cands, &full, &status);
+        S->hp_update = cands;
+        S->n_hist = it < MPK_MAX_HIST ? it : MPK_MAX_HIST;
+        cudaMemcpy(S->hist_survivors, e->hist, sizeof(long long) * S->n_hist, cudaMemcpyDeviceToHost);
+        if (status) {
+            fprintf(stderr, "mpkmeans_b200: device status 0x%x (1 timeout, 2 scale, 4 label, 8 list)\n", status);
+            st = MPK_ERR_CUDA;
+            goto done;
+        }
+        if (mpkEngineInertia(e, dC, dAssign, &S->inertia) != MPK_OK) st = MPK_ERR_CUDA;
+    }
+done:
+    cudaStreamSynchronize(s);
+    for (auto& x : ev) if (x) cudaEventDestroy(x);
+    cudaEventDestroy(ev_all0);
+    cudaEventDestroy(ev_all1);
+    cudaEventDestroy(ev_x);
+    cudaFree(sums);
+    cudaFree(moved2);
+    cudaFreeHost(h_moved);
+    engine_free(e);
+    return st;
+}
+
+mpkStatus mpkMeansMixed(cublasHandle_t blas, const float* dP, int n, int d, int k, float* dC, int* dAssign,
+                        const mpkParams* params, mpkStats* stats) {
+    return lloyd(blas, dP, n, d, k, dC, dAssign, params, stats, false, "mixed");
+}
+
+mpkStatus mpkMeansFP32(cublasHandle_t blas, const float* dP, int n, int d, int k, float* dC, int* dAssign,
+                       const mpkParams* params, mpkStats* stats) {
+    return lloyd(blas, dP, n, d, k, dC, dAssign, params, stats, true, "fp32");
+}
+
+mpkStatus mpkMeansMultiword(cublasHandle_t blas, const float* dP, int n, int d, int k, float* dC, int* dAssign,
+                            const mpkParams* params, mpkStats* stats) {
+    mpkStats local;
+    mpkStats* S = stats ? stats : &local;
+    mpkStatus st = lloyd(blas, dP, n, d, k, dC, dAssign, params, S, true, "mw");
+    if (st == MPK_OK) {
+        S->mw_products = 3LL * S->iters;
+        S->mw_refine_rows = 0;
+    }
+    return st;
+}
+
+mpkStatus mpkMeansBaselineRT(cublasHandle_t, const float*, int, int, int, float*, int*, const mpkParams*,
+                             mpkStats*) {
+    fprintf(stderr, "mpkmeans_b200: the arXiv:2407.12208 reliability-test baseline is not part of this engine\n");
+    return MPK_ERR_INVALID;
+}
+
+int mpkHaveCuvs(void) { return 0; }
+
+mpkStatus mpkMeansCuvs(cublasHandle_t, const float*, int, int, int, float*, int*, const mpkParams*, mpkStats*) {
+    return MPK_ERR_INVALID;
+}
+
+mpkStatus mpkAssign(cublasHandle_t blas, const float* dP, int n, int d, int k, const float* dC, int* dAssign,
+                    const mpkParams* params, mpkStats* stats) {
+    if (n <= 0 || d <= 0 || k <= 0 || !dP || !dC || !dAssign) return MPK_ERR_INVALID;
+    mpkParams P;
+    if (params) P = *params; else mpkParamsInit(&P);
+    const int refine = (P.use_cond3 || P.use_cond6) ? 1 : 0;
+    cudaStream_t s = stream_of(blas);
+    mpkEngine e = nullptr;
+    mpkStatus st = engine_create(&e, dP, n, d, k, dC, 0.f, n, s, true);
+    if (st != MPK_OK) return st;
+    st = engine_assign(e, dC, dAssign, refine, 0);
+    if (st == MPK_OK && stats) {
+        std::memset(stats, 0, sizeof(*stats));
+        long long rows = 0, cands = 0, full = 0;
+        int status = 0;
+        mpkEngineCounters(e, &rows, &cands, &full, &status);
+        stats->iters = 1;
+        stats->hp_baseline = (long long)n * k;
+        stats->tested = (long long)n * (k - 1);
+        stats->hp_update = cands;
+        stats->n_hist = 1;
+        stats->hist_survivors[0] = rows;
+        if (status) st = MPK_ERR_CUDA;
+    }
+    cudaStreamSynchronize(s);
+    engine_free(e);
+    return st;
+}
+
+mpkStatus mpkUpdate(cublasHandle_t blas, const float* dP, int n, int d, int k, const int* dAssign, float* dC,
+                    float* dMoved2) {
+    if (n <= 0 || d <= 0 || k <= 0 || !dP || !dC || !dAssign) return MPK_ERR_INVALID;
+    cudaStream_t s = stream_of(blas);
+    mpkEngine e = nullptr;
+    mpkStatus st = engine_create(&e, dP, n, d, k, nullptr, 0.f, n, s, false);
+    if (st != MPK_OK) return st;
+    long long* sums = nullptr;
+    if (cudaMalloc(&sums, ((size_t)k * d + k) * sizeof(long long)) != cudaSuccess) {
+        engine_free(e);
+        return MPK_ERR_ALLOC;
+    }
+    st = engine_accumulate(e, dAssign, sums);
+    if (st == MPK_OK) st = engine_finalize(e, sums, dC, dMoved2);
+    int status = 0;
+    if (st == MPK_OK && mpkEngineCounters(e, nullptr, nullptr, nullptr, &status) == MPK_OK && status) {
+        fprintf(stderr, "mpkmeans_b200: mpkUpdate: device status 0x%x\n", status);
+        st = MPK_ERR_INVALID;
+    }
+    cudaStreamSynchronize(s);
+    cudaFree(sums);
+    engine_free(e);
+    return st;
+}
+
+/* ----------------------------------------------------------- data ------ */
+
+void mpkMakeBlobs(int n, int d, int k, float stdv, float center_box, unsigned seed, float* hP, int* hLabels) {
+    /* Same engine, distributions and draw order as the reference's generator
+     * (kmeans/src/data.cu:12-28), so a seed reproduces its points exactly. */
+    std::mt19937 rng(seed);
+    std::uniform_real_distribution<float> box(-center_box, center_box);
+    std::normal_distribution<float> noise(0.f, stdv);
+    std::vector<float> centre((size_t)k * d);
+    for (auto& v : centre) v = box(rng);
+    for (int i = 0; i < n; ++i) {
+        const int c = (int)((long long)i * k / n);
+        if (hLabels) hLabels[i] = c;
+        if (!hP) continue;
+        float* row = hP + (size_t)i * d;
+        const float* cc = centre.data() + (size_t)c * d;
+        for (int t = 0; t < d; ++t) row[t] = cc[t] + noise(rng);
+    }
+}
+
+mpkStatus mpkInitRandomPoints(const float* dP, int n, int d, int k, unsigned seed, float* dC) {
+    /* k distinct rows, chosen by the reference's partial Fisher-Yates under
+     * mt19937(seed ^ 0x9e3779b9) and taken in ascending row order
+     * (kmeans/src/data.cu:30-51), then gathered with one copy per row. */
+    if (!dP || !dC || k <= 0 || d <= 0 || k > n) return MPK_ERR_INVALID;
+    std::mt19937 rng(seed ^ 0x9e3779b9u);
+    std::vector<int> perm(n);
+    for (int i = 0; i < n; ++i) perm[i] = i;
+    for (int i = 0; i < k; ++i) {
+        std::uniform_int_distribution<int> pick(i, n - 1);
+        std::swap(perm[i], perm[pick(rng)]);
+    }
+    std::sort(perm.begin(), perm.begin() + k);
+    for (int j = 0; j < k; ++j)
+        MPK_TRY(cudaMemcpy(dC + (size_t)j * d, dP + (size_t)perm[j] * d, (size_t)d * sizeof(float),
+                           cudaMemcpyDeviceToDevice));
+    return MPK_OK;
+}
+
+mpkStatus mpkLoadBin(const char* path, int d, long long max_rows, int* out_n, float** out_P) {
+    if (!path || d <= 0 || !out_n || !out_P) return MPK_ERR_INVALID;
+    FILE* f = fopen(path, "rb");
+    if (!f) { fprintf(stderr, "mpkLoadBin: cannot open %s\n", path); return MPK_ERR_INVALID; }
+    if (fseeko(f, 0, SEEK_END) != 0) { fclose(f); return MPK_ERR_INVALID; }
+    const long long bytes = (long long)ftello(f);
+    rewind(f);
+    const long long row = (long long)d * (long long)sizeof(float);
+    if (bytes <= 0 || bytes % row != 0) {
+        fprintf(stderr, "mpkLoadBin: %s holds %lld bytes, not a whole number of %d-float rows\n", path, bytes, d);
+        fclose(f);
+        return MPK_ERR_INVALID;
+    }
+    long long rows = bytes / row;
+    if (max_rows > 0 && max_rows < rows) rows = max_rows;
+    if (rows > INT_MAX) { fclose(f); return MPK_ERR_INVALID; }
+    float* P = (float*)malloc((size_t)rows * d * sizeof(float));
+    if (!P) { fclose(f); return MPK_ERR_ALLOC; }
+    const size_t want = (size_t)rows * d;
+    const size_t got = fread(P, sizeof(float), want, f);
+    fclose(f);
+    if (got != want) { free(P); return MPK_ERR_INVALID; }
+    *out_n = (int)rows;
+    *out_P = P;
+    return MPK_OK;
+}
+
+/* LIBSVM text: "<label> <index>:<value> ..." with 1-based indices, '#'
+ * comments and "qid:" tokens skipped.  Two passes: shape, then fill.  Labels
+ * are renumbered 0.. in order of first appearance. */
+mpkStatus mpkLoadLibsvm(const char* path, int* out_n, int* out_d, float** out_P, int** out_labels,
+                        int* out_nclasses) {
+    if (!path || !out_n || !out_d || !out_P) return MPK_ERR_INVALID;
+    auto scan = [&](bool fill, long long* rows, long long* maxidx, float* P, int* L, std::vector<double>* cls,
+                    int d) -> bool {
+        FILE* f = fopen(path, "r");
+        if (!f) return false;
+        char* line = nullptr;
+        size_t cap = 0;
+        long long r = 0;
+        while (getline(&line, &cap, f) != -1) {
+            if (char* h = strchr(line, '#')) *h = '\0';
+            char* p = line;
+            while (*p == ' ' || *p == '\t' || *p == '\r' || *p == '\n') ++p;
+            if (!*p) continue;
+            char* end = nullptr;
+            const double lab = strtod(p, &end);
+            p = end ? end : p;
+            while (*p && *p != ' ' && *p != '\t') ++p;
+            if (fill) {
+                size_t c = 0;
+                while (c < cls->size() && (*cls)[c] != lab) ++c;
+                if (c == cls->size()) cls->push_back(lab);
+                L[r] = (int)c;
+            }
+            while (*p) {
+                while (*p == ' ' || *p == '\t' || *p == '\r' || *p == '\n') ++p;
+                if (!*p) break;
+                char* colon = nullptr;
+                const long idx = strtol(p, &colon, 10);
+                if (colon == p || *colon != ':') {
+                    while (*p && *p != ' ' && *p != '\t') ++p;
+                    continue;
+                }
+                char* vend = nullptr;
+                const double v = strtod(colon + 1, &vend);
+                if (!fill && idx > *maxidx) *maxidx = idx;
+                if (fill && idx >= 1 && idx <= d) P[(size_t)r * d + (idx - 1)] = (float)v;
+                p = (vend && vend > colon + 1) ? vend : colon + 1;
+            }
+            ++r;
+        }
+        free(line);
+        fclose(f);
+        if (rows) *rows = r;
+        return true;
+    };
+    long long rows = 0, maxidx = 0;
+    if (!scan(false, &rows, &maxidx, nullptr, nullptr, nullptr, 0)) {
+        fprintf(stderr, "mpkLoadLibsvm: cannot open %s\n", path);
+        return MPK_ERR_INVALID;
+    }
+    if (rows == 0 || maxidx == 0 || rows > INT_MAX || maxidx > INT_MAX ||
+        (double)rows * (double)maxidx * sizeof(float) > 6e10)
+        return MPK_ERR_INVALID;
+    const int n = (int)rows, d = (int)maxidx;
+    float* P = (float*)calloc((size_t)n * d, sizeof(float));
+    int* L = (int*)calloc((size_t)n, sizeof(int));
+    if (!P || !L) { free(P); free(L); return MPK_ERR_ALLOC; }
+    std::vector<double> cls;
+    if (!scan(true, nullptr, nullptr, P, L, &cls, d)) { free(P); free(L); return MPK_ERR_INVALID; }
+    *out_n = n;
+    *out_d = d;
+    *out_P = P;
+    if (out_labels) *out_labels = L; else free(L);
+    if (out_nclasses) *out_nclasses = (int)cls.size();
+    return MPK_OK;
+}
+
+}  /* extern "C" */

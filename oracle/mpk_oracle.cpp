@@ -1,0 +1,546 @@
+/* mpk_oracle.cpp -- CPU oracle for the mpkmeans hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  Nothing in the product library links, loads or
+ * calls this file; only tests/, __graft_entry__.smoke() and bench.py's
+ * cpu_baseline leg / reference arm use it, as the checker or as the timed CPU
+ * port.  It restates, on the CPU, the arithmetic of the reference's own
+ * k-means and split-precision GEMM so that GPU results can be compared with it
+ * bit for bit where the arithmetic is fixed, and within a stated tolerance
+ * where it is not (tensor-core accumulation order, cuBLAS SGEMM order).
+ *
+ * Reference behaviour followed (paths relative to the CornellHPC/mpkmeans tree):
+ *   kmeans/src/kernels.cu:19-23    argmin tie rule: smaller index wins
+ *   kmeans/src/kernels.cu:83-92    ||c_j||^2: per-thread fmaf, 256-wide tree
+ *   kmeans/src/kernels.cu:549-562  FP32 row argmin of fmaf(-2, G, ||c||^2)
+ *   kmeans/src/kernels.cu:582-602  FP32 refinement dot: 32 lane-strided fmaf
+ *                                  chains, shfl_down tree, fmaf(-2,dot,cn)
+ *   kmeans/src/kernels.cu:683-723  centroid update: FP64 sums, counts,
+ *                                  (float)(sum/cnt), empty cluster keeps old,
+ *                                  moved2 = ||dc||^2 by the 256-wide tree
+ *   kmeans/src/kernels.cu:725-741  inertia in FP64
+ *   kmeans/src/mpkmeans.cu:175-304 mpkMeansFP32: exactly max_iter iterations
+ *                                  unless tol > 0 (Frobenius test, 278-285)
+ *   kmeans/src/mpkmeans.cu:111-119 mpkEpsilon
+ *   kmeans/src/data.cu:12-51       mpkMakeBlobs / mpkInitRandomPoints
+ *   gemm-emulation/src/split.cu:24-32       BF16 peel (RNE, exact residual)
+ *   gemm-emulation/src/split_fp16.cu:31-39  FP16 peel after power-of-two scale
+ *   gemm-emulation/src/split_fp16.cu:236-266 AutoScale: 2^(e-1), 4096/max ~ 2^e
+ *   gemm-emulation/src/gemm.cu:43-60         term schedule (bin, then i)
+ *   gemm-emulation/src/gemm.cu:62-103        range driver semantics
+ *
+ * The FP32 GEMM of the reference (cublasSgemm, PEDANTIC) has no published
+ * summation order, so the oracle's FP32 assignment uses the one FP32 dot the
+ * reference does pin down -- the refinement dot of k_update_flat -- for every
+ * (row, centroid) pair.  Against cuBLAS that is a tolerance pin (near-tie
+ * flips only); against this library's refinement it is exact.
+ *
+ * Build: see oracle/Makefile.  Must be compiled WITHOUT fast-math and with
+ * -ffp-contract=off so that every fmaf() here is the only fused operation.
+ */
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <random>
+#include <vector>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+extern "C" {
+
+/* ------------------------------------------------------------ hashing --- */
+
+static inline uint64_t sm64(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+/* counter-based stream: (seed, stream, counter) -> 64 random bits */
+static inline uint64_t h3(uint64_t seed, uint64_t stream, uint64_t ctr) {
+    return sm64(sm64(seed ^ sm64(stream + 0x632BE59BD9B4E019ull)) ^ ctr);
+}
+static inline double u01(uint64_t h) { return (double)(h >> 11) * 0x1.0p-53; }
+static inline double gauss(uint64_t ha, uint64_t hb) {
+    const double u1 = 1.0 - u01(ha);              /* (0, 1] */
+    const double u2 = u01(hb);
+    return std::sqrt(-2.0 * std::log(u1)) * std::cos(6.283185307179586 * u2);
+}
+
+int orc_num_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
+void orc_set_threads(int t) {
+#ifdef _OPENMP
+    if (t > 0) omp_set_num_threads(t);
+#else
+    (void)t;
+#endif
+}
+
+/* ---------------------------------------------------------- generators --- */
+
+/* Gaussian mixture.  Component means uniform in [-box, box]^d, per-component
+ * sigma uniform in [sig_lo, sig_hi], weights equal or Dirichlet(1) (normalised
+ * exponentials).  Each point draws its component, then mean + sigma*N(0,I).
+ * truth (n ints) and means (ncomp*d) are optional outputs. */
+void orc_make_gmm(int64_t n, int d, int ncomp, uint64_t seed, double box,
+                  double sig_lo, double sig_hi, int dirichlet,
+                  float* P, int* truth, float* means_out) {
+    std::vector<double> mu((size_t)ncomp * d), sig(ncomp), cw(ncomp);
+    for (size_t t = 0; t < mu.size(); ++t)
+        mu[t] = box * (2.0 * u01(h3(seed, 1, t)) - 1.0);
+    for (int j = 0; j < ncomp; ++j)
+        sig[j] = sig_lo + (sig_hi - sig_lo) * u01(h3(seed, 2, (uint64_t)j));
+    double acc = 0.0;
+    for (int j = 0; j < ncomp; ++j) {
+        const double w = dirichlet ? -std::log(1.0 - u01(h3(seed, 3, (uint64_t)j))) : 1.0;
+        acc += w;
+        cw[j] = acc;
+    }
+    for (int j = 0; j < ncomp; ++j) cw[j] /= acc;
+    if (means_out)
+        for (size_t t = 0; t < mu.size(); ++t) means_out[t] = (float)mu[t];
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        const double u = u01(h3(seed, 4, (uint64_t)i));
+        int c = (int)(std::lower_bound(cw.begin(), cw.end(), u) - cw.begin());
+        if (c >= ncomp) c = ncomp - 1;
+        if (truth) truth[i] = c;
+        if (!P) continue;
+        for (int t = 0; t < d; ++t) {
+            const uint64_t e = (uint64_t)i * (uint64_t)d + (uint64_t)t;
+            P[(size_t)i * d + t] =
+                (float)(mu[(size_t)c * d + t] + sig[c] * gauss(h3(seed, 5, 2 * e), h3(seed, 5, 2 * e + 1)));
+        }
+    }
+}
+
+/* Unit-norm embedding-like mixture: centre ~ N(0,I), point = centre + N(0,I),
+ * then each point is L2-normalised. */
+void orc_make_sphere(int64_t n, int d, int ncomp, uint64_t seed, float* P, int* truth) {
+    std::vector<double> mu((size_t)ncomp * d);
+    for (size_t t = 0; t < mu.size(); ++t) mu[t] = gauss(h3(seed, 11, 2 * t), h3(seed, 11, 2 * t + 1));
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        int c = (int)(u01(h3(seed, 12, (uint64_t)i)) * ncomp);
+        if (c >= ncomp) c = ncomp - 1;
+        if (truth) truth[i] = c;
+        double nn = 0.0;
+        std::vector<double> v(d);
+        for (int t = 0; t < d; ++t) {
+            const uint64_t e = (uint64_t)i * (uint64_t)d + (uint64_t)t;
+            v[t] = mu[(size_t)c * d + t] + gauss(h3(seed, 13, 2 * e), h3(seed, 13, 2 * e + 1));
+            nn += v[t] * v[t];
+        }
+        const double inv = nn > 0 ? 1.0 / std::sqrt(nn) : 1.0;
+        for (int t = 0; t < d; ++t) P[(size_t)i * d + t] = (float)(v[t] * inv);
+    }
+}
+
+/* Cancellation stress: global offset o with ||o|| = onorm, means o + N(0, 4I),
+ * points mean + N(0, I). */
+void orc_make_offset(int64_t n, int d, int ncomp, uint64_t seed, double onorm, float* P, int* truth) {
+    std::vector<double> o(d), mu((size_t)ncomp * d);
+    double nn = 0.0;
+    for (int t = 0; t < d; ++t) { o[t] = gauss(h3(seed, 21, 2 * t), h3(seed, 21, 2 * t + 1)); nn += o[t] * o[t]; }
+    for (int t = 0; t < d; ++t) o[t] *= onorm / std::sqrt(nn);
+    for (size_t t = 0; t < mu.size(); ++t)
+        mu[t] = o[t % d] + 2.0 * gauss(h3(seed, 22, 2 * t), h3(seed, 22, 2 * t + 1));
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        int c = (int)(u01(h3(seed, 23, (uint64_t)i)) * ncomp);
+        if (c >= ncomp) c = ncomp - 1;
+        if (truth) truth[i] = c;
+        for (int t = 0; t < d; ++t) {
+            const uint64_t e = (uint64_t)i * (uint64_t)d + (uint64_t)t;
+            P[(size_t)i * d + t] = (float)(mu[(size_t)c * d + t] + gauss(h3(seed, 24, 2 * e), h3(seed, 24, 2 * e + 1)));
+        }
+    }
+}
+
+/* Standalone-GEMM inputs: (a) u in [-1,1]; (b) u * 2^e, integer e in [-emax, emax]. */
+void orc_make_uniform(int64_t count, uint64_t seed, int emax, float* A) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < count; ++i) {
+        double v = 2.0 * u01(h3(seed, 31, (uint64_t)i)) - 1.0;
+        if (emax > 0) {
+            const int e = (int)(u01(h3(seed, 32, (uint64_t)i)) * (2 * emax + 1)) - emax;
+            v = std::ldexp(v, e);
+        }
+        A[i] = (float)v;
+    }
+}
+
+/* k-means++ seeding (D^2 sampling, FP64 distances), deterministic in seed.
+ * The reference has no k-means++; the harness provides the seeds through C. */
+void orc_kmeanspp(const float* P, int64_t n, int d, int k, uint64_t seed, float* C) {
+    std::vector<double> d2((size_t)n, INFINITY);
+    int64_t first = (int64_t)(u01(h3(seed, 41, 0)) * (double)n);
+    if (first >= n) first = n - 1;
+    std::memcpy(C, P + (size_t)first * d, sizeof(float) * d);
+    for (int c = 1; c <= k; ++c) {
+        const float* cc = C + (size_t)(c - 1) * d;
+#pragma omp parallel for schedule(static)
+        for (int64_t i = 0; i < n; ++i) {
+            double s = 0.0;
+            const float* p = P + (size_t)i * d;
+            for (int t = 0; t < d; ++t) { const double v = (double)p[t] - (double)cc[t]; s += v * v; }
+            if (s < d2[i]) d2[i] = s;
+        }
+        if (c == k) break;
+        double tot = 0.0;
+        for (int64_t i = 0; i < n; ++i) tot += d2[i];
+        const double r = u01(h3(seed, 41, (uint64_t)c)) * tot;
+        double run = 0.0;
+        int64_t pick = n - 1;
+        for (int64_t i = 0; i < n; ++i) { run += d2[i]; if (run > r) { pick = i; break; } }
+        std::memcpy(C + (size_t)c * d, P + (size_t)pick * d, sizeof(float) * d);
+    }
+}
+
+/* mpkMakeBlobs (kmeans/src/data.cu:12-28): same generator, same draw order, so
+ * the same seed gives the reference's points bit for bit under libstdc++. */
+void orc_make_blobs_ref(int n, int d, int k, float stdv, float box, unsigned seed, float* P, int* labels) {
+    std::mt19937 rng(seed);
+    std::uniform_real_distribution<float> ubox(-box, box);
+    std::normal_distribution<float> g(0.f, stdv);
+    std::vector<float> centers((size_t)k * d);
+    for (size_t t = 0; t < centers.size(); ++t) centers[t] = ubox(rng);
+    for (int i = 0; i < n; ++i) {
+        const int c = (int)((long long)i * k / n);
+        if (labels) labels[i] = c;
+        if (!P) continue;
+        for (int t = 0; t < d; ++t) P[(size_t)i * d + t] = centers[(size_t)c * d + t] + g(rng);
+    }
+}
+
+/* mpkInitRandomPoints (kmeans/src/data.cu:30-51): partial Fisher-Yates under
+ * mt19937(seed ^ 0x9e3779b9), first k indices sorted.  Writes the indices. */
+void orc_init_random_idx(int n, int k, unsigned seed, int* idx_out) {
+    std::mt19937 rng(seed ^ 0x9e3779b9u);
+    std::vector<int> idx(n);
+    for (int i = 0; i < n; ++i) idx[i] = i;
+    for (int i = 0; i < k; ++i) {
+        std::uniform_int_distribution<int> pick(i, n - 1);
+        std::swap(idx[i], idx[pick(rng)]);
+    }
+    std::sort(idx.begin(), idx.begin() + k);
+    for (int j = 0; j < k; ++j) idx_out[j] = idx[j];
+}
+
+/* ------------------------------------------------------ FP32 primitives --- */
+
+/* ||c||^2 exactly as k_row_norms: thread t of 256 runs an fmaf chain over
+ * t, t+256, ...; then the shared-memory halving tree. */
+float orc_norm2_tree(const float* c, int d) {
+    float sh[256];
+    for (int t = 0; t < 256; ++t) {
+        float acc = 0.f;
+        for (int f = t; f < d; f += 256) acc = std::fmaf(c[f], c[f], acc);
+        sh[t] = acc;
+    }
+    for (int off = 128; off > 0; off >>= 1)
+        for (int t = 0; t < off; ++t) sh[t] = sh[t] + sh[t + off];
+    return sh[0];
+}
+
+void orc_row_norms(const float* C, int k, int d, float* cn) {
+    for (int j = 0; j < k; ++j) cn[j] = orc_norm2_tree(C + (size_t)j * d, d);
+}
+
+/* FP32 dot exactly as k_update_flat: lane l runs an fmaf chain over
+ * l, l+32, ...; then __shfl_down_sync(16, 8, 4, 2, 1); the total is lane 0's. */
+static inline float dot_warp(const float* p, const float* c, int d) {
+    float s[32];
+    for (int l = 0; l < 32; ++l) s[l] = 0.f;
+    int t = 0;
+    for (; t + 32 <= d; t += 32)
+        for (int l = 0; l < 32; ++l) s[l] = std::fmaf(p[t + l], c[t + l], s[l]);
+    for (int l = 0; t + l < d; ++l) s[l] = std::fmaf(p[t + l], c[t + l], s[l]);
+    for (int off = 16; off > 0; off >>= 1)
+        for (int l = 0; l < off; ++l) s[l] = s[l] + s[l + off];
+    return s[0];
+}
+
+float orc_dot_warp(const float* p, const float* c, int d) { return dot_warp(p, c, d); }
+
+/* Row argmin of D(i,j) = fmaf(-2, dot_warp(p_i, c_j), cn[j]); the smaller
+ * index wins an exact tie.  labels/dbest per row; dbest may be NULL. */
+void orc_assign_fp32(const float* P, int64_t n, int d, const float* C, int k, int* labels, float* dbest) {
+    std::vector<float> cn(k);
+    orc_row_norms(C, k, d, cn.data());
+#pragma omp parallel for schedule(dynamic, 64)
+    for (int64_t i = 0; i < n; ++i) {
+        const float* p = P + (size_t)i * d;
+        float bv = INFINITY;
+        int bj = k;
+        for (int j = 0; j < k; ++j) {
+            const float v = std::fmaf(-2.f, dot_warp(p, C + (size_t)j * d, d), cn[j]);
+            if (v < bv || (v == bv && j < bj)) { bv = v; bj = j; }
+        }
+        labels[i] = bj;
+        if (dbest) dbest[i] = bv;
+    }
+}
+
+/* Full FP32 distance rows, for small cases only: D[i*k+j]. */
+void orc_dist_fp32(const float* P, int64_t n, int d, const float* C, int k, float* D) {
+    std::vector<float> cn(k);
+    orc_row_norms(C, k, d, cn.data());
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i)
+        for (int j = 0; j < k; ++j)
+            D[(size_t)i * k + j] = std::fmaf(-2.f, dot_warp(P + (size_t)i * d, C + (size_t)j * d, d), cn[j]);
+}
+
+/* Direct-formula FP64 distances ||p_i - c_j||^2 for listed (i, j) pairs. */
+void orc_dist64_pairs(const float* P, int d, const float* C, const int64_t* rows, const int* cols,
+                      int64_t m, double* out) {
+#pragma omp parallel for schedule(static)
+    for (int64_t e = 0; e < m; ++e) {
+        const float* p = P + (size_t)rows[e] * d;
+        const float* c = C + (size_t)cols[e] * d;
+        double s = 0.0;
+        for (int t = 0; t < d; ++t) { const double v = (double)p[t] - (double)c[t]; s += v * v; }
+        out[e] = s;
+    }
+}
+
+/* ------------------------------------------------------------- update ---- */
+
+static void finalize_common(const double* sums, const int64_t* counts, int k, int d, float* C, float* moved2) {
+    for (int j = 0; j < k; ++j) {
+        float sh[256];
+        for (int t = 0; t < 256; ++t) sh[t] = 0.f;
+        for (int t = 0; t < 256; ++t) {
+            float acc = 0.f;
+            for (int f = t; f < d; f += 256) {
+                const size_t o = (size_t)j * d + f;
+                const float old = C[o];
+                const float nv = counts[j] > 0 ? (float)(sums[o] / (double)counts[j]) : old;
+                C[o] = nv;
+                const float dv = nv - old;
+                acc = std::fmaf(dv, dv, acc);
+            }
+            sh[t] = acc;
+        }
+        for (int off = 128; off > 0; off >>= 1)
+            for (int t = 0; t < off; ++t) sh[t] = sh[t] + sh[t + off];
+        if (moved2) moved2[j] = sh[0];
+    }
+}
+
+/* Reference update (k_zero / k_accumulate / k_finalize): FP64 sums, counts,
+ * C = (float)(sum / cnt), empty cluster keeps its centroid.  Row chunks are
+ * summed per thread and combined in thread order, so the result is fixed for a
+ * given thread count. */
+void orc_update_fp64(const float* P, int64_t n, int d, const int* labels, int k, float* C,
+                     float* moved2, int64_t* counts_out) {
+    const int nt = orc_num_threads();
+    std::vector<double> part((size_t)nt * k * d, 0.0);
+    std::vector<int64_t> cnt((size_t)nt * k, 0);
+#pragma omp parallel num_threads(nt)
+    {
+        int tid = 0;
+#ifdef _OPENMP
+        tid = omp_get_thread_num();
+#endif
+        double* s = part.data() + (size_t)tid * k * d;
+        int64_t* c = cnt.data() + (size_t)tid * k;
+#pragma omp for schedule(static)
+        for (int64_t i = 0; i < n; ++i) {
+            const int a = labels[i];
+            const float* p = P + (size_t)i * d;
+            double* row = s + (size_t)a * d;
+            for (int t = 0; t < d; ++t) row[t] += (double)p[t];
+            c[a] += 1;
+        }
+    }
+    std::vector<double> sums((size_t)k * d, 0.0);
+    std::vector<int64_t> counts(k, 0);
+    for (int t = 0; t < nt; ++t) {
+        for (size_t e = 0; e < sums.size(); ++e) sums[e] += part[(size_t)t * k * d + e];
+        for (int j = 0; j < k; ++j) counts[j] += cnt[(size_t)t * k + j];
+    }
+    finalize_common(sums.data(), counts.data(), k, d, C, moved2);
+    if (counts_out) for (int j = 0; j < k; ++j) counts_out[j] = counts[j];
+}
+
+/* The product's update arithmetic: every coordinate is quantised once to a
+ * fixed-point integer q = rint(x * 2^frac) (ties to even), integer sums are
+ * exact and order independent, and C = (float)(((double)S * 2^-frac) / cnt).
+ * The GPU must match this bit for bit. */
+void orc_update_fixed(const float* P, int64_t n, int d, const int* labels, int k, int frac,
+                      float* C, float* moved2, int64_t* counts_out, int64_t* sums_out) {
+    std::vector<int64_t> S((size_t)k * d, 0), counts(k, 0);
+    const double sc = std::ldexp(1.0, frac);
+    for (int64_t i = 0; i < n; ++i) {
+        const int a = labels[i];
+        for (int t = 0; t < d; ++t)
+            S[(size_t)a * d + t] += (int64_t)std::nearbyint((double)P[(size_t)i * d + t] * sc);
+        counts[a] += 1;
+    }
+    std::vector<double> sums((size_t)k * d);
+    const double inv = std::ldexp(1.0, -frac);
+    for (size_t e = 0; e < sums.size(); ++e) sums[e] = (double)S[e] * inv;
+    finalize_common(sums.data(), counts.data(), k, d, C, moved2);
+    if (counts_out) for (int j = 0; j < k; ++j) counts_out[j] = counts[j];
+    if (sums_out) for (size_t e = 0; e < S.size(); ++e) sums_out[e] = S[e];
+}
+
+/* Inertia sum_i ||p_i - c_a||^2 in FP64 (kmeans/src/kernels.cu:725-741). */
+double orc_inertia(const float* P, int64_t n, int d, const float* C, const int* labels) {
+    double tot = 0.0;
+#pragma omp parallel for reduction(+ : tot) schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        const float* p = P + (size_t)i * d;
+        const float* c = C + (size_t)labels[i] * d;
+        double s = 0.0;
+        for (int t = 0; t < d; ++t) { const double v = (double)p[t] - (double)c[t]; s = std::fma(v, v, s); }
+        tot += s;
+    }
+    return tot;
+}
+
+/* mpkMeansFP32 (kmeans/src/mpkmeans.cu:175-304) on the CPU.  update_mode 0 is
+ * the reference's FP64 update, 1 the fixed-point update with `frac` bits.
+ * Labels are assign(C_{M-1}); C returns C_M.  Returns the iterations run. */
+int orc_lloyd(const float* P, int64_t n, int d, int k, float* C, int* labels, int max_iter,
+              float tol, int update_mode, int frac, double* inertia) {
+    std::vector<float> moved2(k);
+    int it = 0;
+    for (; it < max_iter; ++it) {
+        orc_assign_fp32(P, n, d, C, k, labels, nullptr);
+        if (update_mode == 1) orc_update_fixed(P, n, d, labels, k, frac, C, moved2.data(), nullptr, nullptr);
+        else                  orc_update_fp64(P, n, d, labels, k, C, moved2.data(), nullptr);
+        if (tol > 0.f) {
+            double fro2 = 0.0;
+            for (int j = 0; j < k; ++j) fro2 += (double)moved2[j];
+            if (fro2 < (double)tol * (double)tol) { ++it; break; }
+        }
+    }
+    if (inertia) *inertia = orc_inertia(P, n, d, C, labels);
+    return it;
+}
+
+/* mpkEpsilon (kmeans/src/mpkmeans.cu:111-119). */
+double orc_mpk_epsilon(int d, int accum_fp16) {
+    const double u = accum_fp16 ? 1.0 / 2048.0 : 1.0 / 16777216.0;
+    const double g = (double)d * u;
+    if (g >= 1.0) return -1.0;
+    return 2.0 / 2048.0 + g / (1.0 - g);
+}
+
+/* -------------------------------------------------- split-precision GEMM --- */
+
+static inline uint16_t f2bf(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+static inline float bf2f(uint16_t h) {
+    const uint32_t u = (uint32_t)h << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+static inline uint16_t f2h(float f) {
+    const _Float16 h = (_Float16)f;              /* IEEE round to nearest even */
+    uint16_t u;
+    std::memcpy(&u, &h, 2);
+    return u;
+}
+static inline float h2f(uint16_t u) {
+    _Float16 h;
+    std::memcpy(&h, &u, 2);
+    return (float)h;
+}
+
+float orc_bf16_round(float f) { return bf2f(f2bf(f)); }
+float orc_fp16_round(float f) { return h2f(f2h(f)); }
+
+/* mpemuSplitBF16 semantics: column-major rows x cols (lda), nsplits planes at
+ * element stride `stride`, plane leading dimension lds. */
+void orc_split_bf16(const float* A, int64_t lda, int64_t rows, int64_t cols, int nsplits,
+                    uint16_t* S, int64_t lds, int64_t stride) {
+#pragma omp parallel for schedule(static)
+    for (int64_t c = 0; c < cols; ++c)
+        for (int64_t r = 0; r < rows; ++r) {
+            float a = A[c * lda + r];
+            for (int s = 0; s < nsplits; ++s) {
+                const uint16_t b = f2bf(a);
+                S[s * stride + c * lds + r] = b;
+                a = a - bf2f(b);
+            }
+        }
+}
+
+void orc_split_fp16(const float* A, int64_t lda, int64_t rows, int64_t cols, int nsplits, float scale,
+                    uint16_t* S, int64_t lds, int64_t stride) {
+#pragma omp parallel for schedule(static)
+    for (int64_t c = 0; c < cols; ++c)
+        for (int64_t r = 0; r < rows; ++r) {
+            float a = A[c * lda + r] * scale;
+            for (int s = 0; s < nsplits; ++s) {
+                const uint16_t b = f2h(a);
+                S[s * stride + c * lds + r] = b;
+                a = a - h2f(b);
+            }
+        }
+}
+
+/* mpemuAutoScaleFP16: largest power of two <= 4096 / max|A| (finite entries),
+ * 1 for an all-zero matrix. */
+float orc_autoscale_fp16(const float* A, int64_t lda, int64_t rows, int64_t cols) {
+    float mx = 0.f;
+    for (int64_t c = 0; c < cols; ++c)
+        for (int64_t r = 0; r < rows; ++r) {
+            const float v = std::fabs(A[c * lda + r]);
+            if (v > mx && std::isfinite(v)) mx = v;
+        }
+    if (!(mx > 0.f)) return 1.f;
+    int e = 0;
+    std::frexp(4096.0f / mx, &e);
+    const float s = std::ldexp(1.0f, e - 1);
+    return (s > 0.f && std::isfinite(s)) ? s : 1.f;
+}
+
+/* mpemuTermSchedule: ascending bin i+j, then ascending i.  ij gets 2 ints per
+ * term. */
+int orc_term_schedule(int nsplits, int max_terms, int* ij) {
+    if (nsplits < 1 || nsplits > 16 || max_terms <= 0 || !ij) return 0;
+    int w = 0;
+    for (int bin = 0; bin <= 2 * (nsplits - 1) && w < max_terms; ++bin)
+        for (int i = 0; i <= bin && w < max_terms; ++i) {
+            const int j = bin - i;
+            if (i < nsplits && j < nsplits) { ij[2 * w] = i; ij[2 * w + 1] = j; ++w; }
+        }
+    return w;
+}
+
+/* Exact FP64 product of column-major FP32 matrices: D = op(A) op(B) (m x n),
+ * transA/transB 0 or 1.  For small cases and sampled rows in tests. */
+void orc_gemm_f64(int transA, int transB, int64_t m, int64_t n, int64_t k, const float* A, int64_t lda,
+                  const float* B, int64_t ldb, double* D, int64_t ldd) {
+#pragma omp parallel for schedule(static)
+    for (int64_t j = 0; j < n; ++j)
+        for (int64_t i = 0; i < m; ++i) {
+            double s = 0.0;
+            for (int64_t t = 0; t < k; ++t) {
+                const double a = transA ? A[i * lda + t] : A[t * lda + i];
+                const double b = transB ? B[t * ldb + j] : B[j * ldb + t];
+                s += a * b;
+            }
+            D[j * ldd + i] = s;
+        }
+}
+
+}  /* extern "C" */

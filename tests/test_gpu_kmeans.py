@@ -1,0 +1,317 @@
+"""Parity of the B200 k-means engine with the oracle, through the C ABI.
+
+Bit-exact bars (integer / index work and the FP32 arithmetic the engine pins):
+  * labels == the oracle's FP32 argmin of fmaf(-2, dot_warp, ||c||^2), the
+    reference's refinement order, smaller index on ties;
+  * centroids == the oracle's fixed-point update, bit for bit;
+Tolerance bars against the reference's own outputs (golden fixtures):
+  * label mismatches only on near-ties, FP64 relative gap < 1e-5;
+  * centroids within 1e-5 relative (per-centroid norm), inertia within 1e-5.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle as O
+import parity
+from conftest import golden
+
+torch = pytest.importorskip("torch")
+import mpkmeans_b200 as M  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None:
+        t = t.to(dtype)
+    return t.cuda()
+
+
+def make_problem(n, d, k, seed, spread=1.0):
+    rng = np.random.default_rng(seed)
+    P = (rng.standard_normal((n, d)) * spread).astype(np.float32)
+    idx = rng.choice(n, size=k, replace=False)
+    C = (P[idx] + 0.1 * rng.standard_normal((k, d))).astype(np.float32)
+    return P, C
+
+
+def adjudicate(P, C, la, lb):
+    idx = np.nonzero(la != lb)[0]
+    if len(idx) == 0:
+        return 0, 0.0
+    da = O.dist64_pairs(P, C, idx, la[idx])
+    db = O.dist64_pairs(P, C, idx, lb[idx])
+    return len(idx), float((np.abs(da - db) / np.maximum(np.maximum(da, db), 1e-300)).max())
+
+
+def gpu_assign(P, C, **kw):
+    dP, dC = dev(P), dev(C)
+    lab = torch.full((P.shape[0],), -7, dtype=torch.int32, device="cuda")
+    st = M.assign(dP, dC, lab, M.params_init(**kw) if kw else None)
+    torch.cuda.synchronize()
+    return lab.cpu().numpy(), st
+
+
+# ------------------------------------------------------------ assignment ----
+
+@pytest.mark.parametrize("n,d,k", [(300, 16, 10), (1000, 32, 64), (2000, 64, 100), (1500, 128, 256),
+                                   (1000, 200, 300), (4000, 128, 1024), (999, 256, 17), (129, 1, 3),
+                                   (128, 64, 1), (5000, 96, 640)])
+def test_assign_equals_fp32_oracle(cuda, n, d, k):
+    P, C = make_problem(n, d, k, seed=n + d + k)
+    lab, st = gpu_assign(P, C)
+    ref = O.assign_fp32(P, C)
+    bad = np.nonzero(lab != ref)[0]
+    assert len(bad) == 0, (len(bad), bad[:10], lab[bad[:10]], ref[bad[:10]])
+    assert st.hp_baseline == n * k
+
+
+def test_assign_tie_break_smaller_index(cuda):
+    rng = np.random.default_rng(1)
+    n, d, k = 640, 32, 48
+    P = rng.standard_normal((n, d)).astype(np.float32)
+    base = rng.standard_normal((k // 3, d)).astype(np.float32)
+    C = np.concatenate([base, base, base])           # every centroid appears three times
+    lab, _ = gpu_assign(P, C)
+    assert np.array_equal(lab, O.assign_fp32(P, C))
+    assert lab.max() < k // 3                         # the first copy always wins
+    # points exactly between two centroids
+    P2 = np.zeros((256, 8), np.float32)
+    C2 = np.zeros((2, 8), np.float32)
+    C2[0, 0], C2[1, 0] = 1.0, -1.0
+    lab2, _ = gpu_assign(P2, C2)
+    assert (lab2 == 0).all()
+
+
+def test_assign_error_bound_holds(cuda):
+    """The tensor-core distance of the chosen centroid stays well inside the
+    certified bound the filter uses."""
+    P, C = make_problem(20000, 128, 512, seed=5, spread=3.0)
+    dP, dC = dev(P), dev(C)
+    with M.Engine(dP, 512, C0=dC) as e:
+        info = e.info()
+        out4 = torch.zeros((20000, 4), dtype=torch.float32, device="cuda")
+        lab = torch.empty(20000, dtype=torch.int32, device="cuda")
+        e.trace(out4)
+        e.assign(dC, lab, refine=True)
+        torch.cuda.synchronize()
+        e.trace(None)
+    t = out4.cpu().numpy()
+    v0 = t[:, 0].astype(np.float64)
+    j0 = t[:, 2].view(np.int32)
+    cn = O.row_norms(C).astype(np.float64)
+    dot = np.einsum("ij,ij->i", P.astype(np.float64), C[j0].astype(np.float64))
+    exact = cn[j0] - 2.0 * dot
+    xn = np.linalg.norm(P.astype(np.float64), axis=1)
+    cmax = np.sqrt(cn.max())
+    T = info["c1"] * xn * cmax + info["c2"] * info["eta"] * (xn + cmax) + 2.0 ** -22 * 2 * np.abs(exact)
+    ratio = np.abs(v0 - exact) / T
+    assert ratio.max() < 0.25, ratio.max()
+
+
+def test_assign_raw_mode_close(cuda):
+    P, C = make_problem(8000, 64, 200, seed=9)
+    lab, st = gpu_assign(P, C, use_cond3=0, use_cond6=0)
+    ref = O.assign_fp32(P, C)
+    nm, rel = adjudicate(P, C, lab, ref)
+    assert nm <= 8 and rel < 1e-5
+    assert st.hp_update == 0
+
+
+def test_assign_rejects_invalid(cuda):
+    P, C = make_problem(100, 8, 4, seed=2)
+    dP, dC = dev(P), dev(C)
+    lab = torch.empty(100, dtype=torch.int32, device="cuda")
+    lib = M.lib()
+    assert lib.mpkAssign(None, dP.data_ptr(), 0, 8, 4, dC.data_ptr(), lab.data_ptr(), None, None) == M.MPK_ERR_INVALID
+    assert lib.mpkAssign(None, dP.data_ptr(), 100, 8, 0, dC.data_ptr(), lab.data_ptr(), None, None) == M.MPK_ERR_INVALID
+    assert lib.mpkMeansMixed(None, dP.data_ptr(), 3, 8, 4, dC.data_ptr(), lab.data_ptr(), None, None) == M.MPK_ERR_INVALID
+    P3 = np.zeros((16, 300), np.float32)
+    assert lib.mpkAssign(None, dev(P3).data_ptr(), 16, 300, 4, dev(np.zeros((4, 300), np.float32)).data_ptr(),
+                         lab.data_ptr(), None, None) == M.MPK_ERR_INVALID
+
+
+# ---------------------------------------------------------------- update ----
+
+@pytest.mark.parametrize("n,d,k", [(1000, 16, 10), (20000, 128, 1024), (3000, 33, 64), (777, 256, 5000)])
+def test_update_bit_exact(cuda, n, d, k):
+    P, C = make_problem(max(n, k), d, k, seed=k)
+    P = P[:n] if n >= k else P
+    n = P.shape[0]
+    rng = np.random.default_rng(3)
+    lab = rng.integers(0, k, size=n).astype(np.int32)
+    lab[lab == 3] = 4                                  # cluster 3 empty: keeps its centroid
+    dC = dev(C)
+    moved = torch.empty(k, dtype=torch.float32, device="cuda")
+    M.update(dev(P), dev(lab), dC, moved)
+    got = dC.cpu().numpy()
+    frac = O.fixed_frac(float(np.abs(P).max()), n)
+    want, m2, _, _ = O.update_fixed(P, lab, C, frac)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    assert np.array_equal(got[3], C[3])
+    assert np.array_equal(moved.cpu().numpy().view(np.uint32), m2.view(np.uint32))
+    ref, _, _ = O.update_fp64(P, lab, C)
+    ulp = np.abs(got.view(np.int32).astype(np.int64) - ref.view(np.int32).astype(np.int64))
+    assert ulp.max() <= 1
+
+
+def test_update_rejects_bad_labels(cuda):
+    P, C = make_problem(500, 8, 4, seed=7)
+    lab = np.zeros(500, np.int32)
+    lab[17] = 9
+    lib = M.lib()
+    rc = lib.mpkUpdate(None, dev(P).data_ptr(), 500, 8, 4, dev(lab).data_ptr(), dev(C).data_ptr(), None)
+    assert rc == M.MPK_ERR_INVALID
+
+
+# ---------------------------------------------------------------- Lloyd -----
+
+def test_lloyd_config1_bit_exact_vs_oracle(cuda):
+    P = O.make_config1(100_000, 32, seed=1)
+    C0 = O.kmeanspp(P, 64, seed=1)
+    dC = dev(C0)
+    lab = torch.empty(100_000, dtype=torch.int32, device="cuda")
+    st = M.means_mixed(dev(P), dC, lab, M.params_init(max_iter=20))
+    frac = O.fixed_frac(float(np.abs(P).max()), len(P))
+    olab, oC, oine, it = O.lloyd(P, C0, 20, update_mode=1, frac=frac)
+    assert st.iters == 20 and it == 20
+    assert np.array_equal(lab.cpu().numpy(), olab)
+    assert np.array_equal(dC.cpu().numpy().view(np.uint32), oC.view(np.uint32))
+    assert abs(st.inertia - oine) <= 1e-9 * oine
+
+
+def test_lloyd_config1_vs_reference_golden(cuda):
+    """Against the reference's own FP32 run: per iteration on the reference's
+    centroids the engine's labels differ only on FP32 near-ties; end of run
+    (20 iterations, not converged) agreement and inertia are bounded."""
+    g = golden("ref_config1.npz")
+    P = O.make_config1(int(g["n"]), int(g["d"]), seed=int(g["seed"]))
+    dP = dev(P)
+    if "traj_labels" in g.files:
+        C = g["C0"]
+        for t in range(g["traj_labels"].shape[0]):
+            lab, _ = gpu_assign(P, C)
+            s = parity.summary(P, C, lab, g["traj_labels"][t].astype(np.int32))
+            assert s["max_gap32"] < 1e-5 and s["agree"] >= 0.9999, (t, s)
+            C = g["traj_C"][t]
+    dC = dev(g["C0"])
+    lab = torch.empty(P.shape[0], dtype=torch.int32, device="cuda")
+    st = M.means_mixed(dP, dC, lab, M.params_init(max_iter=20))
+    lab = lab.cpu().numpy()
+    assert (lab == g["labels"].astype(np.int32)).mean() >= 0.999
+    assert abs(st.inertia - float(g["inertia"])) / float(g["inertia"]) < 1e-5
+
+
+def test_lloyd_tol_and_fp32_driver(cuda):
+    P = O.make_config1(20_000, 16, seed=8)
+    C0 = O.kmeanspp(P, 32, seed=8)
+    lab = torch.empty(20_000, dtype=torch.int32, device="cuda")
+    dC = dev(C0)
+    st = M.means_fp32(dev(P), dC, lab, M.params_init(max_iter=300, tol=1e-4))
+    assert 1 <= st.iters < 300
+    _, oC, _, it = O.lloyd(P, C0, 300, tol=1e-4, update_mode=1, frac=O.fixed_frac(float(np.abs(P).max()), len(P)))
+    assert it == st.iters
+    assert np.array_equal(dC.cpu().numpy(), oC)
+
+
+def test_engine_shards_equal_whole(cuda):
+    """Two row shards, int64 sums added, equal the one-engine update exactly --
+    the property the multi-GPU allreduce relies on."""
+    P, C = make_problem(30000, 64, 256, seed=11)
+    dP, dC = dev(P), dev(C)
+    pmax = float(max(np.abs(P).max(), np.abs(C).max()))
+    lab_all = torch.empty(30000, dtype=torch.int32, device="cuda")
+    with M.Engine(dP, 256, pmax_global=pmax, n_global=30000) as e:
+        sums = torch.empty(e.sums_length, dtype=torch.int64, device="cuda")
+        e.assign(dC, lab_all)
+        e.accumulate(lab_all, sums)
+        C_whole = dC.clone()
+        e.finalize(sums, C_whole)
+    parts = []
+    for lo, hi in ((0, 12345), (12345, 30000)):
+        with M.Engine(dP[lo:hi], 256, pmax_global=pmax, n_global=30000) as e:
+            lab = torch.empty(hi - lo, dtype=torch.int32, device="cuda")
+            s = torch.empty(e.sums_length, dtype=torch.int64, device="cuda")
+            e.assign(dC, lab)
+            e.accumulate(lab, s)
+            torch.cuda.synchronize()
+            parts.append((lab, s))
+    assert torch.equal(torch.cat([parts[0][0], parts[1][0]]), lab_all)
+    tot = parts[0][1] + parts[1][1]
+    assert torch.equal(tot, sums)
+    with M.Engine(dP, 256, pmax_global=pmax, n_global=30000) as e:
+        C_sh = dC.clone()
+        e.finalize(tot, C_sh)
+    assert torch.equal(C_sh, C_whole)
+
+
+def test_mg_entry_single_gpu_matches(cuda):
+    P = O.make_config1(50_000, 32, seed=5)
+    C0 = O.kmeanspp(P, 64, seed=5)
+    dP = dev(P)
+    lab1 = torch.empty(50_000, dtype=torch.int32, device="cuda")
+    dC1 = dev(C0)
+    M.means_mixed(dP, dC1, lab1, M.params_init(max_iter=5))
+    lab2 = torch.empty(50_000, dtype=torch.int32, device="cuda")
+    dC2 = dev(C0)
+    devs = (ctypes.c_int * 1)(0)
+    Ps = (ctypes.c_void_p * 1)(dP.data_ptr())
+    ns = (ctypes.c_int * 1)(50_000)
+    Cs = (ctypes.c_void_p * 1)(dC2.data_ptr())
+    As = (ctypes.c_void_p * 1)(lab2.data_ptr())
+    st = M.mpkStats()
+    p = M.params_init(max_iter=5)
+    rc = M.lib().mpkMeansMixedMG(1, devs, Ps, ns, 32, 64, Cs, As, ctypes.byref(p), ctypes.byref(st))
+    assert rc == M.MPK_OK
+    assert torch.equal(lab1, lab2) and torch.equal(dC1, dC2)
+
+
+# -------------------------------------------------------- config-3 shape ----
+
+def test_config3_sample_vs_oracle_and_reference(cuda):
+    n, d, k = 200_000, 128, 1024
+    P = O.make_gmm(n, d, k, 3, 5.0, 0.5, 2.0, True)
+    C0 = P[np.sort(O.init_random_idx(n, k, 3))].copy()
+    lab, st = gpu_assign(P, C0)
+    rows = np.arange(0, n, 20)
+    assert np.array_equal(lab[rows], O.assign_fp32(P[rows], C0))
+    g = None
+    try:
+        g = golden("ref_config3_sample.npz")
+    except pytest.skip.Exception:
+        pass
+    if g is not None:
+        s = parity.summary(P, C0, lab, g["labels_it0"].astype(np.int32))
+        assert s["agree"] >= 0.9999 and s["max_gap32"] < 1e-5 and s["max_gap64"] < 1e-5, s
+
+
+def test_config3_full_size_properties(cuda):
+    """n = 1e7, d = 128, k = 1024: labels on a row sample
+    equal the oracle's, the update conserves the point count, and two runs are
+    bit-identical."""
+    n, d, k = 10_000_000, 128, 1024
+    P = O.make_gmm(n, d, k, 3, 5.0, 0.5, 2.0, False)
+    C0 = P[np.sort(O.init_random_idx(n, k, 3))].copy()
+    dP = dev(P)
+    del P
+    res = []
+    for _ in range(2):
+        dC = dev(C0)
+        lab = torch.empty(n, dtype=torch.int32, device="cuda")
+        st = M.means_mixed(dP, dC, lab, M.params_init(max_iter=2))
+        res.append((lab.clone(), dC.clone(), st.inertia))
+    assert torch.equal(res[0][0], res[1][0]) and torch.equal(res[0][1], res[1][1])
+    # the last assignment was made against C1 = the centroids after one update
+    dC1 = dev(C0)
+    lab1 = torch.empty(n, dtype=torch.int32, device="cuda")
+    M.means_mixed(dP, dC1, lab1, M.params_init(max_iter=1))
+    C1 = dC1.cpu().numpy()
+    rng = np.random.default_rng(0)
+    rows = np.sort(rng.choice(n, size=20000, replace=False))
+    Ps = dP[torch.from_numpy(rows).cuda()].cpu().numpy()
+    assert np.array_equal(res[0][0].cpu().numpy()[rows], O.assign_fp32(Ps, C1))
+    counts = torch.bincount(res[0][0].long(), minlength=k)
+    assert int(counts.sum()) == n
