@@ -1,0 +1,435 @@
+#!/usr/bin/env python
+"""bench.py -- Lloyd iterations/s of the B200 k-means engine.
+
+Workload: n = 10,000,000 points, d = 128, k = 1024, FP32; a 1024-component
+Gaussian mixture (means U[-5,5]^d, sigma_j U[0.5,2], Dirichlet(1) weights),
+seeded synthetic data generated on the device; initial centroids are k
+distinct random points.  One step = one Lloyd iteration over all n points:
+centroid split, fused tensor-core assignment, near-tie refinement, the exact
+fixed-point update and (N > 1) one int64 NCCL allreduce of the sums.  With N
+GPUs the n rows are sharded (strong scaling: total work fixed).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+`value` is device-timed (inputs resident in HBM, 5 GB of points > the 126 MB
+L2, so no flush is needed), max over ranks.  `e2e` runs the public C ABI
+(mpkMeansMixed, 25 iterations) from pinned host buffers, copies included.
+`--impl reference` times the reference's own implementation of the path
+(oracle/_ref: CornellHPC/mpkmeans' mpkMeansFP32, compiled from its sources --
+the reference has no CPU k-means; its mixed driver overflows int32 indices at
+this size) on the same workload on rank 0's GPU.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import re
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+N_FULL, D, K = 10_000_000, 128, 1024
+SEED = 3
+E2E_ITERS = 25
+METRIC = "Lloyd iterations/s, config 3 (n=1e7, d=128, k=1024, FP32)"
+UNIT = "iter/s"
+
+
+# --------------------------------------------------------------- setup ------
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--n", type=int, default=N_FULL, help="total points (default: config 3)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return j.get("hbm_gbs", 6650.0), j.get("bf16_tflops", 1590.0), j.get("bf16_tflops_sustained", 1400.0), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def profile_figure(name: str, key: str):
+    """A number recorded in a committed ncu summary (profiles/<name>), or None."""
+    p = ROOT / "profiles" / name
+    if not p.exists():
+        return None
+    m = re.search(rf"^{re.escape(key)}:\s*([0-9.eE+-]+)", p.read_text(), flags=re.M)
+    return float(m.group(1)) if m else None
+
+
+# ---------------------------------------------------------- synthetic data --
+
+def component_params(seed, ncomp, d, box, sig_lo, sig_hi):
+    g = torch.Generator().manual_seed(seed)
+    means = (torch.rand(ncomp, d, generator=g, dtype=torch.float64) * 2 - 1) * box
+    sig = sig_lo + (sig_hi - sig_lo) * torch.rand(ncomp, generator=g, dtype=torch.float64)
+    w = -torch.log1p(-torch.rand(ncomp, generator=g, dtype=torch.float64))
+    cw = torch.cumsum(w / w.sum(), 0)
+    return means.float(), sig.float(), cw
+
+
+def gen_shard(n_local, rank, device):
+    means, sig, cw = component_params(SEED, K, D, 5.0, 0.5, 2.0)
+    means, sig, cw = means.to(device), sig.to(device), cw.to(device)
+    g = torch.Generator(device=device).manual_seed(SEED * 1000003 + rank)
+    P = torch.empty((n_local, D), dtype=torch.float32, device=device)
+    chunk = 1 << 20
+    for r0 in range(0, n_local, chunk):
+        r1 = min(n_local, r0 + chunk)
+        u = torch.rand(r1 - r0, generator=g, device=device, dtype=torch.float64)
+        comp = torch.clamp(torch.searchsorted(cw, u), max=K - 1)
+        P[r0:r1] = means[comp] + sig[comp, None] * torch.randn((r1 - r0, D), generator=g, device=device)
+    return P
+
+
+def shard_rows(n, world, rank):
+    base, rem = divmod(n, world)
+    return base + (1 if rank < rem else 0)
+
+
+# -------------------------------------------------------------- clocks ------
+
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={self.FIELDS}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.flush()
+        rows = [l.split(",") for l in Path(self.f.name).read_text().splitlines() if l.count(",") >= 8]
+        os.unlink(self.f.name)
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i] and "Not" not in r[5 + i]})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------- our engine -----
+
+def run_ours(args, world, rank, local):
+    import mpkmeans_b200 as M
+    dev = torch.device("cuda", local)
+    n_total = args.n
+    n_local = shard_rows(n_total, world, rank)
+    P = gen_shard(n_local, rank, dev)
+    # initial centroids: k distinct rows of rank 0's shard, broadcast
+    if rank == 0:
+        g = torch.Generator(device=dev).manual_seed(SEED)
+        idx = torch.sort(torch.randperm(n_local, generator=g, device=dev)[:K]).values
+        C0 = P[idx].clone()
+    else:
+        C0 = torch.empty((K, D), dtype=torch.float32, device=dev)
+    pmax = torch.maximum(P.abs().max(), C0.abs().max()).reshape(1)
+    if world > 1:
+        dist.broadcast(C0, 0)
+        pmax = torch.maximum(P.abs().max(), C0.abs().max()).reshape(1)
+        dist.all_reduce(pmax, op=dist.ReduceOp.MAX)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    eng = M.Engine(P, K, pmax_global=float(pmax.item()), n_global=n_total, stream=stream)
+    labels = torch.empty(n_local, dtype=torch.int32, device=dev)
+    sums = torch.empty(eng.sums_length, dtype=torch.int64, device=dev)
+    C = C0.clone()
+
+    def step():
+        eng.assign(C, labels)
+        eng.accumulate(labels, sums)
+        if world > 1:
+            dist.all_reduce(sums)
+        eng.finalize(sums, C)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = Clocks(local)
+    time.sleep(0.3)
+    eng.profile(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    prof = eng.profile_read()
+    t_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t_ms, op=dist.ReduceOp.MAX)
+    t_ms = float(t_ms.item())
+    cnt = eng.counters()
+
+    # one more assignment on saved centroids, for the label check (untimed)
+    C_chk = C.clone()
+    eng.assign(C_chk, labels)
+    torch.cuda.synchronize()
+
+    res = {"t_ms": t_ms, "prof": prof, "clk": clk, "counters": cnt, "n_local": n_local}
+    res["e2e"] = None if args.no_e2e else run_e2e(M, P, C0, world, rank, dev, n_total)
+    res["cpu"] = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        res["cpu"] = cpu_baseline(P, C_chk, labels)
+    if cnt["status"] != 0:
+        raise RuntimeError(f"engine device status {cnt['status']}")
+    eng.close()
+    return res
+
+
+def run_e2e(M, P, C0, world, rank, dev, n_total, steps=2):
+    """Public API from pinned host buffers: H2D of the points and start
+    centroids, the fit (25 iterations), D2H of labels and centroids."""
+    hP = torch.empty(P.shape, dtype=torch.float32, pin_memory=True)
+    hP.copy_(P)
+    hC0 = torch.empty(C0.shape, dtype=torch.float32, pin_memory=True)
+    hC0.copy_(C0)
+    hL = torch.empty(P.shape[0], dtype=torch.int32, pin_memory=True)
+    hC = torch.empty(C0.shape, dtype=torch.float32, pin_memory=True)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+
+    def one():
+        dP = hP.to(dev, non_blocking=True)
+        dC = hC0.to(dev, non_blocking=True)
+        lab = torch.empty(P.shape[0], dtype=torch.int32, device=dev)
+        if world == 1:
+            M.means_mixed(dP, dC, lab, M.params_init(max_iter=E2E_ITERS), blas=torch.cuda.current_blas_handle())
+        else:
+            pmax = torch.maximum(dP.abs().max(), dC.abs().max()).reshape(1)
+            dist.all_reduce(pmax, op=dist.ReduceOp.MAX)
+            with M.Engine(dP, K, pmax_global=float(pmax.item()), n_global=n_total, stream=stream) as e:
+                s = torch.empty(e.sums_length, dtype=torch.int64, device=dev)
+                for _ in range(E2E_ITERS):
+                    e.assign(dC, lab)
+                    e.accumulate(lab, s)
+                    dist.all_reduce(s)
+                    e.finalize(s, dC)
+        hL.copy_(lab, non_blocking=True)
+        hC.copy_(dC, non_blocking=True)
+
+    one()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        one()
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t = float(t.item())
+    return {"value": E2E_ITERS * steps / (t / 1e3), "unit": UNIT,
+            "h2d_bytes_per_step": int(P.numel() * 4 + C0.numel() * 4),
+            "d2h_bytes_per_step": int(P.shape[0] * 4 + C0.numel() * 4),
+            "iters_per_step": E2E_ITERS, "api": "mpkMeansMixed" if world == 1 else "mpkEngine* + NCCL allreduce"}
+
+
+def cpu_baseline(P, C_chk, labels):
+    """The oracle port (C++/OpenMP restatement of mpkMeansFP32) on this host's
+    cores: one Lloyd iteration (assignment + FP64 update) on a bounded row
+    sample of the same workload, extrapolated to n.  Its labels on the sample
+    also score the GPU labels against the same centroids (label match %)."""
+    import oracle as O
+    threads = O.lib().orc_num_threads()
+    rng = np.random.default_rng(0)
+    n = P.shape[0]
+    pilot = np.sort(rng.choice(n, size=min(n, 4000), replace=False))
+    Ps = P[torch.from_numpy(pilot).to(P.device)].cpu().numpy()
+    C = C_chk.cpu().numpy()
+    t0 = time.perf_counter()
+    O.assign_fp32(Ps, C)
+    t_pilot = (time.perf_counter() - t0) / len(pilot)
+    m = int(min(n, max(len(pilot), 12.0 / max(t_pilot, 1e-9))))
+    rows = np.sort(rng.choice(n, size=m, replace=False))
+    Ps = P[torch.from_numpy(rows).to(P.device)].cpu().numpy()
+    t0 = time.perf_counter()
+    lab = O.assign_fp32(Ps, C)
+    O.update_fp64(Ps, lab, C)
+    t = time.perf_counter() - t0
+    gpu_lab = labels[torch.from_numpy(rows).to(labels.device)].cpu().numpy()
+    match = float((gpu_lab == lab).mean()) * 100.0
+    t_full = t * n / m
+    return {"value": 1.0 / t_full, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{m} of {n} rows, one iteration (assignment + FP64 update), {t:.1f} s, extrapolated x{n / m:.1f}",
+            "label_match_pct": match, "label_match_rows": m}
+
+
+# ----------------------------------------------------------- reference ------
+
+def run_reference(args, world, rank, local):
+    if rank != 0:
+        return None
+    ref_path = ROOT / "oracle" / "_ref" / "libmpkref.so"
+    if not ref_path.exists():
+        return {"unavailable": "oracle/_ref/libmpkref.so was not built (needs the reference sources at build time)"}
+    import mpkmeans_b200 as M   # struct layouts only
+    ref = ctypes.CDLL(str(ref_path))
+    VP = ctypes.c_void_p
+    ref.mpkMeansFP32.argtypes = [VP, VP, ctypes.c_int, ctypes.c_int, ctypes.c_int, VP, VP,
+                                 ctypes.POINTER(M.mpkParams), ctypes.POINTER(M.mpkStats)]
+    ref.mpkParamsInit.argtypes = [ctypes.POINTER(M.mpkParams)]
+    dev = torch.device("cuda", local)
+    n = args.n
+    P = gen_shard(n, 0, dev)
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    C0 = P[torch.sort(torch.randperm(n, generator=g, device=dev)[:K]).values].clone()
+    lab = torch.empty(n, dtype=torch.int32, device=dev)
+    blas = torch.cuda.current_blas_handle()
+    iters = 2
+    prm = M.mpkParams()
+    ref.mpkParamsInit(ctypes.byref(prm))
+    prm.max_iter = iters
+
+    def one():
+        C = C0.clone()
+        st = M.mpkStats()
+        rc = ref.mpkMeansFP32(blas, P.data_ptr(), n, D, K, C.data_ptr(), lab.data_ptr(), ctypes.byref(prm),
+                              ctypes.byref(st))
+        if rc != 0:
+            raise RuntimeError(f"reference mpkMeansFP32 returned {rc}")
+
+    for _ in range(max(1, args.warmup)):
+        one()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        one()
+    e1.record()
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1)
+    value = iters * args.steps / (t / 1e3)
+    return {"value": value, "t_ms": t, "iters_per_step": iters}
+
+
+# ------------------------------------------------------------------ main ----
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup()
+    if world != args.gpus and rank == 0:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    hbm, bf16, bf16_sus, peak_src = measured_peaks()
+    cfg = {"workload": "config 3: 1024-component Gaussian mixture, n=1e7, d=128, k=1024",
+           "n": args.n, "d": D, "k": K, "parallelism": f"rows sharded x{world}, int64 allreduce",
+           "l2": "inputs (5.1 GB points) larger than L2; no flush"}
+
+    if args.impl == "reference":
+        r = run_reference(args, world, rank, local)
+        if rank == 0:
+            if r is None or "unavailable" in r:
+                print(json.dumps({"impl": "reference", "unavailable": (r or {}).get("unavailable", "rank 0 only")}))
+            else:
+                line = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": 1,
+                        "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["t_ms"] / args.steps,
+                        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                        "data": "synthetic (device-generated, seeded)", "config": cfg,
+                        "cpu_baseline": {"kind": "reference", "cores": 1, "value": r["value"], "unit": UNIT,
+                                         "sample": f"full config-3 workload, {r['iters_per_step']} iterations per "
+                                                   "step, through the reference's mpkMeansFP32 (cuBLAS SGEMM + its "
+                                                   "kernels) on one B200; the reference has no CPU k-means"},
+                        "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+                print(json.dumps(line))
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    r = run_ours(args, world, rank, local)
+    if rank == 0:
+        t_ms = r["t_ms"]
+        value = args.steps / (t_ms / 1e3)
+        prof = r["prof"]
+        n_local = r["n_local"]
+        a_ms = prof["assign_ms"] / max(1, prof["assign_launches"])
+        u_ms = prof["accum_ms"] / max(1, prof["accum_launches"])
+        flops = 2.0 * n_local * K * D * 3
+        achieved = flops / (a_ms / 1e3) / 1e12
+        traffic = profile_figure("assign_tc_config3.md", "dram_bytes_per_launch")
+        ubytes = n_local * D * 4 + n_local * 4
+        u_gbs = ubytes / (u_ms / 1e3) / 1e9
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t_ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16x3->f32", "data": "synthetic (device-generated, seeded)", "config": cfg,
+            "effective_tflops": 2.0 * args.n * K * D * value / 1e12,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": bf16_sus, "unit": "TFLOP/s",
+                         "frac": achieved / bf16_sus, "traffic": traffic,
+                         "kernel": "k_assign_tc (fused FP16x3 split GEMM + argmin)",
+                         "work": "2*n*k*d*3 tensor FLOP per launch", "peak_source": f"{peak_src} sustained bf16",
+                         "frac_of_burst": achieved / bf16, "avg_launch_ms": a_ms},
+            "roofline_update": {"bound": "hbm", "achieved": u_gbs, "peak": hbm, "unit": "GB/s", "frac": u_gbs / hbm,
+                                "kernel": "update: k_label_hist + k_bin_scan + k_label_scatter + k_segsum", "work": "n*d*4 + n*4 bytes per update",
+                                "avg_launch_ms": u_ms},
+            "gpu_launches": 8 * args.steps,
+            "refined_rows_per_iter": r["counters"]["rows_refined"] / max(1, args.warmup + args.steps + 1),
+            "refined_candidates_per_iter": r["counters"]["cand_refined"] / max(1, args.warmup + args.steps + 1),
+            "class_rescan_rows_per_iter": r["counters"]["rows_full_scan"] / max(1, args.warmup + args.steps + 1),
+            "clocks": r["clk"],
+        }
+        if r["cpu"] is not None:
+            line["cpu_baseline"] = {k_: r["cpu"][k_] for k_ in ("value", "unit", "cores", "kind", "sample")}
+            line["label_match_pct"] = r["cpu"]["label_match_pct"]
+            line["label_match_rows"] = r["cpu"]["label_match_rows"]
+        if r["e2e"] is not None:
+            line["e2e"] = r["e2e"]
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -21,6 +21,15 @@ mpkStatus mpkDebugSetAssignTrace(mpkEngine e, float* dOut4);
  * and the two error-bound constants of the assignment filter. */
 mpkStatus mpkDebugEngineInfo(mpkEngine e, float* scale, float* eta, int* frac, float* c1, float* c2);
 
+/* While enabled, the engine records a CUDA event pair on its stream around
+ * every assignment kernel and every accumulation (update) kernel launch. */
+mpkStatus mpkDebugProfile(mpkEngine e, int enable);
+
+/* Synchronises; summed device milliseconds and launch counts of the two
+ * kernels since profiling was enabled; clears the record. */
+mpkStatus mpkDebugProfileRead(mpkEngine e, double* assign_ms, long long* assign_launches, double* accum_ms,
+                              long long* accum_launches);
+
 #ifdef __cplusplus
 }
 #endif

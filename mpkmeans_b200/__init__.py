@@ -108,6 +108,9 @@ SIGNATURES = {
     "mpkDebugSetAssignTrace": (_I, [_P, _P]),
     "mpkDebugEngineInfo": (_I, [_P, ctypes.POINTER(_F), ctypes.POINTER(_F), ctypes.POINTER(_I),
                                 ctypes.POINTER(_F), ctypes.POINTER(_F)]),
+    "mpkDebugProfile": (_I, [_P, _I]),
+    "mpkDebugProfileRead": (_I, [_P, ctypes.POINTER(_D), ctypes.POINTER(_LL), ctypes.POINTER(_D),
+                                 ctypes.POINTER(_LL)]),
 }
 
 _lib = None
@@ -250,6 +253,16 @@ class Engine:
         check("mpkDebugEngineInfo", lib().mpkDebugEngineInfo(self.h, ctypes.byref(sc), ctypes.byref(eta),
                                                              ctypes.byref(fr), ctypes.byref(c1), ctypes.byref(c2)))
         return {"scale": sc.value, "eta": eta.value, "frac": fr.value, "c1": c1.value, "c2": c2.value}
+
+    def profile(self, enable: bool = True) -> None:
+        check("mpkDebugProfile", lib().mpkDebugProfile(self.h, int(bool(enable))))
+
+    def profile_read(self) -> dict:
+        a, u = _D(), _D()
+        na, nu = _LL(), _LL()
+        check("mpkDebugProfileRead", lib().mpkDebugProfileRead(self.h, ctypes.byref(a), ctypes.byref(na),
+                                                               ctypes.byref(u), ctypes.byref(nu)))
+        return {"assign_ms": a.value, "assign_launches": na.value, "accum_ms": u.value, "accum_launches": nu.value}
 
     def trace(self, out4) -> None:
         check("mpkDebugSetAssignTrace", lib().mpkDebugSetAssignTrace(self.h, _ptr(out4)))

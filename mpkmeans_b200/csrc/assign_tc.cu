@@ -13,23 +13,26 @@
  *               hi*hi + lo*hi + hi*lo as tcgen05.mma kind::f16 (FP16
  *               operands, FP32 accumulation) into a double-buffered TMEM
  *               accumulator.
- *   warps 2-5   epilogue: tcgen05.ld of the accumulator, D = ||c||^2 - 2 x.c
- *               (the ||x||^2 term is a per-row constant and is dropped, as in
- *               the reference), and a running top-4 (value, index) per row.
+ *   warps 2-9   epilogue, two warps per TMEM lane quarter, each taking half
+ *               the columns of a tile: tcgen05.ld of the accumulator,
+ *               D = ||c||^2 - 2 x.c (fma.rn.f32x2 on column pairs; the ||x||^2
+ *               term is a per-row constant and is dropped, as in the
+ *               reference), and, without branches, for each of 8 column
+ *               classes (column mod 8) the best value with its column and the
+ *               runner-up value.
  *
- * After the last centroid tile of a row tile, every row writes its argmin.  A
- * row whose runner-up lies within the certified error bound T of the best is
- * appended to the refinement list with every top-4 candidate inside T (and an
- * overflow mark when the 4th is also inside T, in which case the refinement
- * scans all k).  The bound covers (a) the FP16x2 split and the dropped lo*lo
- * term, (b) the tensor-core FP32 accumulation, (c) the rounding of the FP32
- * distance that any FP32 evaluation of ||c||^2 - 2 x.c would make; so a row
- * that is not refined has the same argmin under any FP32 summation order, and
- * a refined row gets the exact FP32 answer from the refinement kernel.
+ * After the last centroid tile of a row tile the two halves exchange their
+ * summaries through shared memory and every row writes its argmin (smaller
+ * index on ties).  A row whose runner-up lies within the certified error
+ * bound T of the best is appended to the refinement list with every class
+ * best inside T; when some class's runner-up is also inside T that class may
+ * hold further candidates and the entry marks it for a scan of its columns.  The bound
+ * covers (a) the FP16x2 split and the dropped lo*lo term, (b) the tensor-core
+ * FP32 accumulation, (c) the rounding any FP32 evaluation of ||c||^2 - 2 x.c
+ * makes; so an unrefined row has the same argmin under any FP32 summation
+ * order, and a refined row gets the exact FP32 answer from the refinement.
  */
 #include "engine.cuh"
-
-#include <cstdio>
 
 namespace mpk {
 namespace {
@@ -37,22 +40,46 @@ namespace {
 constexpr int BM = 128;
 constexpr int KC = 64;                  /* FP16 elements per 128-byte swizzle row */
 constexpr int ROW_BYTES = 128;
-constexpr int kThreads = 192;           /* 6 warps */
-constexpr int kSmemBudget = 224 * 1024;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kSmemMax = 232448;        /* 227 KB, no static shared memory */
+constexpr int kMiscBytes = 2048;        /* barriers + the epilogue exchange */
+constexpr int kClasses = 8;
 
 template <int BN, int NKC>
 struct Cfg {
     static constexpr int A_CHUNK = BM * ROW_BYTES;            /* one plane, one K chunk */
     static constexpr int A_TILE = 2 * NKC * A_CHUNK;          /* hi + lo                */
     static constexpr int B_STAGE = BN * ROW_BYTES;
-    static constexpr int A_BUFS = (2 * A_TILE + 2 * B_STAGE <= kSmemBudget) ? 2 : 1;
-    static constexpr int B_RAW = (kSmemBudget - A_BUFS * A_TILE) / B_STAGE;
+    static constexpr int BUDGET = kSmemMax - kMiscBytes;
+    static constexpr int A_BUFS = (2 * A_TILE + 3 * B_STAGE <= BUDGET) ? 2 : 1;
+    static constexpr int B_RAW = (BUDGET - A_BUFS * A_TILE) / B_STAGE;
     static constexpr int B_STAGES = B_RAW > 8 ? 8 : B_RAW;
-    static constexpr int SMEM_BYTES = A_BUFS * A_TILE + B_STAGES * B_STAGE + 1024;
+    static constexpr int TILE_BYTES = A_BUFS * A_TILE + B_STAGES * B_STAGE;
+    static constexpr int SMEM_BYTES = TILE_BYTES + kMiscBytes;
     static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int HALF = BN / 2;                       /* columns per epilogue warp */
+    static constexpr int CHUNKS = HALF / 32;
     static_assert(B_STAGES >= 2, "shared memory too small for two B stages");
+    static_assert(SMEM_BYTES <= kSmemMax, "shared memory");
     static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512, "TMEM columns");
+    static_assert(HALF % 32 == 0, "epilogue half must be whole 32-column chunks");
 };
+
+/* Shared-memory block after the tiles. */
+struct Misc {
+    uint64_t a_full[2], a_empty[2], b_full[8], b_empty[8], t_full[2], t_empty[2], fin;
+    uint32_t tmem_slot;
+    int abort_flag;
+    float wmax[kThreads / 32];
+    /* Row r is exchanged by thread r of the two halves only.  Half 1 writes
+     * (best value, runner-up, best column) before the first named barrier;
+     * half 0 reads them and overwrites the same words with (row best, bound,
+     * refinement slot) for half 1 before the second. */
+    float xa[BM], xb[BM];
+    int xc[BM];
+};
+static_assert(sizeof(Misc) <= kMiscBytes, "misc block");
 
 __device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status) {
     int ok = 0;
@@ -68,6 +95,23 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
     }
 }
 
+__device__ __forceinline__ void named_bar(int id, int count) {
+    asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(count) : "memory");
+}
+
+/* Two FP32 fused multiply-adds in one instruction: (a0,a1)*(b,b)+(c0,c1). */
+__device__ __forceinline__ void fma2(float a0, float a1, uint64_t bb, float c0, float c1, float& d0, float& d1) {
+    uint64_t a, c, d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(c) : "f"(c0), "f"(c1));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(bb), "l"(c));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
+}
+
+__device__ __forceinline__ float thr_of(float T0, float v, float v0) {
+    return (T0 + 0x1.0p-22f * (fabsf(v) + fabsf(v0))) * (1.0f + 0x1.0p-20f);
+}
+
 template <int BN, int NKC>
 __global__ void __launch_bounds__(kThreads, 1)
 k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmC,
@@ -75,43 +119,44 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
             DevParams* __restrict__ prm, int* __restrict__ labels, RefineEntry* __restrict__ list,
             int refine, BoundConsts bc, float4* __restrict__ dbg) {
     using Cf = Cfg<BN, NKC>;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* smA = smem;
     uint8_t* smB = smem + Cf::A_BUFS * Cf::A_TILE;
-
-    __shared__ __align__(8) uint64_t a_full[2], a_empty[2], b_full[8], b_empty[8], t_full[2], t_empty[2], fin_bar;
-    __shared__ uint32_t tmem_slot;
-    __shared__ volatile int abort_flag;
-    __shared__ float s_wmax[kThreads / 32];
+    Misc& ms = *reinterpret_cast<Misc*>(smem + Cf::TILE_BYTES);
+    volatile int* abort_flag = &ms.abort_flag;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long num_mt = (n + BM - 1) / BM;
     const int NT = (k + BN - 1) / BN;
     int* status = &prm->status;
 
+    /* the 128-byte swizzle needs 1024-byte aligned tiles */
+    if (smem_u32(smem) & 1023u) {
+        if (threadIdx.x == 0) atomicOr(status, MPK_DEV_TIMEOUT);
+        return;
+    }
     if (threadIdx.x == 0) {
-        for (int i = 0; i < Cf::A_BUFS; ++i) { mbar_init(&a_full[i], 1); mbar_init(&a_empty[i], 1); }
-        for (int i = 0; i < Cf::B_STAGES; ++i) { mbar_init(&b_full[i], 1); mbar_init(&b_empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&t_full[i], 1); mbar_init(&t_empty[i], 128); }
-        mbar_init(&fin_bar, 1);
-        abort_flag = 0;
+        for (int i = 0; i < Cf::A_BUFS; ++i) { mbar_init(&ms.a_full[i], 1); mbar_init(&ms.a_empty[i], 1); }
+        for (int i = 0; i < Cf::B_STAGES; ++i) { mbar_init(&ms.b_full[i], 1); mbar_init(&ms.b_empty[i], 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&ms.t_full[i], 1); mbar_init(&ms.t_empty[i], 32 * kEpiWarps); }
+        mbar_init(&ms.fin, 1);
+        ms.abort_flag = 0;
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) { tma_prefetch_desc(&tmX); tma_prefetch_desc(&tmC); }
-    if (warp == 1) tmem_alloc(&tmem_slot, Cf::TMEM_COLS);
+    if (warp == 1) tmem_alloc(&ms.tmem_slot, Cf::TMEM_COLS);
 
     /* max_j ||c_j||, for the error bound; cn holds ||c_j||^2 */
     {
         float m = 0.f;
         for (int j = threadIdx.x; j < k; j += kThreads) m = fmaxf(m, cn[j]);
         m = warp_max(m);
-        if (lane == 0) s_wmax[warp] = m;
+        if (lane == 0) ms.wmax[warp] = m;
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem_base = tmem_slot;
+    const uint32_t tmem_base = ms.tmem_slot;
 
     if (warp == 0) {
         /* ------------------------------------------------ TMA producer --- */
@@ -126,31 +171,31 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
             for (long long mt = blockIdx.x; mt < num_mt && ok; mt += gridDim.x, ++lt) {
                 const int ab = lt % Cf::A_BUFS;
                 const uint32_t au = (uint32_t)(lt / Cf::A_BUFS);
-                if (!mbar_wait(&a_empty[ab], (au & 1u) ^ 1u, &abort_flag, status)) { ok = false; break; }
-                mbar_expect_tx(&a_full[ab], Cf::A_TILE);
+                if (!mbar_wait(&ms.a_empty[ab], (au & 1u) ^ 1u, abort_flag, status)) { ok = false; break; }
+                mbar_expect_tx(&ms.a_full[ab], Cf::A_TILE);
                 a_last[ab] = au;
                 for (int p = 0; p < 2; ++p)
                     for (int kc = 0; kc < NKC; ++kc)
-                        tma_load_3d(&tmX, &a_full[ab], smA + ab * Cf::A_TILE + (p * NKC + kc) * Cf::A_CHUNK,
+                        tma_load_3d(&tmX, &ms.a_full[ab], smA + ab * Cf::A_TILE + (p * NKC + kc) * Cf::A_CHUNK,
                                     kc * KC, (int)(mt * BM), p);
                 for (int nt = 0; nt < NT && ok; ++nt)
                     for (int kc = 0; kc < NKC && ok; ++kc)
                         for (int p = 0; p < 2; ++p) {
                             const int st = (int)(bs % Cf::B_STAGES);
                             const uint32_t bu = bs / Cf::B_STAGES;
-                            if (!mbar_wait(&b_empty[st], (bu & 1u) ^ 1u, &abort_flag, status)) { ok = false; break; }
-                            mbar_expect_tx(&b_full[st], Cf::B_STAGE);
+                            if (!mbar_wait(&ms.b_empty[st], (bu & 1u) ^ 1u, abort_flag, status)) { ok = false; break; }
+                            mbar_expect_tx(&ms.b_full[st], Cf::B_STAGE);
                             b_last[st] = bu;
-                            tma_load_3d(&tmC, &b_full[st], smB + st * Cf::B_STAGE, kc * KC, nt * BN, p);
+                            tma_load_3d(&tmC, &ms.b_full[st], smB + st * Cf::B_STAGE, kc * KC, nt * BN, p);
                             ++bs;
                         }
             }
             if (!ok) {
                 /* let every load already issued land before the CTA exits */
                 for (int i = 0; i < Cf::A_BUFS; ++i)
-                    if (a_last[i] != 0xffffffffu) drain_wait(&a_full[i], a_last[i] & 1u);
+                    if (a_last[i] != 0xffffffffu) drain_wait(&ms.a_full[i], a_last[i] & 1u);
                 for (int i = 0; i < Cf::B_STAGES; ++i)
-                    if (b_last[i] != 0xffffffffu) drain_wait(&b_full[i], b_last[i] & 1u);
+                    if (b_last[i] != 0xffffffffu) drain_wait(&ms.b_full[i], b_last[i] & 1u);
             }
         }
     } else if (warp == 1) {
@@ -163,13 +208,13 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
             for (long long mt = blockIdx.x; mt < num_mt && ok; mt += gridDim.x, ++lt) {
                 const int ab = lt % Cf::A_BUFS;
                 const uint32_t au = (uint32_t)(lt / Cf::A_BUFS);
-                if (!mbar_wait(&a_full[ab], au & 1u, &abort_flag, status)) { ok = false; break; }
+                if (!mbar_wait(&ms.a_full[ab], au & 1u, abort_flag, status)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t a_addr = smem_u32(smA + ab * Cf::A_TILE);
                 for (int nt = 0; nt < NT && ok; ++nt, ++ts) {
                     const int tb = (int)(ts & 1u);
                     const uint32_t tu = ts >> 1;
-                    if (!mbar_wait(&t_empty[tb], (tu & 1u) ^ 1u, &abort_flag, status)) { ok = false; break; }
+                    if (!mbar_wait(&ms.t_empty[tb], (tu & 1u) ^ 1u, abort_flag, status)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + (uint32_t)(tb * BN);
                     uint32_t accum = 0;
@@ -179,7 +224,7 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                         /* centroid hi plane: x_hi * c_hi and x_lo * c_hi */
                         int st = (int)(bs % Cf::B_STAGES);
                         uint32_t bu = bs / Cf::B_STAGES;
-                        if (!mbar_wait(&b_full[st], bu & 1u, &abort_flag, status)) { ok = false; break; }
+                        if (!mbar_wait(&ms.b_full[st], bu & 1u, abort_flag, status)) { ok = false; break; }
                         tc_fence_after();
                         const uint32_t bh = smem_u32(smB + st * Cf::B_STAGE);
 #pragma unroll
@@ -192,112 +237,173 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                         for (int ks = 0; ks < KC / 16; ++ks)
                             umma_f16(d_tmem, sw128_desc(al + ks * 32, 16, 1024), sw128_desc(bh + ks * 32, 16, 1024),
                                      idesc, 1);
-                        umma_commit(&b_empty[st]);
+                        umma_commit(&ms.b_empty[st]);
                         ++bs;
                         /* centroid lo plane: x_hi * c_lo */
                         st = (int)(bs % Cf::B_STAGES);
                         bu = bs / Cf::B_STAGES;
-                        if (!mbar_wait(&b_full[st], bu & 1u, &abort_flag, status)) { ok = false; break; }
+                        if (!mbar_wait(&ms.b_full[st], bu & 1u, abort_flag, status)) { ok = false; break; }
                         tc_fence_after();
                         const uint32_t bl = smem_u32(smB + st * Cf::B_STAGE);
 #pragma unroll
                         for (int ks = 0; ks < KC / 16; ++ks)
                             umma_f16(d_tmem, sw128_desc(ah + ks * 32, 16, 1024), sw128_desc(bl + ks * 32, 16, 1024),
                                      idesc, 1);
-                        umma_commit(&b_empty[st]);
+                        umma_commit(&ms.b_empty[st]);
                         ++bs;
                     }
-                    if (ok) umma_commit(&t_full[tb]);
+                    if (ok) umma_commit(&ms.t_full[tb]);
                 }
-                if (ok) umma_commit(&a_empty[ab]);
+                if (ok) umma_commit(&ms.a_empty[ab]);
             }
-            /* every MMA issued by this thread has completed once fin_bar flips */
-            umma_commit(&fin_bar);
-            drain_wait(&fin_bar, 0);
+            /* every MMA issued by this thread has completed once fin flips */
+            umma_commit(&ms.fin);
+            drain_wait(&ms.fin, 0);
         }
     } else {
         /* --------------------------------------------------- epilogue ---- */
-        const int q = warp & 3;                       /* TMEM lane quarter */
+        const int ew = warp - 2;                       /* 0..7 */
+        const int half = ew >> 2;                      /* column half of every tile */
+        const int q = warp & 3;                        /* TMEM lane quarter */
         const int r_loc = q * 32 + lane;
         const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16);
         const float ns = prm->neg2_inv_s2;
+        uint64_t ns2;
+        asm("mov.b64 %0, {%1, %1};" : "=l"(ns2) : "f"(ns));
         const float eta = prm->eta;
         float cmax = 0.f;
-        for (int w = 0; w < kThreads / 32; ++w) cmax = fmaxf(cmax, s_wmax[w]);
+        for (int w = 0; w < kThreads / 32; ++w) cmax = fmaxf(cmax, ms.wmax[w]);
         cmax = sqrtf(cmax);
         uint32_t ts = 0;
         bool ok = true;
-        for (long long mt = blockIdx.x; mt < num_mt && ok; mt += gridDim.x) {
-            float v0 = INFINITY, v1 = INFINITY, v2 = INFINITY, v3 = INFINITY;
-            int j0 = -1, j1 = -1, j2 = -1, j3 = -1;
+        /* The loop runs every tile even after a failed wait (ok == false, the
+         * kernel is aborting): both halves must reach the same named barriers. */
+        for (long long mt = blockIdx.x; mt < num_mt; mt += gridDim.x) {
+            float a0[kClasses], a1[kClasses];
+            int i0[kClasses];
+#pragma unroll
+            for (int c = 0; c < kClasses; ++c) { a0[c] = INFINITY; a1[c] = INFINITY; i0[c] = -1; }
             for (int nt = 0; nt < NT; ++nt, ++ts) {
                 const int tb = (int)(ts & 1u);
                 const uint32_t tu = ts >> 1;
-                if (!wait_warp(&t_full[tb], tu & 1u, &abort_flag, status)) { ok = false; break; }
+                if (ok) ok = wait_warp(&ms.t_full[tb], tu & 1u, abort_flag, status);
+                if (!ok) continue;
                 tc_fence_after();
-#pragma unroll 1
-                for (int c = 0; c < BN / 32; ++c) {
-                    uint32_t r[32];
-                    tmem_ld32(t_lane + (uint32_t)(tb * BN + c * 32), r);
+                const int col0 = half * Cf::HALF;              /* first column of this warp */
+                int pos[kClasses];                               /* column in this tile, -1 */
+#pragma unroll
+                for (int c = 0; c < kClasses; ++c) pos[c] = -1;
+#pragma unroll
+                for (int cc = 0; cc < Cf::CHUNKS; cc += 2) {
+                    uint32_t r[2][32];
+                    tmem_ld32(t_lane + (uint32_t)(tb * BN + col0 + cc * 32), r[0]);
+                    if (cc + 1 < Cf::CHUNKS) tmem_ld32(t_lane + (uint32_t)(tb * BN + col0 + (cc + 1) * 32), r[1]);
                     tmem_ld_wait();
-                    const int jb = nt * BN + c * 32;
-                    const float4* cn4 = reinterpret_cast<const float4*>(cn + jb);
 #pragma unroll
-                    for (int u = 0; u < 8; ++u) {
-                        const float4 cc = __ldg(cn4 + u);
-                        const float cv[4] = {cc.x, cc.y, cc.z, cc.w};
+                    for (int h = 0; h < 2; ++h) {
+                        if (cc + h >= Cf::CHUNKS) break;
+                        const int jt = col0 + (cc + h) * 32;     /* tile-relative column of r[h][0] */
+                        const float4* cn4 = reinterpret_cast<const float4*>(cn + nt * BN + jt);
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float D = fmaf(__uint_as_float(r[4 * u + e]), ns, cv[e]);
-                            if (D < v3) {
-                                const int jj = jb + 4 * u + e;
-                                if (D < v2) {
-                                    v3 = v2; j3 = j2;
-                                    if (D < v1) {
-                                        v2 = v1; j2 = j1;
-                                        if (D < v0) { v1 = v0; j1 = j0; v0 = D; j0 = jj; }
-                                        else { v1 = D; j1 = jj; }
-                                    } else { v2 = D; j2 = jj; }
-                                } else { v3 = D; j3 = jj; }
+                        for (int u = 0; u < 8; ++u) {
+                            const float4 cv = __ldg(cn4 + u);
+                            float D[4];
+                            fma2(__uint_as_float(r[h][4 * u]), __uint_as_float(r[h][4 * u + 1]), ns2, cv.x, cv.y,
+                                 D[0], D[1]);
+                            fma2(__uint_as_float(r[h][4 * u + 2]), __uint_as_float(r[h][4 * u + 3]), ns2, cv.z, cv.w,
+                                 D[2], D[3]);
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const int c = (4 * u + e) & (kClasses - 1);
+                                const bool p = D[e] < a0[c];
+                                a1[c] = fminf(a1[c], fmaxf(a0[c], D[e]));
+                                pos[c] = p ? (jt + 4 * u + e) : pos[c];
+                                a0[c] = fminf(a0[c], D[e]);
                             }
                         }
                     }
                 }
                 tc_fence_before();
-                mbar_arrive(&t_empty[tb]);
+                mbar_arrive(&ms.t_empty[tb]);
+#pragma unroll
+                for (int c = 0; c < kClasses; ++c)
+                    if (pos[c] >= 0) i0[c] = nt * BN + pos[c];
             }
-            if (!ok) break;
 
+            /* this half's best (smaller column on ties) and runner-up value */
+            float hv0 = a0[0], hv1 = a1[0];
+            int hj0 = i0[0];
+#pragma unroll
+            for (int c = 1; c < kClasses; ++c) {
+                const bool better = a0[c] < hv0 || (a0[c] == hv0 && (unsigned)i0[c] < (unsigned)hj0);
+                hv1 = fminf(hv1, fminf(a1[c], better ? hv0 : a0[c]));
+                hv0 = better ? a0[c] : hv0;
+                hj0 = better ? i0[c] : hj0;
+            }
+            const int bar_id = 1 + q;
+            if (half == 1) {
+                ms.xa[r_loc] = hv0;
+                ms.xb[r_loc] = hv1;
+                ms.xc[r_loc] = hj0;
+            }
+            named_bar(bar_id, 64);
             const long long row = mt * BM + r_loc;
-            bool flag = false;
-            int ovf = 0, c1 = -1, c2 = -1, c3 = -1;
-            if (row < n) {
-                labels[row] = j0;
-                if (dbg) dbg[row] = make_float4(v0, v1, __int_as_float(j0), __int_as_float(j1));
-                if (refine && j1 >= 0) {
-                    const float xn = xnorm[row];
-                    const float T0 = bc.c1 * xn * cmax + bc.c2 * eta * (xn + cmax);
-                    const float av0 = fabsf(v0);
-                    const float t1 = (T0 + 0x1.0p-22f * (fabsf(v1) + av0)) * (1.0f + 0x1.0p-20f);
-                    flag = (v1 - v0) <= t1;
-                    if (flag) {
-                        c1 = j1;
-                        if (j2 >= 0 && (v2 - v0) <= (T0 + 0x1.0p-22f * (fabsf(v2) + av0)) * (1.0f + 0x1.0p-20f)) c2 = j2;
-                        if (j3 >= 0 && (v3 - v0) <= (T0 + 0x1.0p-22f * (fabsf(v3) + av0)) * (1.0f + 0x1.0p-20f)) { c3 = j3; ovf = 1; }
+            if (half == 0) {
+                const float ov0 = ms.xa[r_loc], ov1 = ms.xb[r_loc];
+                const int oj0 = ms.xc[r_loc];
+                const bool other = ov0 < hv0 || (ov0 == hv0 && (unsigned)oj0 < (unsigned)hj0);
+                const float v1 = fminf(fminf(hv1, ov1), other ? hv0 : ov0);
+                const float v0 = other ? ov0 : hv0;
+                const int j0 = other ? oj0 : hj0;
+                float T0 = 0.f;
+                bool flag = false;
+                if (ok && row < n) {
+                    labels[row] = j0;
+                    if (dbg) dbg[row] = make_float4(v0, v1, __int_as_float(j0), __int_as_float(0));
+                    if (refine) {
+                        const float xn = xnorm[row];
+                        T0 = bc.c1 * xn * cmax + bc.c2 * eta * (xn + cmax);
+                        flag = (v1 - v0) <= thr_of(T0, v1, v0);
                     }
                 }
+                int slot = -1;
+                const unsigned m = __ballot_sync(0xffffffffu, flag);
+                if (m) {
+                    unsigned base = 0;
+                    if (lane == 0) base = atomicAdd(&prm->nflag, (unsigned)__popc(m));
+                    base = __shfl_sync(0xffffffffu, base, 0);
+                    if (flag) slot = (int)(base + __popc(m & ((1u << lane) - 1u)));
+                }
+                ms.xa[r_loc] = v0;
+                ms.xb[r_loc] = T0;
+                ms.xc[r_loc] = slot;
+                if (slot >= 0) {
+                    RefineEntry* E = list + slot;
+                    int ovf = 0;
+#pragma unroll
+                    for (int c = 0; c < kClasses; ++c) {
+                        const bool in0 = i0[c] >= 0 && (a0[c] - v0) <= thr_of(T0, a0[c], v0);
+                        E->c[c] = in0 ? i0[c] : -1;
+                        ovf |= (a1[c] - v0) <= thr_of(T0, a1[c], v0) ? (1 << c) : 0;
+                    }
+                    E->row = (int)row;
+                    E->ovf[0] = ovf;
+                }
             }
-            const unsigned m = __ballot_sync(0xffffffffu, flag);
-            if (m) {
-                unsigned base = 0;
-                if (lane == 0) base = atomicAdd(&prm->nflag, (unsigned)__popc(m));
-                base = __shfl_sync(0xffffffffu, base, 0);
-                if (flag) {
-                    RefineEntry e;
-                    e.row = (int)row;
-                    e.ovf = ovf;
-                    e.c[0] = j0; e.c[1] = c1; e.c[2] = c2; e.c[3] = c3;
-                    list[base + __popc(m & ((1u << lane) - 1u))] = e;
+            named_bar(bar_id, 64);
+            if (half == 1) {
+                const int slot = ms.xc[r_loc];
+                if (slot >= 0) {
+                    const float v0 = ms.xa[r_loc], T0 = ms.xb[r_loc];
+                    RefineEntry* E = list + slot;
+                    int ovf = 0;
+#pragma unroll
+                    for (int c = 0; c < kClasses; ++c) {
+                        const bool in0 = i0[c] >= 0 && (a0[c] - v0) <= thr_of(T0, a0[c], v0);
+                        E->c[kClasses + c] = in0 ? i0[c] : -1;
+                        ovf |= (a1[c] - v0) <= thr_of(T0, a1[c], v0) ? (1 << c) : 0;
+                    }
+                    E->ovf[1] = ovf;
                 }
             }
         }

@@ -31,10 +31,16 @@ struct DevParams {
     unsigned long long novf_total;   /* rows refined against all k centroids  */
 };
 
+/* A row to re-decide in FP32.  The assignment epilogue tracks, per column
+ * class (tile half h, column mod 8 = c), the best column and the runner-up
+ * value; c[8h + c] is that class's best when it lies within the bound of the
+ * row's best, and bit c of ovf[h] is set when the class's runner-up does too
+ * (the class may then hold more candidates: all its columns are rescanned). */
 struct RefineEntry {
     int row;
-    int ovf;             /* 1: candidate list may be incomplete, scan all k */
-    int c[4];            /* candidate centroids, -1 when unused             */
+    int ovf[2];
+    int pad;
+    int c[16];
 };
 
 /* Error-bound constants of the assignment filter (host computed). */
@@ -73,11 +79,19 @@ int  assign_supported(int d);                /* 1 when d fits the kernel      */
 cudaError_t launch_assign(const AssignArgs& a, cudaStream_t s);
 
 /* ---- refine / update (kernels.cu) ---- */
-void launch_refine(const float* P, const float* C, const float* cn, int d, int k,
+void launch_refine(const float* P, const float* C, const float* cn, int d, int k, int bn,
                    const RefineEntry* list, DevParams* prm, int* labels, long long n_cap,
                    unsigned long long* hist_slot, int num_sms, cudaStream_t s);
-void launch_accum_fixed(const float* P, long long n, int d, const int* labels, int k,
-                        DevParams* prm, long long* sums, long long* counts, int num_sms, cudaStream_t s);
+/* Scratch of the sorted update: perm n ints, bin_start k+1, cursor k, hist k. */
+struct UpdateScratch {
+    int* perm;
+    int* bin_start;
+    int* cursor;
+    int* hist;
+};
+/* sums (k*d int64) must be zero on entry; counts (k int64) are written. */
+void launch_update_sorted(const float* P, long long n, int d, const int* labels, int k, DevParams* prm,
+                          long long* sums, long long* counts, UpdateScratch sc, int num_sms, cudaStream_t s);
 void launch_finalize_fixed(const long long* sums, const long long* counts, int k, int d,
                            const DevParams* prm, float* C, float* moved2, cudaStream_t s);
 void launch_inertia(const float* P, const float* C, const int* labels, long long n, int d,

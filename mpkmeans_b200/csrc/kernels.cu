@@ -36,8 +36,8 @@ __global__ void k_maxabs(const float* __restrict__ A, long long count, float* ou
  *   scale s = largest power of two with s * max|P, C0| <= 4096, the rule of
  *             gemm-emulation/src/split_fp16.cu:255-262, so hi words sit well
  *             inside FP16's normal range and lo words keep 11 bits;
- *   frac    = 62 - E - ceil(log2 n) with max|P| < 2^E, so that n quantised
- *             coordinates of magnitude < 2^(E+frac) sum below 2^62. */
+ *   frac    = min(100, 62 - E - ceil(log2 n)) with max|P| < 2^E, so that n
+ *             quantised coordinates of magnitude < 2^(E+frac) sum below 2^62. */
 __global__ void k_set_scale(DevParams* prm, long long n_total) {
     const float m = fmaxf(prm->pmax, prm->c0max);
     float s = 1.f;
@@ -55,7 +55,7 @@ __global__ void k_set_scale(DevParams* prm, long long n_total) {
     int lg = 0;
     while ((1ll << lg) < n_total && lg < 62) ++lg;
     int frac = 62 - E - lg;
-    if (frac > 200) frac = 200;
+    if (frac > 100) frac = 100;   /* 2^frac stays a finite FP32 scale */
     prm->frac = frac;
 }
 
@@ -132,52 +132,92 @@ __global__ void k_prep_c(const float* __restrict__ C, int k, int d, int dp, DevP
 
 /* ------------------------------------------------------------- refine ---- */
 
-/* FP32 dot in the order of the reference's refinement (kmeans/src/kernels.cu
- * 582-602): lane l runs an fmaf chain over l, l+32, ...; shfl_down tree.  The
- * total is valid in lane 0. */
-__device__ __forceinline__ float dot_warp(const float* __restrict__ p, const float* __restrict__ c, int d, int lane) {
-    float acc = 0.f;
-    for (int t = lane; t < d; t += 32) acc = fmaf(p[t], c[t], acc);
-    for (int off = 16; off > 0; off >>= 1) acc += __shfl_down_sync(FULL, acc, off);
-    return acc;
+/* Up to four candidate distances at once, each exactly as the reference's
+ * refinement forms it (kmeans/src/kernels.cu:582-602): lane l runs an fmaf chain over l, l+32, ... (the point
+ * row is held in registers, pr[i] = p[lane + 32 i]), the shfl_down tree sums
+ * the lanes, and D = fmaf(-2, dot, ||c||^2).  The best (smaller index on a
+ * tie) is folded into (bv, bj), valid in lane 0. */
+__device__ __forceinline__ void eval4(const float (&pr)[8], const float* __restrict__ C, const float* __restrict__ cn,
+                                      int d, int lane, const int (&j)[4], float& bv, int& bj) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int t = lane + 32 * i;
+        if (t < d) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                if (j[q] >= 0) acc[q] = fmaf(pr[i], __ldg(C + (size_t)j[q] * d + t), acc[q]);
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[q] += __shfl_down_sync(FULL, acc[q], off);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        if (j[q] < 0) continue;
+        const float v = fmaf(-2.f, acc[q], cn[j[q]]);
+        if (v < bv || (v == bv && j[q] < bj)) { bv = v; bj = j[q]; }
+    }
 }
 
-/* One warp per refinement entry: recompute each candidate's distance in FP32,
- * D = fmaf(-2, dot, ||c||^2), and keep the smallest, the smaller index on a
- * tie.  An overflow entry scans all k centroids. */
+/* One warp per refinement entry: the listed candidates, then every column of
+ * each overflowing class, in batches of four; the label is the smallest FP32
+ * distance, the smaller index on a tie.  Control flow is warp uniform (every
+ * lane reads the same entry). */
 __global__ void k_refine(const float* __restrict__ P, const float* __restrict__ C, const float* __restrict__ cn,
-                         int d, int k, const RefineEntry* __restrict__ list, DevParams* __restrict__ prm,
+                         int d, int k, int bn, const RefineEntry* __restrict__ list, DevParams* __restrict__ prm,
                          int* __restrict__ labels, long long cap, unsigned long long* hist_slot) {
     const int lane = threadIdx.x & 31;
     const long long nf = prm->nflag < (unsigned long long)cap ? (long long)prm->nflag : cap;
     const long long wstride = (long long)gridDim.x * (blockDim.x >> 5);
     const long long w0 = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int halfw = bn / 2;
     unsigned long long ncand = 0, novf = 0;
     for (long long e = w0; e < nf; e += wstride) {
         const RefineEntry E = list[e];
         const float* p = P + (size_t)E.row * d;
+        float pr[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int t = lane + 32 * i;
+            pr[i] = t < d ? p[t] : 0.f;
+        }
         float bv = INFINITY;
         int bj = k;
-        if (E.ovf) {
-            for (int j = 0; j < k; ++j) {
-                const float dot = dot_warp(p, C + (size_t)j * d, d, lane);
-                const float v = fmaf(-2.f, dot, cn[j]);
-                if (v < bv || (v == bv && j < bj)) { bv = v; bj = j; }
+        int batch[4] = {-1, -1, -1, -1};
+        int nb = 0;
+        auto push = [&](int j) {
+            batch[nb++] = j;
+            if (nb == 4) {
+                eval4(pr, C, cn, d, lane, batch, bv, bj);
+                batch[0] = batch[1] = batch[2] = batch[3] = -1;
+                nb = 0;
             }
-            ncand += (unsigned long long)k;
+        };
+#pragma unroll 1
+        for (int q = 0; q < 16; ++q)
+            if (E.c[q] >= 0) { push(E.c[q]); ++ncand; }
+        if (E.ovf[0] | E.ovf[1]) {
             ++novf;
-        } else {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int j = E.c[q];
-                if (j < 0) continue;
-                const float dot = dot_warp(p, C + (size_t)j * d, d, lane);
-                const float v = fmaf(-2.f, dot, cn[j]);
-                if (v < bv || (v == bv && j < bj)) { bv = v; bj = j; }
-                ++ncand;
-            }
+#pragma unroll 1
+            for (int h = 0; h < 2; ++h)
+#pragma unroll 1
+                for (int c = 0; c < 8; ++c) {
+                    if (!((E.ovf[h] >> c) & 1)) continue;
+#pragma unroll 1
+                    for (int base = h * halfw + c; base < k; base += bn)
+#pragma unroll 1
+                        for (int m = 0; m < halfw; m += 8) {
+                            const int j = base + m;
+                            if (j >= k) break;
+                            push(j);
+                            ++ncand;
+                        }
+                }
         }
-        if (lane == 0) labels[E.row] = bj;   /* lane 0 holds the reduced dot */
+        if (nb) eval4(pr, C, cn, d, lane, batch, bv, bj);
+        if (lane == 0) labels[E.row] = bj;   /* lane 0 holds the reduced dots */
     }
     if (lane == 0 && ncand) {
         atomicAdd(&prm->ncand_total, ncand);
@@ -187,84 +227,6 @@ __global__ void k_refine(const float* __restrict__ P, const float* __restrict__ 
         atomicAdd(&prm->nflag_total, (unsigned long long)nf);
         if (hist_slot) *hist_slot = (unsigned long long)nf;
     }
-}
-
-/* ------------------------------------------------------------- update ---- */
-
-/* Segmented fixed-point sum of the points per label.
- *
- * Each CTA owns a slice of F coordinates and a contiguous run of rows, and
- * keeps a private k x F table of int64 sums (plus k counts for slice 0) in
- * shared memory.  Every coordinate is quantised once, q = rint(x * 2^frac),
- * so the sums are exact integers: order independent, identical on every run
- * and on any number of GPUs, and within 2^-frac per point of the reference's
- * FP64 accumulation (kmeans/src/kernels.cu:690-703).  The private tables are
- * then added into the global int64 sums, one atomic per non-zero entry. */
-template <int F>
-__global__ void k_accum_fixed(const float* __restrict__ P, long long n, int d, const int* __restrict__ labels,
-                              int k, DevParams* __restrict__ prm, long long* __restrict__ sums,
-                              long long* __restrict__ counts, long long rows_per_cta) {
-    extern __shared__ __align__(16) unsigned char sm_raw[];
-    unsigned long long* acc = reinterpret_cast<unsigned long long*>(sm_raw);
-    unsigned int* cnt = reinterpret_cast<unsigned int*>(acc + (size_t)k * F);
-    const int slice = blockIdx.y;
-    const int f0 = slice * F;
-    const bool do_count = (slice == 0);
-    for (int e = threadIdx.x; e < k * F; e += blockDim.x) acc[e] = 0ull;
-    if (do_count) for (int e = threadIdx.x; e < k; e += blockDim.x) cnt[e] = 0u;
-    __syncthreads();
-
-    constexpr int RPW = 32 / F;                       /* rows per warp step */
-    const int lane = threadIdx.x & 31;
-    const int rs = lane / F, f = lane % F;
-    const int col = f0 + f;
-    const bool colok = col < d;
-    const double sc = ldexp(1.0, prm->frac);
-    const int nwarps = blockDim.x >> 5;
-    const long long r0 = (long long)blockIdx.x * rows_per_cta;
-    long long r1 = r0 + rows_per_cta;
-    if (r1 > n) r1 = n;
-    const long long step = (long long)nwarps * RPW;
-    bool badlab = false;
-
-    constexpr int U = 8;
-    long long i = r0 + (long long)(threadIdx.x >> 5) * RPW + rs;
-    for (; i + (U - 1) * step < r1; i += U * step) {
-        int a[U];
-        float x[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const long long ii = i + u * step;
-            a[u] = labels[ii];
-            x[u] = colok ? P[(size_t)ii * d + col] : 0.f;
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            if ((unsigned)a[u] >= (unsigned)k) { badlab = true; continue; }
-            const long long qv = __double2ll_rn((double)x[u] * sc);
-            if (qv) atomicAdd(&acc[(size_t)a[u] * F + f], (unsigned long long)qv);
-            if (do_count && f == 0) atomicAdd(&cnt[a[u]], 1u);
-        }
-    }
-    for (; i < r1; i += step) {
-        const int a = labels[i];
-        if ((unsigned)a >= (unsigned)k) { badlab = true; continue; }
-        const float x = colok ? P[(size_t)i * d + col] : 0.f;
-        const long long qv = __double2ll_rn((double)x * sc);
-        if (qv) atomicAdd(&acc[(size_t)a * F + f], (unsigned long long)qv);
-        if (do_count && f == 0) atomicAdd(&cnt[a], 1u);
-    }
-    if (badlab) atomicOr(&prm->status, MPK_DEV_LABEL_RANGE);
-    __syncthreads();
-    for (int e = threadIdx.x; e < k * F; e += blockDim.x) {
-        const unsigned long long v = acc[e];
-        const int c = f0 + (e % F);
-        if (v && c < d)
-            atomicAdd(reinterpret_cast<unsigned long long*>(&sums[(size_t)(e / F) * d + c]), v);
-    }
-    if (do_count)
-        for (int e = threadIdx.x; e < k; e += blockDim.x)
-            if (cnt[e]) atomicAdd(reinterpret_cast<unsigned long long*>(&counts[e]), (unsigned long long)cnt[e]);
 }
 
 /* C_j = (float)((S_j * 2^-frac) / count_j); an empty cluster keeps its old
@@ -383,48 +345,10 @@ void launch_prep_c(const float* C, int k, int kpad, int d, int dp, DevParams* pr
     k_prep_c<<<kpad, 256, 0, s>>>(C, k, d, dp, prm, planes, (long long)k * dp, cn);
 }
 
-void launch_refine(const float* P, const float* C, const float* cn, int d, int k, const RefineEntry* list,
+void launch_refine(const float* P, const float* C, const float* cn, int d, int k, int bn, const RefineEntry* list,
                    DevParams* prm, int* labels, long long n_cap, unsigned long long* hist_slot, int num_sms,
                    cudaStream_t s) {
-    k_refine<<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, list, prm, labels, n_cap, hist_slot);
-}
-
-/* Slice width F: the widest power of two (<= 32) whose k x F int64 table plus
- * k counts fits in ~96 KB, so two or more CTAs share an SM. */
-static int accum_f_for(int k) {
-    int F = 32;
-    while (F > 1 && (size_t)k * F * 8 + (size_t)k * 4 > 96 * 1024) F >>= 1;
-    return F;
-}
-
-template <int F>
-static void launch_accum_f(const float* P, long long n, int d, const int* labels, int k, DevParams* prm,
-                           long long* sums, long long* counts, int num_sms, cudaStream_t s) {
-    const int slices = (d + F - 1) / F;
-    const size_t smem = (size_t)k * F * 8 + (size_t)k * 4;
-    static_assert(F >= 1 && F <= 32, "slice width");
-    cudaFuncSetAttribute(k_accum_fixed<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    /* about three resident CTAs per SM in total, split over the slices */
-    long long chunks = (3LL * num_sms + slices - 1) / slices;
-    if (chunks < 1) chunks = 1;
-    long long rows = (n + chunks - 1) / chunks;
-    if (rows < 1) rows = 1;
-    chunks = (n + rows - 1) / rows;
-    dim3 grid((unsigned)chunks, (unsigned)slices);
-    k_accum_fixed<F><<<grid, 512, smem, s>>>(P, n, d, labels, k, prm, sums, counts, rows);
-}
-
-void launch_accum_fixed(const float* P, long long n, int d, const int* labels, int k, DevParams* prm,
-                        long long* sums, long long* counts, int num_sms, cudaStream_t s) {
-    if (n <= 0) return;
-    switch (accum_f_for(k)) {
-        case 32: launch_accum_f<32>(P, n, d, labels, k, prm, sums, counts, num_sms, s); break;
-        case 16: launch_accum_f<16>(P, n, d, labels, k, prm, sums, counts, num_sms, s); break;
-        case 8: launch_accum_f<8>(P, n, d, labels, k, prm, sums, counts, num_sms, s); break;
-        case 4: launch_accum_f<4>(P, n, d, labels, k, prm, sums, counts, num_sms, s); break;
-        case 2: launch_accum_f<2>(P, n, d, labels, k, prm, sums, counts, num_sms, s); break;
-        default: launch_accum_f<1>(P, n, d, labels, k, prm, sums, counts, num_sms, s); break;
-    }
+    k_refine<<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, bn, list, prm, labels, n_cap, hist_slot);
 }
 
 void launch_finalize_fixed(const long long* sums, const long long* counts, int k, int d, const DevParams* prm,

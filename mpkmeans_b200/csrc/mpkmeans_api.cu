@@ -116,13 +116,33 @@ struct mpkEngine_s {
     DevParams* prm = nullptr;
     double* dInertia = nullptr;
     unsigned long long* hist = nullptr;   /* MPK_MAX_HIST slots */
+    UpdateScratch us{nullptr, nullptr, nullptr, nullptr};
     CUtensorMap tmX, tmC;
     BoundConsts bc;
-    float4* dbg = nullptr;                /* test hook, set by mpkDebugAssignTop */
+    float4* dbg = nullptr;                /* test hook, set by mpkDebugSetAssignTrace */
+    bool prof = false;                    /* bench hook: events around the hot kernels */
+    std::vector<cudaEvent_t> ev_assign, ev_accum;
 };
+
+static void prof_mark(mpkEngine e, std::vector<cudaEvent_t>& v) {
+    if (!e->prof) return;
+    cudaEvent_t ev = nullptr;
+    if (cudaEventCreate(&ev) == cudaSuccess) {
+        cudaEventRecord(ev, e->s);
+        v.push_back(ev);
+    }
+}
+
+static void prof_clear(mpkEngine e) {
+    for (auto x : e->ev_assign) cudaEventDestroy(x);
+    for (auto x : e->ev_accum) cudaEventDestroy(x);
+    e->ev_assign.clear();
+    e->ev_accum.clear();
+}
 
 static void engine_free(mpkEngine e) {
     if (!e) return;
+    prof_clear(e);
     cudaFree(e->Xs);
     cudaFree(e->xnorm);
     cudaFree(e->Cs);
@@ -131,6 +151,10 @@ static void engine_free(mpkEngine e) {
     cudaFree(e->prm);
     cudaFree(e->dInertia);
     cudaFree(e->hist);
+    cudaFree(e->us.perm);
+    cudaFree(e->us.bin_start);
+    cudaFree(e->us.cursor);
+    cudaFree(e->us.hist);
     delete e;
 }
 
@@ -176,6 +200,10 @@ static mpkStatus engine_create(mpkEngine* out, const float* dP, long long n, int
     ALLOC(e->prm, sizeof(DevParams));
     ALLOC(e->dInertia, sizeof(double));
     ALLOC(e->hist, sizeof(unsigned long long) * MPK_MAX_HIST);
+    ALLOC(e->us.perm, sizeof(int) * (size_t)(n > 0 ? n : 1));
+    ALLOC(e->us.bin_start, sizeof(int) * ((size_t)k + 1));
+    ALLOC(e->us.cursor, sizeof(int) * (size_t)k);
+    ALLOC(e->us.hist, sizeof(int) * (size_t)k);
     if (need_assign) {
         ALLOC(e->Xs, (size_t)2 * (n > 0 ? n : 1) * e->dp * sizeof(__half));
         ALLOC(e->xnorm, (size_t)(n > 0 ? n : 1) * sizeof(float));
@@ -256,13 +284,15 @@ static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int r
     a.bc = e->bc;
     a.num_sms = e->num_sms;
     a.dbg = e->dbg;
+    prof_mark(e, e->ev_assign);
     cudaError_t err = launch_assign(a, e->s);
+    prof_mark(e, e->ev_assign);
     if (err != cudaSuccess) {
         fprintf(stderr, "mpkmeans_b200: assignment launch failed: %s\n", cudaGetErrorString(err));
         return MPK_ERR_CUDA;
     }
     if (refine)
-        launch_refine(e->P, dC, e->cn, e->d, e->k, e->list, e->prm, dAssign, e->n,
+        launch_refine(e->P, dC, e->cn, e->d, e->k, assign_bn_for(e->k), e->list, e->prm, dAssign, e->n,
                       (hist_it >= 0 && hist_it < MPK_MAX_HIST) ? e->hist + hist_it : nullptr, e->num_sms, e->s);
     return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
 }
@@ -270,8 +300,10 @@ static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int r
 static mpkStatus engine_accumulate(mpkEngine e, const int* dAssign, long long* dSums) {
     const long long len = (long long)e->k * e->d + e->k;
     cudaMemsetAsync(dSums, 0, (size_t)len * sizeof(long long), e->s);
-    launch_accum_fixed(e->P, e->n, e->d, dAssign, e->k, e->prm, dSums, dSums + (long long)e->k * e->d,
-                       e->num_sms, e->s);
+    prof_mark(e, e->ev_accum);
+    launch_update_sorted(e->P, e->n, e->d, dAssign, e->k, e->prm, dSums, dSums + (long long)e->k * e->d, e->us,
+                         e->num_sms, e->s);
+    prof_mark(e, e->ev_accum);
     return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
 }
 
@@ -347,6 +379,41 @@ long long mpkEngineSumsLength(mpkEngine e) { return e ? (long long)e->k * e->d +
 mpkStatus mpkDebugSetAssignTrace(mpkEngine e, float* dOut4) {
     if (!e) return MPK_ERR_INVALID;
     e->dbg = reinterpret_cast<float4*>(dOut4);
+    return MPK_OK;
+}
+
+/* Bench hook: while enabled, the engine records a CUDA event pair on its
+ * stream around every assignment kernel and every accumulation kernel. */
+mpkStatus mpkDebugProfile(mpkEngine e, int enable) {
+    if (!e) return MPK_ERR_INVALID;
+    cudaStreamSynchronize(e->s);
+    prof_clear(e);
+    e->prof = enable != 0;
+    return MPK_OK;
+}
+
+/* Synchronises, returns the summed device time and launch counts of the two
+ * kernels since mpkDebugProfile(e, 1), and clears the record. */
+mpkStatus mpkDebugProfileRead(mpkEngine e, double* assign_ms, long long* assign_launches, double* accum_ms,
+                              long long* accum_launches) {
+    if (!e) return MPK_ERR_INVALID;
+    MPK_TRY(cudaStreamSynchronize(e->s));
+    double a = 0.0, u = 0.0;
+    for (size_t i = 0; i + 1 < e->ev_assign.size(); i += 2) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, e->ev_assign[i], e->ev_assign[i + 1]);
+        a += ms;
+    }
+    for (size_t i = 0; i + 1 < e->ev_accum.size(); i += 2) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, e->ev_accum[i], e->ev_accum[i + 1]);
+        u += ms;
+    }
+    if (assign_ms) *assign_ms = a;
+    if (assign_launches) *assign_launches = (long long)(e->ev_assign.size() / 2);
+    if (accum_ms) *accum_ms = u;
+    if (accum_launches) *accum_launches = (long long)(e->ev_accum.size() / 2);
+    prof_clear(e);
     return MPK_OK;
 }
 

@@ -231,7 +231,7 @@ def fixed_frac(pmax: float, n_total: int) -> int:
     lg = 0
     while (1 << lg) < n_total and lg < 62:
         lg += 1
-    return min(62 - E - lg, 200)
+    return min(62 - E - lg, 100)
 
 
 def mpk_epsilon(d, accum_fp16=0):
