@@ -205,6 +205,23 @@ mpkStatus mpkMeansMixedMG(int ngpu, const int* devices, const float* const* dPsh
                           int d, int k, float* const* dC, int* const* dAssign,
                           const mpkParams* params, mpkStats* stats);
 
+/* The centroid update of mpkUpdate for callers that cannot allocate device
+ * memory (a device owned by a pool or custom allocator, an allocator that may
+ * not be re-entered from a library, a fixed device footprint).  It calls no
+ * cudaMalloc, cudaFree or allocating library routine: its scratch is one
+ * fixed 32 MiB array in the library's device image, held by every GPU that
+ * loads the library until exit.  Sizes are limited by that array:
+ *   256 + 8*(k*d + k) + 3*4*(k + 1) + 4*n bytes (each part rounded up to
+ *   256) must not exceed 32 MiB -- e.g. n up to about 8.1 million rows at
+ *   d = 128, k = 1024; larger sizes return MPK_ERR_INVALID (use mpkUpdate).
+ * The first call on each device looks up the array's device address (make it
+ * before any stream capture).  The array is shared by every call and keeps
+ * the last call's contents (cleared where needed at each call): calls that
+ * overlap on the GPU race.  Synchronises `stream` to report invalid labels.
+ * Same result as mpkUpdate, bit for bit.  No counterpart in the reference. */
+mpkStatus mpkUpdateNoAlloc(cudaStream_t stream, const float* dP, int n, int d, int k,
+                           const int* dAssign, float* dC, float* dMoved2);
+
 /* ----------------------------------------------- new: engine handle --- */
 
 /* A fit in explicit steps, for callers that drive the iteration themselves

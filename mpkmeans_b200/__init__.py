@@ -95,6 +95,7 @@ SIGNATURES = {
     "mpkAssign": (_I, [_P, _P, _I, _I, _I, _P, _P, _PARAMS, _STATS]),
     "mpkUpdate": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
     "mpkMeansMixedMG": (_I, [_I, _P, _P, _P, _I, _I, _P, _P, _PARAMS, _STATS]),
+    "mpkUpdateNoAlloc": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
     "mpkEngineCreate": (_I, [ctypes.POINTER(_P), _P, _LL, _I, _I, _P, _F, _LL, _P]),
     "mpkEngineDestroy": (_I, [_P]),
     "mpkEngineAssign": (_I, [_P, _P, _P, _I]),
