@@ -238,10 +238,14 @@ def run_e2e(M, P, C0, world, rank, dev, n_total, steps=2):
     hC = torch.empty(C0.shape, dtype=torch.float32, pin_memory=True)
     stream = torch.cuda.current_stream(dev).cuda_stream
 
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+
     def one():
+        marks[0].record()
         dP = hP.to(dev, non_blocking=True)
         dC = hC0.to(dev, non_blocking=True)
         lab = torch.empty(P.shape[0], dtype=torch.int32, device=dev)
+        marks[1].record()
         if world == 1:
             M.means_mixed(dP, dC, lab, M.params_init(max_iter=E2E_ITERS), blas=torch.cuda.current_blas_handle())
         else:
@@ -254,8 +258,10 @@ def run_e2e(M, P, C0, world, rank, dev, n_total, steps=2):
                     e.accumulate(lab, s)
                     dist.all_reduce(s)
                     e.finalize(s, dC)
+        marks[2].record()
         hL.copy_(lab, non_blocking=True)
         hC.copy_(dC, non_blocking=True)
+        marks[3].record()
 
     one()
     torch.cuda.synchronize()
@@ -271,7 +277,9 @@ def run_e2e(M, P, C0, world, rank, dev, n_total, steps=2):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     t = float(t.item())
-    return {"value": E2E_ITERS * steps / (t / 1e3), "unit": UNIT,
+    brk = {"h2d_ms": marks[0].elapsed_time(marks[1]), "fit_ms": marks[1].elapsed_time(marks[2]),
+           "d2h_ms": marks[2].elapsed_time(marks[3])}
+    return {"value": E2E_ITERS * steps / (t / 1e3), "unit": UNIT, "last_step_ms": brk,
             "h2d_bytes_per_step": int(P.numel() * 4 + C0.numel() * 4),
             "d2h_bytes_per_step": int(P.shape[0] * 4 + C0.numel() * 4),
             "iters_per_step": E2E_ITERS, "api": "mpkMeansMixed" if world == 1 else "mpkEngine* + NCCL allreduce"}

@@ -1,7 +1,7 @@
 /* common.cuh -- shared device helpers for the B200 (sm_100a) k-means engine.
  *
  * Inline PTX for the Blackwell pieces the kernels use: mbarriers with bounded
- * waits, TMA tile loads (no cluster multicast anywhere), tcgen05 TMEM
+ * waits, TMA tile loads (each CTA loads its own tiles), tcgen05 TMEM
  * allocation, MMA issue/commit and TMEM loads.  Every wait is bounded by the
  * global timer: a wait that runs out records an error code in the engine's
  * device status word and makes the kernel wind down instead of spinning.
@@ -95,7 +95,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 }
 
 /* 3D tiled load, coordinates innermost first; completes on `bar` with
- * complete_tx.  No multicast. */
+ * complete_tx into this CTA's shared memory only. */
 __device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint64_t* bar, void* smem,
                                             int x, int y, int z) {
     asm volatile(

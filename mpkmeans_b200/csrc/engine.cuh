@@ -100,6 +100,13 @@ void launch_count_diff(const int* a, const int* b, long long n, unsigned long lo
 void launch_add_const(float* p, long long count, float c, cudaStream_t s);
 void launch_standardize(float* P, int n, int d, cudaStream_t s);
 
+/* ---- device memory (mpkmeans_api.cu) ----
+ * Engine scratch comes from one stream-ordered memory pool per device whose
+ * release threshold keeps freed blocks cached, so a second fit of the same
+ * size allocates nothing new from the driver. */
+cudaError_t dev_alloc(void** p, size_t bytes, cudaStream_t s);
+void dev_free(void* p, cudaStream_t s);
+
 /* ---- tensor maps (engine host code) ---- */
 bool make_tmap_planes(CUtensorMap* map, const __half* base, long long rows, int dp, int box_rows);
 

@@ -106,7 +106,7 @@ extern "C" mpkStatus mpkMeansMixedMG(int ngpu, const int* devices, const float* 
     std::vector<long long*> sums(ngpu, nullptr);
     std::vector<float*> moved(ngpu, nullptr);
     std::vector<ncclComm_t> comm(ngpu, nullptr);
-    float* h_moved = nullptr;
+    std::vector<float> h_moved((size_t)k);
     cudaEvent_t e0 = nullptr, e1 = nullptr;
     mpkStatus rc = MPK_OK;
     const long long len = (long long)k * d + k;
@@ -124,8 +124,11 @@ extern "C" mpkStatus mpkMeansMixedMG(int ngpu, const int* devices, const float* 
         cudaSetDevice(devices[g]);
         rc = mpkEngineCreate(&eng[g], dPshard[g], nshard[g], d, k, nullptr, pmax > 0.f ? pmax : 1.f, n_total, st[g]);
         if (rc != MPK_OK) goto done;
-        if (cudaMalloc(&sums[g], (size_t)len * sizeof(long long)) != cudaSuccess ||
-            cudaMalloc(&moved[g], (size_t)k * sizeof(float)) != cudaSuccess) { rc = MPK_ERR_ALLOC; goto done; }
+        if (mpk::dev_alloc((void**)&sums[g], (size_t)len * sizeof(long long), st[g]) != cudaSuccess ||
+            mpk::dev_alloc((void**)&moved[g], (size_t)k * sizeof(float), st[g]) != cudaSuccess) {
+            rc = MPK_ERR_ALLOC;
+            goto done;
+        }
     }
     {
         const ncclResult_t r = N.commInitAll(comm.data(), ngpu, devices);
@@ -135,7 +138,6 @@ extern "C" mpkStatus mpkMeansMixedMG(int ngpu, const int* devices, const float* 
             goto done;
         }
     }
-    if (cudaMallocHost(&h_moved, (size_t)k * sizeof(float)) != cudaSuccess) { rc = MPK_ERR_ALLOC; goto done; }
     cudaSetDevice(devices[0]);
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
@@ -165,7 +167,7 @@ extern "C" mpkStatus mpkMeansMixedMG(int ngpu, const int* devices, const float* 
         S->tested += n_total * (k - 1);
         if (P.tol > 0.f || P.verbose) {
             cudaSetDevice(devices[0]);
-            cudaMemcpyAsync(h_moved, moved[0], (size_t)k * sizeof(float), cudaMemcpyDeviceToHost, st[0]);
+            cudaMemcpyAsync(h_moved.data(), moved[0], (size_t)k * sizeof(float), cudaMemcpyDeviceToHost, st[0]);
             if (cudaStreamSynchronize(st[0]) != cudaSuccess) { rc = MPK_ERR_CUDA; goto done; }
             double fro2 = 0.0;
             for (int j = 0; j < k; ++j) fro2 += (double)h_moved[j];
@@ -203,14 +205,16 @@ done:
         if (st[g]) cudaStreamSynchronize(st[g]);
         if (comm[g]) N.commDestroy(comm[g]);
         if (eng[g]) mpkEngineDestroy(eng[g]);
-        cudaFree(sums[g]);
-        cudaFree(moved[g]);
-        if (st[g]) cudaStreamDestroy(st[g]);
+        mpk::dev_free(sums[g], st[g]);
+        mpk::dev_free(moved[g], st[g]);
+        if (st[g]) {
+            cudaStreamSynchronize(st[g]);
+            cudaStreamDestroy(st[g]);
+        }
     }
     cudaSetDevice(devices[0]);
     if (e0) cudaEventDestroy(e0);
     if (e1) cudaEventDestroy(e1);
-    cudaFreeHost(h_moved);
     cudaSetDevice(prev_dev);
     return rc;
 }

@@ -99,6 +99,45 @@ int current_sm_count(int* dev_out, int* cc_major) {
 
 }  /* namespace */
 
+/* ------------------------------------------------------ memory pool ---- */
+
+namespace mpk {
+
+static cudaMemPool_t engine_pool(int dev) {
+    static std::mutex m;
+    static cudaMemPool_t pools[64] = {};
+    if (dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(m);
+    if (!pools[dev]) {
+        cudaMemPoolProps props = {};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.handleTypes = cudaMemHandleTypeNone;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        cudaMemPool_t pool = nullptr;
+        if (cudaMemPoolCreate(&pool, &props) != cudaSuccess) return nullptr;
+        unsigned long long keep = ~0ull;   /* never return freed blocks to the driver early */
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+        pools[dev] = pool;
+    }
+    return pools[dev];
+}
+
+cudaError_t dev_alloc(void** p, size_t bytes, cudaStream_t s) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    cudaMemPool_t pool = engine_pool(dev);
+    if (!pool) return cudaErrorMemoryAllocation;
+    return cudaMallocFromPoolAsync(p, bytes, pool, s);
+}
+
+void dev_free(void* p, cudaStream_t s) {
+    if (p) cudaFreeAsync(p, s);
+}
+
+}  /* namespace mpk */
+
 /* ------------------------------------------------------------ engine ---- */
 
 struct mpkEngine_s {
@@ -143,18 +182,9 @@ static void prof_clear(mpkEngine e) {
 static void engine_free(mpkEngine e) {
     if (!e) return;
     prof_clear(e);
-    cudaFree(e->Xs);
-    cudaFree(e->xnorm);
-    cudaFree(e->Cs);
-    cudaFree(e->cn);
-    cudaFree(e->list);
-    cudaFree(e->prm);
-    cudaFree(e->dInertia);
-    cudaFree(e->hist);
-    cudaFree(e->us.perm);
-    cudaFree(e->us.bin_start);
-    cudaFree(e->us.cursor);
-    cudaFree(e->us.hist);
+    void* bufs[] = {e->Xs, e->xnorm, e->Cs, e->cn, e->list, e->prm, e->dInertia, e->hist,
+                    e->us.perm, e->us.bin_start, e->us.cursor, e->us.hist};
+    for (void* b : bufs) dev_free(b, e->s);
     delete e;
 }
 
@@ -192,8 +222,8 @@ static mpkStatus engine_create(mpkEngine* out, const float* dP, long long n, int
     const long long ng = n_global > 0 ? n_global : (n > 0 ? n : 1);
 
 #define ALLOC(ptr, bytes)                                                      \
-    if (cudaMalloc((void**)&(ptr), (size_t)(bytes)) != cudaSuccess) {          \
-        fprintf(stderr, "mpkmeans_b200: cudaMalloc of %lld bytes failed\n", (long long)(bytes)); \
+    if (dev_alloc((void**)&(ptr), (size_t)(bytes), s) != cudaSuccess) {        \
+        fprintf(stderr, "mpkmeans_b200: allocation of %lld bytes failed\n", (long long)(bytes)); \
         engine_free(e);                                                        \
         return MPK_ERR_ALLOC;                                                  \
     }
@@ -522,13 +552,12 @@ static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k
     cudaEventRecord(ev_x, s);
     long long* sums = nullptr;
     float* moved2 = nullptr;
-    float* h_moved = nullptr;
+    std::vector<float> h_moved((size_t)k);
     const int iters_cap = P.max_iter > 0 ? P.max_iter : 0;
     std::vector<cudaEvent_t> ev((size_t)iters_cap * 4, nullptr);
     int it = 0;
-    if (cudaMalloc(&sums, ((size_t)k * d + k) * sizeof(long long)) != cudaSuccess ||
-        cudaMalloc(&moved2, (size_t)k * sizeof(float)) != cudaSuccess ||
-        cudaMallocHost(&h_moved, (size_t)k * sizeof(float)) != cudaSuccess) {
+    if (dev_alloc((void**)&sums, ((size_t)k * d + k) * sizeof(long long), s) != cudaSuccess ||
+        dev_alloc((void**)&moved2, (size_t)k * sizeof(float), s) != cudaSuccess) {
         st = MPK_ERR_ALLOC;
         goto done;
     }
@@ -544,7 +573,7 @@ static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k
         S->hp_baseline += (long long)n * k;
         S->tested += (long long)n * (k - 1);
         if (P.tol > 0.f || P.verbose) {
-            cudaMemcpyAsync(h_moved, moved2, (size_t)k * sizeof(float), cudaMemcpyDeviceToHost, s);
+            cudaMemcpyAsync(h_moved.data(), moved2, (size_t)k * sizeof(float), cudaMemcpyDeviceToHost, s);
             if (cudaStreamSynchronize(s) != cudaSuccess) { st = MPK_ERR_CUDA; goto done; }
             double fro2 = 0.0;
             for (int j = 0; j < k; ++j) fro2 += (double)h_moved[j];
@@ -588,10 +617,10 @@ done:
     cudaEventDestroy(ev_all0);
     cudaEventDestroy(ev_all1);
     cudaEventDestroy(ev_x);
-    cudaFree(sums);
-    cudaFree(moved2);
-    cudaFreeHost(h_moved);
+    dev_free(sums, s);
+    dev_free(moved2, s);
     engine_free(e);
+    cudaStreamSynchronize(s);
     return st;
 }
 
@@ -666,7 +695,7 @@ mpkStatus mpkUpdate(cublasHandle_t blas, const float* dP, int n, int d, int k, c
     mpkStatus st = engine_create(&e, dP, n, d, k, nullptr, 0.f, n, s, false);
     if (st != MPK_OK) return st;
     long long* sums = nullptr;
-    if (cudaMalloc(&sums, ((size_t)k * d + k) * sizeof(long long)) != cudaSuccess) {
+    if (dev_alloc((void**)&sums, ((size_t)k * d + k) * sizeof(long long), s) != cudaSuccess) {
         engine_free(e);
         return MPK_ERR_ALLOC;
     }
@@ -677,9 +706,9 @@ mpkStatus mpkUpdate(cublasHandle_t blas, const float* dP, int n, int d, int k, c
         fprintf(stderr, "mpkmeans_b200: mpkUpdate: device status 0x%x\n", status);
         st = MPK_ERR_INVALID;
     }
-    cudaStreamSynchronize(s);
-    cudaFree(sums);
+    dev_free(sums, s);
     engine_free(e);
+    cudaStreamSynchronize(s);
     return st;
 }
 

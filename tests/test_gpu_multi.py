@@ -1,0 +1,40 @@
+"""Multi-GPU entry point: mpkMeansMixedMG over two B200s equals the one-GPU
+mpkMeansMixed bit for bit (exact int64 sums, one global operand scale)."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+torch = pytest.importorskip("torch")
+import mpkmeans_b200 as M  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def test_mg_two_gpus_equals_one(cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    P = O.make_gmm(200_000, 64, 128, 9, 5.0, 0.5, 2.0, True)
+    C0 = P[np.sort(O.init_random_idx(200_000, 128, 9))].copy()
+    lab1 = torch.empty(200_000, dtype=torch.int32, device="cuda:0")
+    dC1 = torch.from_numpy(C0).to("cuda:0")
+    M.means_mixed(torch.from_numpy(P).to("cuda:0"), dC1, lab1, M.params_init(max_iter=6))
+    halves = [(0, 123_457), (123_457, 200_000)]
+    dPs = [torch.from_numpy(P[a:b]).to(f"cuda:{g}") for g, (a, b) in enumerate(halves)]
+    dCs = [torch.from_numpy(C0).to(f"cuda:{g}") for g in range(2)]
+    dAs = [torch.empty(b - a, dtype=torch.int32, device=f"cuda:{g}") for g, (a, b) in enumerate(halves)]
+    arr = lambda t, xs: (t * 2)(*xs)
+    st = M.mpkStats()
+    p = M.params_init(max_iter=6)
+    rc = M.lib().mpkMeansMixedMG(2, arr(ctypes.c_int, [0, 1]), arr(ctypes.c_void_p, [x.data_ptr() for x in dPs]),
+                                 arr(ctypes.c_int, [b - a for a, b in halves]), 64, 128,
+                                 arr(ctypes.c_void_p, [x.data_ptr() for x in dCs]),
+                                 arr(ctypes.c_void_p, [x.data_ptr() for x in dAs]), ctypes.byref(p), ctypes.byref(st))
+    assert rc == M.MPK_OK
+    assert st.iters == 6
+    labs = torch.cat([dAs[0].cpu(), dAs[1].cpu()])
+    assert torch.equal(labs, lab1.cpu())
+    for g in range(2):
+        assert torch.equal(dCs[g].cpu(), dC1.cpu())
