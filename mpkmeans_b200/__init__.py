@@ -107,6 +107,36 @@ SIGNATURES = {
                                ctypes.POINTER(_I)]),
     "mpkEngineSumsLength": (_LL, [_P]),
     "mpkDebugSetAssignTrace": (_I, [_P, _P]),
+    # include/mpemu.h
+    "mpemuStatusString": (ctypes.c_char_p, [_I]),
+    "mpemuSplitLd": (ctypes.c_int64, [ctypes.c_int64]),
+    "mpemuSplitStride": (ctypes.c_int64, [ctypes.c_int64, ctypes.c_int64]),
+    "mpemuSplitBytes": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int64, _I]),
+    "mpemuSplitBF16": (_I, [_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _I, _P, ctypes.c_int64,
+                            ctypes.c_int64, _P]),
+    "mpemuGemmBF16": (_I, [_P, _I, _I, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _F, _P, ctypes.c_int64, _P,
+                           ctypes.c_int64, _F, _P, ctypes.c_int64]),
+    "mpemuTermCount": (_I, [_I]),
+    "mpemuTermSchedule": (_I, [_I, _I, _P]),
+    "mpemuGemmEmulatedRange": (_I, [_P, _I, _I, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _F, _P,
+                                    ctypes.c_int64, ctypes.c_int64, _P, ctypes.c_int64, ctypes.c_int64, _I, _I, _I,
+                                    _F, _P, ctypes.c_int64]),
+    "mpemuGemmEmulated": (_I, [_P, _I, _I, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _F, _P, ctypes.c_int64,
+                               ctypes.c_int64, _P, ctypes.c_int64, ctypes.c_int64, _I, _I, _F, _P, ctypes.c_int64]),
+    "mpemuMultiwordMacs": (_I, [_I]),
+    "mpemuSplitFP16": (_I, [_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _I, _F, _P, ctypes.c_int64,
+                            ctypes.c_int64, _P]),
+    "mpemuAutoScaleFP16": (_I, [_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.POINTER(_F), _P]),
+    "mpemuCheckSplitFP16": (_I, [_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _I, _F, _P, ctypes.c_int64,
+                                 ctypes.c_int64, _P, _P]),
+    "mpemuGemmFP16": (_I, [_P, _I, _I, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _F, _P, ctypes.c_int64, _P,
+                           ctypes.c_int64, _F, _P, ctypes.c_int64]),
+    "mpemuGemmMultiwordRange": (_I, [_P, _I, _I, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _F, _P,
+                                     ctypes.c_int64, ctypes.c_int64, _F, _P, ctypes.c_int64, ctypes.c_int64, _F, _I,
+                                     _I, _I, _F, _P, ctypes.c_int64]),
+    "mpemuGemmMultiword": (_I, [_P, _I, _I, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _F, _P, ctypes.c_int64,
+                                ctypes.c_int64, _F, _P, ctypes.c_int64, ctypes.c_int64, _F, _I, _I, _F, _P,
+                                ctypes.c_int64]),
     "mpkDebugEngineInfo": (_I, [_P, ctypes.POINTER(_F), ctypes.POINTER(_F), ctypes.POINTER(_I),
                                 ctypes.POINTER(_F), ctypes.POINTER(_F)]),
     "mpkDebugProfile": (_I, [_P, _I]),

@@ -1,0 +1,441 @@
+/* mpemu_api.cu -- the split-precision GEMM C ABI (include/mpemu.h).
+ *
+ * Splits, AutoScale and the split check are bandwidth-bound SIMT kernels; the
+ * GEMM drivers validate exactly as the reference does (gemm.cu:62-103,
+ * gemm_fp16.cu:32-78, split.cu:124-147, split_fp16.cu:205-289), build TMA
+ * descriptors over the packed split planes and launch the tcgen05 kernel of
+ * gemm_tc.cu once per call.  Layouts TMA cannot address (a leading dimension
+ * or plane stride that is not a multiple of 8 elements, a misaligned base)
+ * take a plain SIMT kernel with the same term order.
+ */
+#include "engine.cuh"
+#include "gemm_tc.cuh"
+#include "mpemu.h"
+
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdio>
+#include <mutex>
+
+using namespace mpk;
+
+namespace {
+
+constexpr int kBlock = 256;
+
+/* ------------------------------------------------------------- splits ---- */
+
+template <typename W>
+__device__ __forceinline__ W to_word(float a);
+template <>
+__device__ __forceinline__ __nv_bfloat16 to_word<__nv_bfloat16>(float a) { return __float2bfloat16_rn(a); }
+template <>
+__device__ __forceinline__ __half to_word<__half>(float a) { return __float2half_rn(a); }
+__device__ __forceinline__ float from_word(__nv_bfloat16 w) { return __bfloat162float(w); }
+__device__ __forceinline__ float from_word(__half w) { return __half2float(w); }
+
+/* Every element of a column-major rows x cols matrix: a = scale * A(r, c);
+ * word s = round(a), a -= word (exact), for s = 0..nsplits-1. */
+template <typename W>
+__global__ void k_split(const float* __restrict__ A, long long lda, long long rows, long long cols, int nsplits,
+                        float scale, W* __restrict__ S, long long lds, long long stride) {
+    const long long total = rows * cols;
+    const long long step = (long long)gridDim.x * blockDim.x;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += step) {
+        const long long c = e / rows, r = e - c * rows;
+        float a = A[c * lda + r] * scale;
+        W* dst = S + c * lds + r;
+        for (int s = 0; s < nsplits; ++s) {
+            const W w = to_word<W>(a);
+            dst[(long long)s * stride] = w;
+            a = a - from_word(w);
+        }
+    }
+}
+
+__global__ void k_maxabs_finite(const float* __restrict__ A, long long lda, long long rows, long long cols,
+                                float* out) {
+    float m = 0.f;
+    const long long total = rows * cols;
+    const long long step = (long long)gridDim.x * blockDim.x;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += step) {
+        const long long c = e / rows, r = e - c * rows;
+        const float v = fabsf(A[c * lda + r]);
+        if (v > m && isfinite(v)) m = v;
+    }
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0 && m > 0.f) atomicMax(reinterpret_cast<unsigned int*>(out), __float_as_uint(m));
+}
+
+/* Classifies each FP16 word: [0] not finite, [1] zero while the residual was
+ * not, or subnormal, [2] clean. */
+__global__ void k_check_split(const float* __restrict__ A, long long lda, long long rows, long long cols,
+                              int nsplits, float scale, const __half* __restrict__ S, long long lds, long long stride,
+                              unsigned long long* counts) {
+    unsigned long long over = 0, sub = 0, ok = 0;
+    const long long total = rows * cols;
+    const long long step = (long long)gridDim.x * blockDim.x;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += step) {
+        const long long c = e / rows, r = e - c * rows;
+        float res = A[c * lda + r] * scale;
+        for (int s = 0; s < nsplits; ++s) {
+            const float w = __half2float(S[(long long)s * stride + c * lds + r]);
+            const float aw = fabsf(w);
+            if (!isfinite(w)) ++over;
+            else if ((aw == 0.f && res != 0.f) || (aw > 0.f && aw < 6.103515625e-05f)) ++sub;
+            else ++ok;
+            res -= w;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        over += __shfl_xor_sync(0xffffffffu, over, o);
+        sub += __shfl_xor_sync(0xffffffffu, sub, o);
+        ok += __shfl_xor_sync(0xffffffffu, ok, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+        if (over) atomicAdd(&counts[0], over);
+        if (sub) atomicAdd(&counts[1], sub);
+        if (ok) atomicAdd(&counts[2], ok);
+    }
+}
+
+/* C := beta * C (an empty term range, or k = 0; BLAS semantics). */
+__global__ void k_scale_c(float* C, long long ldc, int m, int n, float beta) {
+    const long long total = (long long)m * n;
+    const long long step = (long long)gridDim.x * blockDim.x;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += step) {
+        const long long c = e / m, r = e - c * m;
+        float* p = C + c * ldc + r;
+        *p = beta == 0.f ? 0.f : beta * *p;
+    }
+}
+
+/* Fallback for layouts TMA cannot take: one thread per output, the same
+ * term-major, K-ascending FP32 accumulation. */
+template <typename W>
+__global__ void k_gemm_simt(bool ta, bool tb, int m, int n, int k, const W* __restrict__ A, long long lda,
+                            long long sa, const W* __restrict__ B, long long ldb, long long sb, GemmTerms terms,
+                            float alpha, float beta, int init_mode, float* C, long long ldc) {
+    const long long total = (long long)m * n;
+    const long long step = (long long)gridDim.x * blockDim.x;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += step) {
+        const int j = (int)(e / m), i = (int)(e - (long long)j * m);
+        float* dst = C + (long long)j * ldc + i;
+        float acc = (init_mode && beta != 0.f) ? beta * *dst / alpha : 0.f;
+        for (int t = 0; t < terms.n; ++t) {
+            const W* a = A + terms.ia[t] * sa;
+            const W* b = B + terms.ib[t] * sb;
+            for (int kk = 0; kk < k; ++kk) {
+                const float av = from_word(ta ? a[(long long)i * lda + kk] : a[(long long)kk * lda + i]);
+                const float bv = from_word(tb ? b[(long long)kk * ldb + j] : b[(long long)j * ldb + kk]);
+                acc = fmaf(av, bv, acc);
+            }
+        }
+        if (init_mode) *dst = acc * alpha;
+        else *dst = beta != 0.f ? fmaf(alpha, acc, beta * *dst) : alpha * acc;
+    }
+}
+
+int grid_for(long long items) {
+    long long b = (items + kBlock - 1) / kBlock;
+    if (b < 1) b = 1;
+    return (int)(b > 148 * 16 ? 148 * 16 : b);
+}
+
+cudaStream_t stream_of(cublasHandle_t h) {
+    cudaStream_t s = nullptr;
+    if (h) cublasGetStream(h, &s);
+    return s;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+/* 3D map over nplanes column-major planes: (contiguous dim, other dim, plane). */
+bool plane_map(CUtensorMap* map, const void* base, bool bf16, long long inner, long long outer, long long ld,
+               long long pstride, int nplanes, int box_inner, int box_outer) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)nplanes};
+    cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)pstride * 2};
+    cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    return fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+              const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+/* One device int per GPU for the kernel's status word (bounded waits). */
+int* gemm_status(int* sms) {
+    static std::mutex m;
+    static int* st[64] = {};
+    static int nsm[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(m);
+    if (!st[dev]) {
+        if (cudaMalloc(&st[dev], sizeof(int)) != cudaSuccess) return nullptr;
+        cudaMemset(st[dev], 0, sizeof(int));
+        cudaDeviceGetAttribute(&nsm[dev], cudaDevAttrMultiProcessorCount, dev);
+    }
+    *sms = nsm[dev];
+    return st[dev];
+}
+
+bool power_of_two(float a) {
+    if (!(a > 0.f) || !std::isfinite(a)) return false;
+    int e = 0;
+    return std::frexp(a, &e) == 0.5f;
+}
+
+/* Shared driver: dC := alpha * sum over schedule positions [b, e) + beta * dC.
+ * Checks follow the reference's order and results: bad split count or range
+ * -> INVALID_VALUE; an empty range with beta == 1 succeeds untouched; a
+ * missing handle -> INVALID_VALUE (gemm.cu:7-18); a leading dimension cuBLAS
+ * would reject -> CUBLAS_ERROR. */
+mpemuStatus_t gemm_range(cublasHandle_t handle, cublasOperation_t opA, cublasOperation_t opB, int64_t m, int64_t n,
+                         int64_t k, float alpha, const void* dSA, int64_t lda, int64_t strideA, const void* dSB,
+                         int64_t ldb, int64_t strideB, int nsplits, int b, int e, float beta, float* dC,
+                         int64_t ldc, bool bf16) {
+    if (nsplits < 1 || nsplits > MPEMU_MAX_SPLITS) return MPEMU_STATUS_INVALID_VALUE;
+    const int total = nsplits * nsplits;
+    if (e == MPEMU_ALL_MACS) e = total;
+    if (b < 0 || e > total || b > e) return MPEMU_STATUS_INVALID_VALUE;
+    if (b == e && beta == 1.0f) return MPEMU_STATUS_SUCCESS;
+    if (!handle || !dC) return MPEMU_STATUS_INVALID_VALUE;
+    if (m < 0 || n < 0 || k < 0) return MPEMU_STATUS_INVALID_VALUE;
+    if (b < e && k > 0 && (!dSA || !dSB)) return MPEMU_STATUS_INVALID_VALUE;
+    if (m == 0 || n == 0) return MPEMU_STATUS_SUCCESS;
+    if (ldc < m) return MPEMU_STATUS_CUBLAS_ERROR;
+    if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return MPEMU_STATUS_INVALID_VALUE;
+    const cudaStream_t s = stream_of(handle);
+    if (b == e || k == 0) {
+        if (beta == 1.0f) return MPEMU_STATUS_SUCCESS;
+        k_scale_c<<<grid_for(m * n), kBlock, 0, s>>>(dC, ldc, (int)m, (int)n, beta);
+        return cudaGetLastError() == cudaSuccess ? MPEMU_STATUS_SUCCESS : MPEMU_STATUS_CUDA_ERROR;
+    }
+    mpemuTerm_t sched[MPEMU_MAX_SPLITS * MPEMU_MAX_SPLITS];
+    mpemuTermSchedule(nsplits, e, sched);
+    GemmTerms terms;
+    terms.n = e - b;
+    for (int t = b; t < e; ++t) {
+        terms.ia[t - b] = sched[t].i;
+        terms.ib[t - b] = sched[t].j;
+    }
+    const bool ta = (opA != CUBLAS_OP_N), tb = (opB != CUBLAS_OP_N);
+    /* stored shapes: A is m x k (op N) or k x m (op T); B is k x n (op N) or n x k (op T) */
+    const int64_t a_rows = ta ? k : m, b_rows = tb ? n : k;
+    if (lda < a_rows || ldb < b_rows) return MPEMU_STATUS_CUBLAS_ERROR;
+    const int init_mode = (power_of_two(alpha) && (beta == 0.f || beta == 1.f)) ? 1 : 0;
+    const bool tma_ok = ((reinterpret_cast<uintptr_t>(dSA) | reinterpret_cast<uintptr_t>(dSB)) % 16 == 0) &&
+                        lda % 8 == 0 && ldb % 8 == 0 && strideA % 8 == 0 && strideB % 8 == 0 &&
+                        (nsplits == 1 || (strideA > 0 && strideB > 0));
+    int sms = 0;
+    int* status = gemm_status(&sms);
+    if (!status) return MPEMU_STATUS_CUDA_ERROR;
+    if (!tma_ok) {
+        if (bf16)
+            k_gemm_simt<__nv_bfloat16><<<grid_for(m * n), kBlock, 0, s>>>(
+                ta, tb, (int)m, (int)n, (int)k, (const __nv_bfloat16*)dSA, lda, strideA, (const __nv_bfloat16*)dSB,
+                ldb, strideB, terms, alpha, beta, init_mode, dC, ldc);
+        else
+            k_gemm_simt<__half><<<grid_for(m * n), kBlock, 0, s>>>(ta, tb, (int)m, (int)n, (int)k,
+                                                                   (const __half*)dSA, lda, strideA,
+                                                                   (const __half*)dSB, ldb, strideB, terms, alpha,
+                                                                   beta, init_mode, dC, ldc);
+        return cudaGetLastError() == cudaSuccess ? MPEMU_STATUS_SUCCESS : MPEMU_STATUS_CUDA_ERROR;
+    }
+    CUtensorMap tmA, tmB;
+    const int planes = nsplits;
+    const bool a_mn = !ta, b_mn = tb;
+    const bool okA = a_mn ? plane_map(&tmA, dSA, bf16, m, k, lda, strideA > 0 ? strideA : lda * k, planes, 64, 64)
+                          : plane_map(&tmA, dSA, bf16, k, m, lda, strideA > 0 ? strideA : lda * m, planes, 64, 128);
+    const bool okB = b_mn ? plane_map(&tmB, dSB, bf16, n, k, ldb, strideB > 0 ? strideB : ldb * k, planes, 64, 64)
+                          : plane_map(&tmB, dSB, bf16, k, n, ldb, strideB > 0 ? strideB : ldb * n, planes, 64,
+                                      mpk::gemm_tile_n(beta, init_mode));
+    if (!okA || !okB) {
+        fprintf(stderr, "mpemu: tensor map encoding failed\n");
+        return MPEMU_STATUS_CUDA_ERROR;
+    }
+    GemmArgs g;
+    g.tmA = &tmA;
+    g.tmB = &tmB;
+    g.m = (int)m;
+    g.n = (int)n;
+    g.k = (int)k;
+    g.a_mn = a_mn;
+    g.b_mn = b_mn;
+    g.bf16 = bf16;
+    g.terms = terms;
+    g.alpha = alpha;
+    g.beta = beta;
+    g.init_mode = init_mode;
+    g.C = dC;
+    g.ldc = ldc;
+    g.status = status;
+    g.num_sms = sms;
+    return launch_gemm_tc(g, s) == cudaSuccess ? MPEMU_STATUS_SUCCESS : MPEMU_STATUS_CUDA_ERROR;
+}
+
+template <typename W>
+mpemuStatus_t split_impl(const float* dA, int64_t lda, int64_t rows, int64_t cols, int nsplits, float scale,
+                         W* dS, int64_t lds, int64_t stride, cudaStream_t s) {
+    if (!dA || !dS) return MPEMU_STATUS_INVALID_VALUE;
+    if (rows < 0 || cols < 0) return MPEMU_STATUS_INVALID_VALUE;
+    if (nsplits < 1 || nsplits > MPEMU_MAX_SPLITS) return MPEMU_STATUS_INVALID_VALUE;
+    if (lda < rows || lds < rows) return MPEMU_STATUS_INVALID_VALUE;
+    if (stride < lds * cols) return MPEMU_STATUS_INVALID_VALUE;
+    if (rows == 0 || cols == 0) return MPEMU_STATUS_SUCCESS;
+    k_split<W><<<grid_for(rows * cols), kBlock, 0, s>>>(dA, lda, rows, cols, nsplits, scale, dS, lds, stride);
+    return cudaGetLastError() == cudaSuccess ? MPEMU_STATUS_SUCCESS : MPEMU_STATUS_CUDA_ERROR;
+}
+
+}  /* namespace */
+
+extern "C" {
+
+const char* mpemuStatusString(mpemuStatus_t s) {
+    switch (s) {
+        case MPEMU_STATUS_SUCCESS: return "MPEMU_STATUS_SUCCESS";
+        case MPEMU_STATUS_INVALID_VALUE: return "MPEMU_STATUS_INVALID_VALUE";
+        case MPEMU_STATUS_CUDA_ERROR: return "MPEMU_STATUS_CUDA_ERROR";
+        case MPEMU_STATUS_CUBLAS_ERROR: return "MPEMU_STATUS_CUBLAS_ERROR";
+        default: return "MPEMU_STATUS_UNKNOWN";
+    }
+}
+
+int64_t mpemuSplitLd(int64_t rows) { return (rows + 7) / 8 * 8; }
+int64_t mpemuSplitStride(int64_t lds, int64_t cols) { return lds * cols; }
+size_t mpemuSplitBytes(int64_t rows, int64_t cols, int nsplits) {
+    if (nsplits < 1 || nsplits > MPEMU_MAX_SPLITS) return 0;
+    return (size_t)mpemuSplitStride(mpemuSplitLd(rows), cols) * (size_t)nsplits * 2;
+}
+
+int mpemuTermCount(int nsplits) {
+    return (nsplits < 1 || nsplits > MPEMU_MAX_TERM_SPLITS) ? 0 : nsplits * nsplits;
+}
+
+int mpemuTermSchedule(int nsplits, int maxTerms, mpemuTerm_t* terms) {
+    if (nsplits < 1 || nsplits > MPEMU_MAX_TERM_SPLITS || maxTerms <= 0 || !terms) return 0;
+    int w = 0;
+    for (int bin = 0; bin <= 2 * (nsplits - 1) && w < maxTerms; ++bin)
+        for (int i = 0; i <= bin && w < maxTerms; ++i) {
+            const int j = bin - i;
+            if (i < nsplits && j < nsplits) terms[w++] = mpemuTerm_t{i, j};
+        }
+    return w;
+}
+
+int mpemuMultiwordMacs(int p) { return (p < 1 || p > MPEMU_MAX_SPLITS) ? 0 : p * (p + 1) / 2; }
+
+mpemuStatus_t mpemuSplitBF16(const float* dA, int64_t lda, int64_t rows, int64_t cols, int nsplits,
+                             __nv_bfloat16* dS, int64_t lds, int64_t splitStride, cudaStream_t stream) {
+    return split_impl<__nv_bfloat16>(dA, lda, rows, cols, nsplits, 1.0f, dS, lds, splitStride, stream);
+}
+
+mpemuStatus_t mpemuSplitFP16(const float* dA, int64_t lda, int64_t rows, int64_t cols, int nsplits, float scale,
+                             __half* dS, int64_t lds, int64_t splitStride, cudaStream_t stream) {
+    if (!(scale > 0.0f)) return MPEMU_STATUS_INVALID_VALUE;
+    return split_impl<__half>(dA, lda, rows, cols, nsplits, scale, dS, lds, splitStride, stream);
+}
+
+mpemuStatus_t mpemuAutoScaleFP16(const float* dA, int64_t lda, int64_t rows, int64_t cols, float* hScale,
+                                 cudaStream_t stream) {
+    if (!dA || !hScale) return MPEMU_STATUS_INVALID_VALUE;
+    *hScale = 1.0f;
+    if (rows <= 0 || cols <= 0) return MPEMU_STATUS_SUCCESS;
+    static std::mutex m;
+    static float* scratch[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return MPEMU_STATUS_CUDA_ERROR;
+    std::lock_guard<std::mutex> lock(m);   /* one scratch word per device: serialise */
+    if (!scratch[dev] && cudaMalloc(&scratch[dev], sizeof(float)) != cudaSuccess) return MPEMU_STATUS_CUDA_ERROR;
+    if (cudaMemsetAsync(scratch[dev], 0, sizeof(float), stream) != cudaSuccess) return MPEMU_STATUS_CUDA_ERROR;
+    k_maxabs_finite<<<grid_for(rows * cols), kBlock, 0, stream>>>(dA, lda, rows, cols, scratch[dev]);
+    float hmax = 0.f;
+    cudaMemcpyAsync(&hmax, scratch[dev], sizeof(float), cudaMemcpyDeviceToHost, stream);
+    if (cudaStreamSynchronize(stream) != cudaSuccess) return MPEMU_STATUS_CUDA_ERROR;
+    if (!(hmax > 0.f)) return MPEMU_STATUS_SUCCESS;
+    int e = 0;
+    std::frexp(4096.0f / hmax, &e);
+    const float sc = std::ldexp(1.0f, e - 1);
+    *hScale = (sc > 0.f && std::isfinite(sc)) ? sc : 1.0f;
+    return MPEMU_STATUS_SUCCESS;
+}
+
+mpemuStatus_t mpemuCheckSplitFP16(const float* dA, int64_t lda, int64_t rows, int64_t cols, int nsplits,
+                                  float scale, const __half* dS, int64_t lds, int64_t splitStride,
+                                  unsigned long long* dCounts, cudaStream_t stream) {
+    if (!dA || !dS || !dCounts) return MPEMU_STATUS_INVALID_VALUE;
+    if (nsplits < 1 || nsplits > MPEMU_MAX_SPLITS) return MPEMU_STATUS_INVALID_VALUE;
+    if (rows <= 0 || cols <= 0) return MPEMU_STATUS_SUCCESS;
+    k_check_split<<<grid_for(rows * cols), kBlock, 0, stream>>>(dA, lda, rows, cols, nsplits, scale, dS, lds,
+                                                                 splitStride, dCounts);
+    return cudaGetLastError() == cudaSuccess ? MPEMU_STATUS_SUCCESS : MPEMU_STATUS_CUDA_ERROR;
+}
+
+mpemuStatus_t mpemuGemmBF16(cublasHandle_t handle, cublasOperation_t opA, cublasOperation_t opB, int64_t m,
+                            int64_t n, int64_t k, float alpha, const __nv_bfloat16* dAi, int64_t lda,
+                            const __nv_bfloat16* dBj, int64_t ldb, float beta, float* dC, int64_t ldc) {
+    return gemm_range(handle, opA, opB, m, n, k, alpha, dAi, lda, 0, dBj, ldb, 0, 1, 0, 1, beta, dC, ldc, true);
+}
+
+mpemuStatus_t mpemuGemmFP16(cublasHandle_t handle, cublasOperation_t opA, cublasOperation_t opB, int64_t m,
+                            int64_t n, int64_t k, float alpha, const __half* dAi, int64_t lda, const __half* dBj,
+                            int64_t ldb, float beta, float* dC, int64_t ldc) {
+    return gemm_range(handle, opA, opB, m, n, k, alpha, dAi, lda, 0, dBj, ldb, 0, 1, 0, 1, beta, dC, ldc, false);
+}
+
+mpemuStatus_t mpemuGemmEmulatedRange(cublasHandle_t handle, cublasOperation_t opA, cublasOperation_t opB,
+                                     int64_t m, int64_t n, int64_t k, float alpha, const __nv_bfloat16* dSA,
+                                     int64_t lda, int64_t strideA, const __nv_bfloat16* dSB, int64_t ldb,
+                                     int64_t strideB, int nsplits, int macBegin, int macEnd, float beta, float* dC,
+                                     int64_t ldc) {
+    return gemm_range(handle, opA, opB, m, n, k, alpha, dSA, lda, strideA, dSB, ldb, strideB, nsplits, macBegin,
+                      macEnd, beta, dC, ldc, true);
+}
+
+mpemuStatus_t mpemuGemmEmulated(cublasHandle_t handle, cublasOperation_t opA, cublasOperation_t opB, int64_t m,
+                                int64_t n, int64_t k, float alpha, const __nv_bfloat16* dSA, int64_t lda,
+                                int64_t strideA, const __nv_bfloat16* dSB, int64_t ldb, int64_t strideB,
+                                int nsplits, int nmacs, float beta, float* dC, int64_t ldc) {
+    return mpemuGemmEmulatedRange(handle, opA, opB, m, n, k, alpha, dSA, lda, strideA, dSB, ldb, strideB, nsplits, 0,
+                                  nmacs, beta, dC, ldc);
+}
+
+mpemuStatus_t mpemuGemmMultiwordRange(cublasHandle_t handle, cublasOperation_t opA, cublasOperation_t opB,
+                                      int64_t m, int64_t n, int64_t k, float alpha, const __half* dSA, int64_t lda,
+                                      int64_t strideA, float scaleA, const __half* dSB, int64_t ldb,
+                                      int64_t strideB, float scaleB, int nsplits, int macBegin, int macEnd,
+                                      float beta, float* dC, int64_t ldc) {
+    if (!(scaleA > 0.0f) || !(scaleB > 0.0f)) return MPEMU_STATUS_INVALID_VALUE;
+    /* the words carry scaleA * scaleB; powers of two in normal use, so exact */
+    const float a = alpha / (scaleA * scaleB);
+    return gemm_range(handle, opA, opB, m, n, k, a, dSA, lda, strideA, dSB, ldb, strideB, nsplits, macBegin, macEnd,
+                      beta, dC, ldc, false);
+}
+
+mpemuStatus_t mpemuGemmMultiword(cublasHandle_t handle, cublasOperation_t opA, cublasOperation_t opB, int64_t m,
+                                 int64_t n, int64_t k, float alpha, const __half* dSA, int64_t lda, int64_t strideA,
+                                 float scaleA, const __half* dSB, int64_t ldb, int64_t strideB, float scaleB,
+                                 int nsplits, int nmacs, float beta, float* dC, int64_t ldc) {
+    return mpemuGemmMultiwordRange(handle, opA, opB, m, n, k, alpha, dSA, lda, strideA, scaleA, dSB, ldb, strideB,
+                                   scaleB, nsplits, 0, nmacs, beta, dC, ldc);
+}
+
+}  /* extern "C" */

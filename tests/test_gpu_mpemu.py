@@ -1,0 +1,316 @@
+"""The split-precision GEMM ABI (include/mpemu.h) on a B200, through the C ABI.
+
+Pins: splits bit-exact against the oracle and against the reference's own
+split outputs (tests/golden/ref_mpemu.npz); AutoScale and the term schedule
+exactly; GEMMs within the error model of the exact FP64 sum of the split
+words' products and close to the reference's cuBLAS results; bitwise
+resumability of ranges (gemm-emulation/bench/test_refine.cu); accuracy
+against FP64 within twice that of native FP32 SGEMM.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import golden
+
+torch = pytest.importorskip("torch")
+import mpkmeans_b200 as M  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+OK = 0
+
+
+def lib():
+    return M.lib()
+
+
+def handle():
+    return torch.cuda.current_blas_handle()
+
+
+def split_gpu(A_cm, rows, cols, lda, nsplits, bf16=True, scale=1.0):
+    """A_cm: column-major storage as a (cols, lda) float32 array."""
+    lds = int(lib().mpemuSplitLd(rows))
+    stride = lds * cols
+    dA = torch.from_numpy(np.ascontiguousarray(A_cm, np.float32)).cuda()
+    dS = torch.zeros(stride * nsplits, dtype=torch.int16, device="cuda")
+    if bf16:
+        rc = lib().mpemuSplitBF16(dA.data_ptr(), lda, rows, cols, nsplits, dS.data_ptr(), lds, stride, None)
+    else:
+        rc = lib().mpemuSplitFP16(dA.data_ptr(), lda, rows, cols, nsplits, scale, dS.data_ptr(), lds, stride, None)
+    assert rc == OK
+    torch.cuda.synchronize()
+    return dS, lds, stride
+
+
+def autoscale_gpu(A_cm, rows, cols, lda):
+    dA = torch.from_numpy(np.ascontiguousarray(A_cm, np.float32)).cuda()
+    sc = ctypes.c_float()
+    assert lib().mpemuAutoScaleFP16(dA.data_ptr(), lda, rows, cols, ctypes.byref(sc), None) == OK
+    return sc.value
+
+
+def words_f64(S_u16, nsplits, lds, stride, rows, cols, bf16, scale=1.0):
+    planes = []
+    for s in range(nsplits):
+        w = S_u16[s * stride:(s + 1) * stride]
+        f = O.bf16_to_f32(w) if bf16 else O.fp16_to_f32(w)
+        planes.append(f.reshape(cols, lds)[:, :rows].astype(np.float64) / scale)
+    return planes                      # each (cols, rows): column-major storage
+
+
+def exact_emulated(opa, opb, m, n, k, Ap, Bp, terms):
+    """Exact FP64 sum over terms of op(A_i) op(B_j); planes are (cols, rows) column-major arrays."""
+    D = np.zeros((m, n))
+    for (i, j) in terms:
+        A = Ap[i].T if True else None          # stored rows x cols
+        B = Bp[j].T
+        opA = A if opa == 0 else A.T           # m x k
+        opB = B if opb == 0 else B.T           # k x n
+        D += opA @ opB
+    return D
+
+
+def gemm_bf16(opa, opb, m, n, k, dSA, lda, sa, dSB, ldb, sb, nsplits, b, e, dC, alpha=1.0, beta=0.0):
+    return lib().mpemuGemmEmulatedRange(handle(), opa, opb, m, n, k, alpha, dSA.data_ptr(), lda, sa, dSB.data_ptr(),
+                                        ldb, sb, nsplits, b, e, beta, dC.data_ptr(), m)
+
+
+def gemm_fp16(opa, opb, m, n, k, dSA, lda, sa, scA, dSB, ldb, sb, scB, nsplits, b, e, dC, alpha=1.0, beta=0.0):
+    return lib().mpemuGemmMultiwordRange(handle(), opa, opb, m, n, k, alpha, dSA.data_ptr(), lda, sa, scA,
+                                         dSB.data_ptr(), ldb, sb, scB, nsplits, b, e, beta, dC.data_ptr(), m)
+
+
+# ------------------------------------------------------------------ splits --
+
+@pytest.mark.parametrize("rows,cols,lda,emax", [(1024, 64, 1024, 0), (1023, 77, 1023, 0), (100, 33, 101, 0),
+                                                 (1, 1, 1, 0), (7, 3, 9, 0), (512, 64, 512, 8)])
+def test_splits_bit_exact_vs_oracle(cuda, rows, cols, lda, emax):
+    A = O.make_uniform((cols, lda), 7 + rows, emax=emax)
+    for ns in (1, 2, 3, 4):
+        dS, lds, stride = split_gpu(A, rows, cols, lda, ns, bf16=True)
+        want, _, _ = O.split_bf16(A, rows, cols, lda, ns)
+        assert np.array_equal(dS.cpu().numpy().view(np.uint16), want)
+    sc = autoscale_gpu(A, rows, cols, lda)
+    assert sc == O.autoscale_fp16(A, rows, cols, lda)
+    for ns in (1, 2, 3):
+        dS, lds, stride = split_gpu(A, rows, cols, lda, ns, bf16=False, scale=sc)
+        want, _, _ = O.split_fp16(A, rows, cols, lda, ns, sc)
+        assert np.array_equal(dS.cpu().numpy().view(np.uint16), want)
+
+
+def test_splits_equal_reference_outputs(cuda):
+    g = golden("ref_mpemu.npz")
+    rows, cols, lda = (int(x) for x in g["shape"])
+    A = g["A"]
+    for ns in (1, 2, 3, 4):
+        dS, _, _ = split_gpu(A, rows, cols, lda, ns, bf16=True)
+        assert np.array_equal(dS.cpu().numpy().view(np.uint16), g[f"bf16_split_{ns}"])
+    sc = autoscale_gpu(A, rows, cols, lda)
+    assert np.float32(sc) == g["fp16_scale"]
+    for ns in (1, 2, 3):
+        dS, _, _ = split_gpu(A, rows, cols, lda, ns, bf16=False, scale=sc)
+        assert np.array_equal(dS.cpu().numpy().view(np.uint16), g[f"fp16_split_{ns}"])
+
+
+def test_schedule_and_macs(cuda):
+    t = (ctypes.c_int * 32)()
+    nt = lib().mpemuTermSchedule(3, 16, t)
+    got = [(t[2 * i], t[2 * i + 1]) for i in range(nt)]
+    assert got == [(0, 0), (0, 1), (1, 0), (0, 2), (1, 1), (2, 0), (1, 2), (2, 1), (2, 2)]
+    assert [lib().mpemuTermSchedule(3, c, t) for c in (1, 3, 6, 9)] == [1, 3, 6, 9]
+    assert [lib().mpemuMultiwordMacs(p) for p in range(5)] == [0, 1, 3, 6, 10]
+    assert lib().mpemuTermCount(16) == 256 and lib().mpemuTermCount(17) == 0
+    assert lib().mpemuSplitLd(13) == 16 and lib().mpemuSplitBytes(13, 5, 3) == 16 * 5 * 3 * 2
+
+
+def test_check_split_counts(cuda):
+    A = O.make_uniform((64, 64), 5) * np.float32(0.5)
+    sc = autoscale_gpu(A, 64, 64, 64)
+    dA = torch.from_numpy(A).cuda()
+    for scale in (1.0, sc):
+        dS, lds, stride = split_gpu(A, 64, 64, 64, 2, bf16=False, scale=scale)
+        cnt = torch.zeros(3, dtype=torch.int64, device="cuda")
+        assert lib().mpemuCheckSplitFP16(dA.data_ptr(), 64, 64, 64, 2, scale, dS.data_ptr(), lds, stride,
+                                         cnt.data_ptr(), None) == OK
+        c = cnt.cpu().numpy()
+        assert c.sum() == 2 * 64 * 64 and c[0] == 0
+        if scale != 1.0:
+            assert c[1] < c[2]
+
+
+# ------------------------------------------------------------------- GEMM ---
+
+def _operands(opa, opb, m, n, k, seed, emax=0):
+    ra, ca = (m, k) if opa == 0 else (k, m)
+    rb, cb = (k, n) if opb == 0 else (n, k)
+    A = O.make_uniform((ca, ra), seed, emax=emax)
+    B = O.make_uniform((cb, rb), seed + 1, emax=emax)
+    return A, (ra, ca), B, (rb, cb)
+
+
+@pytest.mark.parametrize("m,n,k", [(96, 72, 80), (300, 200, 150), (128, 256, 64), (1, 1, 1), (513, 257, 129)])
+@pytest.mark.parametrize("opa,opb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_gemm_error_model(cuda, m, n, k, opa, opb):
+    A, (ra, ca), B, (rb, cb) = _operands(opa, opb, m, n, k, 31 + m + 2 * opa + opb)
+    dSA, la, sa = split_gpu(A, ra, ca, ra, 3, bf16=True)
+    dSB, lb, sb = split_gpu(B, rb, cb, rb, 3, bf16=True)
+    Ap = words_f64(dSA.cpu().numpy().view(np.uint16), 3, la, sa, ra, ca, True)
+    Bp = words_f64(dSB.cpu().numpy().view(np.uint16), 3, lb, sb, rb, cb, True)
+    absA = np.abs(A[:, :ra].T.astype(np.float64))
+    absB = np.abs(B[:, :rb].T.astype(np.float64))
+    absAB = (absA if opa == 0 else absA.T) @ (absB if opb == 0 else absB.T)
+    sched = O.term_schedule(3, 9)
+    for macs in (1, 3, 6, 9):
+        dC = torch.zeros(n * m, dtype=torch.float32, device="cuda")
+        assert gemm_bf16(opa, opb, m, n, k, dSA, la, sa, dSB, lb, sb, 3, 0, macs, dC) == OK
+        torch.cuda.synchronize()
+        got = dC.cpu().numpy().reshape(n, m).T.astype(np.float64)
+        D = exact_emulated(opa, opb, m, n, k, Ap, Bp, sched[:macs])
+        bound = (macs * ((k + 15) // 16) + 16) * 2.0 ** -22 * absAB + 1e-30
+        assert np.all(np.abs(got - D) <= bound), (macs, float(np.max(np.abs(got - D) / bound)))
+
+
+def test_gemm_close_to_reference_outputs(cuda):
+    g = golden("ref_mpemu.npz")
+    m, n, k = (int(x) for x in g["gemm_shape"])
+    for opa in (0, 1):
+        for opb in (0, 1):
+            A, B = g[f"gemm_A_{opa}{opb}"], g[f"gemm_B_{opa}{opb}"]
+            ra, ca = (m, k) if opa == 0 else (k, m)
+            rb, cb = (k, n) if opb == 0 else (n, k)
+            dSA, la, sa = split_gpu(A, ra, ca, ra, 3, True)
+            dSB, lb, sb = split_gpu(B, rb, cb, rb, 3, True)
+            D = O.gemm_f64(opa, opb, m, n, k, A, ra, B, rb)                    # exact product, (n, m)
+            absAB = O.gemm_f64(opa, opb, m, n, k, np.abs(A), ra, np.abs(B), rb)
+            for macs, tol in ((1, 2 ** -7), (3, 2 ** -14), (6, 2 ** -19), (9, 2 ** -19)):
+                dC = torch.zeros(n * m, dtype=torch.float32, device="cuda")
+                assert gemm_bf16(opa, opb, m, n, k, dSA, la, sa, dSB, lb, sb, 3, 0, macs, dC) == OK
+                torch.cuda.synchronize()
+                got = dC.cpu().numpy().reshape(n, m)
+                ref = g[f"gemm_bf16_{opa}{opb}_{macs}"].reshape(n, m)
+                assert np.all(np.abs(got - ref) <= 2 * tol * absAB + 1e-30)
+                assert np.all(np.abs(got - D) <= tol * absAB + 1e-30)
+            sA = autoscale_gpu(A, ra, ca, ra)
+            sB = autoscale_gpu(B, rb, cb, rb)
+            dSA, la, sa = split_gpu(A, ra, ca, ra, 2, False, sA)
+            dSB, lb, sb = split_gpu(B, rb, cb, rb, 2, False, sB)
+            for macs, tol in ((1, 2 ** -9), (3, 2 ** -19)):
+                dC = torch.zeros(n * m, dtype=torch.float32, device="cuda")
+                assert gemm_fp16(opa, opb, m, n, k, dSA, la, sa, sA, dSB, lb, sb, sB, 2, 0, macs, dC) == OK
+                torch.cuda.synchronize()
+                got = dC.cpu().numpy().reshape(n, m)
+                ref = g[f"gemm_fp16_{opa}{opb}_{macs}"].reshape(n, m)
+                assert np.all(np.abs(got - ref) <= 2 * tol * absAB + 1e-30)
+
+
+def test_ranges_resume_bitwise(cuda):
+    # gemm-emulation/bench/test_refine.cu: [0,e) == [0,c) + [c,e) for every cut
+    N = 256
+    A = O.make_uniform((N, N), 11)
+    B = O.make_uniform((N, N), 22)
+    dSA, l, s = split_gpu(A, N, N, N, 3, True)
+    dSB, _, _ = split_gpu(B, N, N, N, 3, True)
+    whole = torch.zeros(N * N, dtype=torch.float32, device="cuda")
+    assert gemm_bf16(0, 0, N, N, N, dSA, l, s, dSB, l, s, 3, 0, 9, whole) == OK
+    for cut in range(1, 9):
+        part = torch.zeros(N * N, dtype=torch.float32, device="cuda")
+        assert gemm_bf16(0, 0, N, N, N, dSA, l, s, dSB, l, s, 3, 0, cut, part) == OK
+        assert gemm_bf16(0, 0, N, N, N, dSA, l, s, dSB, l, s, 3, cut, 9, part, beta=1.0) == OK
+        torch.cuda.synchronize()
+        assert torch.equal(part, whole), cut
+    # MPEMU_ALL_MACS, the whole-budget driver, and an empty range with beta = 1
+    part = torch.zeros(N * N, dtype=torch.float32, device="cuda")
+    assert gemm_bf16(0, 0, N, N, N, dSA, l, s, dSB, l, s, 3, 0, 4, part) == OK
+    assert gemm_bf16(0, 0, N, N, N, dSA, l, s, dSB, l, s, 3, 4, -1, part, beta=1.0) == OK
+    torch.cuda.synchronize()
+    assert torch.equal(part, whole)
+    six = torch.zeros(N * N, dtype=torch.float32, device="cuda")
+    assert lib().mpemuGemmEmulated(handle(), 0, 0, N, N, N, 1.0, dSA.data_ptr(), l, s, dSB.data_ptr(), l, s, 3, 6,
+                                   0.0, six.data_ptr(), N) == OK
+    six_r = torch.zeros(N * N, dtype=torch.float32, device="cuda")
+    assert gemm_bf16(0, 0, N, N, N, dSA, l, s, dSB, l, s, 3, 0, 6, six_r) == OK
+    keep = six_r.clone()
+    assert gemm_bf16(0, 0, N, N, N, dSA, l, s, dSB, l, s, 3, 6, 6, six_r, beta=1.0) == OK
+    torch.cuda.synchronize()
+    assert torch.equal(six, six_r) and torch.equal(six_r, keep)
+    # FP16 multiword, autoscaled operands
+    sA, sB = autoscale_gpu(A, N, N, N), autoscale_gpu(B, N, N, N)
+    dHA, _, _ = split_gpu(A, N, N, N, 3, False, sA)
+    dHB, _, _ = split_gpu(B, N, N, N, 3, False, sB)
+    whole = torch.zeros(N * N, dtype=torch.float32, device="cuda")
+    assert gemm_fp16(0, 0, N, N, N, dHA, l, s, sA, dHB, l, s, sB, 3, 0, 6, whole) == OK
+    for cut in range(1, 6):
+        part = torch.zeros(N * N, dtype=torch.float32, device="cuda")
+        assert gemm_fp16(0, 0, N, N, N, dHA, l, s, sA, dHB, l, s, sB, 3, 0, cut, part) == OK
+        assert gemm_fp16(0, 0, N, N, N, dHA, l, s, sA, dHB, l, s, sB, 3, cut, 6, part, beta=1.0) == OK
+        torch.cuda.synchronize()
+        assert torch.equal(part, whole), cut
+
+
+def test_unaligned_layout_fallback(cuda):
+    m, n, k = 77, 45, 33
+    A = O.make_uniform((k, m + 1), 3)         # lda = m + 1 (odd): not TMA-addressable
+    B = O.make_uniform((n, k), 4)
+    lda = m + 1
+    dA = torch.from_numpy(A).cuda()
+    lds = lda                                   # plane leading dimension equal to lda, not a multiple of 8
+    dSA = torch.zeros(lds * k * 3, dtype=torch.int16, device="cuda")
+    assert lib().mpemuSplitBF16(dA.data_ptr(), lda, m, k, 3, dSA.data_ptr(), lds, lds * k, None) == OK
+    dSB, lb, sb = split_gpu(B, k, n, k, 3, True)
+    dC = torch.zeros(n * m, dtype=torch.float32, device="cuda")
+    assert gemm_bf16(0, 0, m, n, k, dSA, lds, lds * k, dSB, lb, sb, 3, 0, 9, dC) == OK
+    torch.cuda.synchronize()
+    exact = O.gemm_f64(0, 0, m, n, k, A, lda, B, k).reshape(n, m)
+    absAB = O.gemm_f64(0, 0, m, n, k, np.abs(A), lda, np.abs(B), k).reshape(n, m)
+    assert np.all(np.abs(dC.cpu().numpy().reshape(n, m) - exact) <= 2 ** -19 * absAB + 1e-30)
+
+
+def test_invalid_arguments(cuda):
+    d = torch.zeros(64, dtype=torch.int16, device="cuda")
+    c = torch.zeros(64, dtype=torch.float32, device="cuda")
+    L = lib()
+    assert L.mpemuGemmEmulatedRange(handle(), 0, 0, 4, 4, 4, 1.0, d.data_ptr(), 8, 32, d.data_ptr(), 8, 32, 5, 0, 1,
+                                    0.0, c.data_ptr(), 4) == 1
+    assert L.mpemuGemmEmulatedRange(handle(), 0, 0, 4, 4, 4, 1.0, d.data_ptr(), 8, 32, d.data_ptr(), 8, 32, 3, 2, 1,
+                                    0.0, c.data_ptr(), 4) == 1
+    assert L.mpemuGemmEmulatedRange(None, 0, 0, 4, 4, 4, 1.0, d.data_ptr(), 8, 32, d.data_ptr(), 8, 32, 3, 3, 3,
+                                    1.0, c.data_ptr(), 4) == 0      # empty range with beta 1: no-op
+    assert L.mpemuGemmEmulatedRange(None, 0, 0, 4, 4, 4, 1.0, d.data_ptr(), 8, 32, d.data_ptr(), 8, 32, 3, 0, 3,
+                                    0.0, c.data_ptr(), 4) == 1      # no handle
+    assert L.mpemuSplitBF16(c.data_ptr(), 4, 4, 4, 5, d.data_ptr(), 8, 32, None) == 1
+    assert L.mpemuSplitFP16(c.data_ptr(), 4, 4, 4, 2, 0.0, d.data_ptr(), 8, 32, None) == 1
+    assert L.mpemuStatusString(3) == b"MPEMU_STATUS_CUBLAS_ERROR"
+
+
+# ----------------------------------------------------- config-2 accuracy ----
+
+@pytest.mark.parametrize("emax", [0, 8])
+def test_emulated_error_within_twice_native_sgemm(cuda, emax):
+    """BASELINE config 2 criterion at N = 2048: max |C - C64| of the emulated
+    GEMMs (BF16x3 with 6 products; FP16x2 scaled with 3) within 2x that of
+    native FP32 SGEMM (TF32 off)."""
+    N = 2048
+    A = O.make_uniform((N, N), 1000 + emax, emax=emax)       # column-major storage
+    B = O.make_uniform((N, N), 2000 + emax, emax=emax)
+    tA, tB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    # column-major C = A B  <=>  row-major C^T = B^T A^T, i.e. torch: (B_rm @ A_rm) with rm = the stored arrays
+    C64 = (tB.double() @ tA.double())
+    torch.backends.cuda.matmul.allow_tf32 = False
+    C32 = tB @ tA
+    native = float((C32.double() - C64).abs().max())
+    dSA, l, s = split_gpu(A, N, N, N, 3, True)
+    dSB, _, _ = split_gpu(B, N, N, N, 3, True)
+    dC = torch.zeros(N * N, dtype=torch.float32, device="cuda")
+    assert gemm_bf16(0, 0, N, N, N, dSA, l, s, dSB, l, s, 3, 0, 6, dC) == OK
+    bf = float((dC.reshape(N, N).double() - C64).abs().max())
+    sA, sB = autoscale_gpu(A, N, N, N), autoscale_gpu(B, N, N, N)
+    dHA, _, _ = split_gpu(A, N, N, N, 2, False, sA)
+    dHB, _, _ = split_gpu(B, N, N, N, 2, False, sB)
+    assert gemm_fp16(0, 0, N, N, N, dHA, l, s, sA, dHB, l, s, sB, 2, 0, 3, dC) == OK
+    fp = float((dC.reshape(N, N).double() - C64).abs().max())
+    assert bf <= 2 * native, (bf, native)
+    assert fp <= 2 * native, (fp, native)
