@@ -45,14 +45,20 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kSmemMax = 232448;        /* 227 KB, no static shared memory */
 constexpr int kMiscBytes = 2048;        /* barriers + the epilogue exchange */
 constexpr int kClasses = 8;
+constexpr int kMaxDim = 1 << 16;        /* TMA coordinates and the error-bound model */
 
+/* NKC > 0: the point tile (hi, lo planes, NKC chunks of 64) stays resident
+ * while every centroid tile streams past it.  NKC == 0 (d > 256): the point
+ * chunks stream too, through their own ring of (hi, lo) stages, next to the
+ * centroid ring. */
 template <int BN, int NKC>
 struct Cfg {
+    static constexpr bool STREAM = NKC == 0;
     static constexpr int A_CHUNK = BM * ROW_BYTES;            /* one plane, one K chunk */
-    static constexpr int A_TILE = 2 * NKC * A_CHUNK;          /* hi + lo                */
+    static constexpr int A_TILE = STREAM ? 2 * A_CHUNK : 2 * NKC * A_CHUNK;   /* hi + lo: a tile or a stage */
     static constexpr int B_STAGE = BN * ROW_BYTES;
     static constexpr int BUDGET = kSmemMax - kMiscBytes;
-    static constexpr int A_BUFS = (2 * A_TILE + 3 * B_STAGE <= BUDGET) ? 2 : 1;
+    static constexpr int A_BUFS = STREAM ? 3 : ((2 * A_TILE + 3 * B_STAGE <= BUDGET) ? 2 : 1);
     static constexpr int B_RAW = (BUDGET - A_BUFS * A_TILE) / B_STAGE;
     static constexpr int B_STAGES = B_RAW > 8 ? 8 : B_RAW;
     static constexpr int TILE_BYTES = A_BUFS * A_TILE + B_STAGES * B_STAGE;
@@ -68,7 +74,7 @@ struct Cfg {
 
 /* Shared-memory block after the tiles. */
 struct Misc {
-    uint64_t a_full[2], a_empty[2], b_full[8], b_empty[8], t_full[2], t_empty[2], fin;
+    uint64_t a_full[4], a_empty[4], b_full[8], b_empty[8], t_full[2], t_empty[2], fin;
     uint32_t tmem_slot;
     int abort_flag;
     float wmax[kThreads / 32];
@@ -115,10 +121,12 @@ __device__ __forceinline__ float thr_of(float T0, float v, float v0) {
 template <int BN, int NKC>
 __global__ void __launch_bounds__(kThreads, 1)
 k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmC,
-            long long n, int k, const float* __restrict__ xnorm, const float* __restrict__ cn,
+            long long n, int k, int nkc_rt, const float* __restrict__ xnorm, const float* __restrict__ cn,
             DevParams* __restrict__ prm, int* __restrict__ labels, RefineEntry* __restrict__ list,
             int refine, BoundConsts bc, float4* __restrict__ dbg) {
     using Cf = Cfg<BN, NKC>;
+    static_assert(Cf::A_BUFS <= 4, "A ring");
+    const int nkc = Cf::STREAM ? nkc_rt : NKC;   /* K chunks of 64 */
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* smA = smem;
     uint8_t* smB = smem + Cf::A_BUFS * Cf::A_TILE;
@@ -161,34 +169,51 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
     if (warp == 0) {
         /* ------------------------------------------------ TMA producer --- */
         if (lane == 0) {
-            uint32_t a_last[2] = {0xffffffffu, 0xffffffffu};
+            uint32_t a_last[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
             uint32_t b_last[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) b_last[i] = 0xffffffffu;
-            uint32_t bs = 0;
+            uint32_t bs = 0, as = 0;
             int lt = 0;
             bool ok = true;
+            auto load_b = [&](int nt, int kc) {
+                for (int p = 0; p < 2; ++p) {
+                    const int st = (int)(bs % Cf::B_STAGES);
+                    const uint32_t bu = bs / Cf::B_STAGES;
+                    if (!mbar_wait(&ms.b_empty[st], (bu & 1u) ^ 1u, abort_flag, status)) { ok = false; return; }
+                    mbar_expect_tx(&ms.b_full[st], Cf::B_STAGE);
+                    b_last[st] = bu;
+                    tma_load_3d(&tmC, &ms.b_full[st], smB + st * Cf::B_STAGE, kc * KC, nt * BN, p);
+                    ++bs;
+                }
+            };
             for (long long mt = blockIdx.x; mt < num_mt && ok; mt += gridDim.x, ++lt) {
+                if (Cf::STREAM) {
+                    for (int nt = 0; nt < NT && ok; ++nt)
+                        for (int kc = 0; kc < nkc && ok; ++kc, ++as) {
+                            const int ab = (int)(as % Cf::A_BUFS);
+                            const uint32_t au = as / Cf::A_BUFS;
+                            if (!mbar_wait(&ms.a_empty[ab], (au & 1u) ^ 1u, abort_flag, status)) { ok = false; break; }
+                            mbar_expect_tx(&ms.a_full[ab], Cf::A_TILE);
+                            a_last[ab] = au;
+                            for (int p = 0; p < 2; ++p)
+                                tma_load_3d(&tmX, &ms.a_full[ab], smA + ab * Cf::A_TILE + p * Cf::A_CHUNK, kc * KC,
+                                            (int)(mt * BM), p);
+                            load_b(nt, kc);
+                        }
+                    continue;
+                }
                 const int ab = lt % Cf::A_BUFS;
                 const uint32_t au = (uint32_t)(lt / Cf::A_BUFS);
                 if (!mbar_wait(&ms.a_empty[ab], (au & 1u) ^ 1u, abort_flag, status)) { ok = false; break; }
                 mbar_expect_tx(&ms.a_full[ab], Cf::A_TILE);
                 a_last[ab] = au;
                 for (int p = 0; p < 2; ++p)
-                    for (int kc = 0; kc < NKC; ++kc)
-                        tma_load_3d(&tmX, &ms.a_full[ab], smA + ab * Cf::A_TILE + (p * NKC + kc) * Cf::A_CHUNK,
+                    for (int kc = 0; kc < nkc; ++kc)
+                        tma_load_3d(&tmX, &ms.a_full[ab], smA + ab * Cf::A_TILE + (p * nkc + kc) * Cf::A_CHUNK,
                                     kc * KC, (int)(mt * BM), p);
                 for (int nt = 0; nt < NT && ok; ++nt)
-                    for (int kc = 0; kc < NKC && ok; ++kc)
-                        for (int p = 0; p < 2; ++p) {
-                            const int st = (int)(bs % Cf::B_STAGES);
-                            const uint32_t bu = bs / Cf::B_STAGES;
-                            if (!mbar_wait(&ms.b_empty[st], (bu & 1u) ^ 1u, abort_flag, status)) { ok = false; break; }
-                            mbar_expect_tx(&ms.b_full[st], Cf::B_STAGE);
-                            b_last[st] = bu;
-                            tma_load_3d(&tmC, &ms.b_full[st], smB + st * Cf::B_STAGE, kc * KC, nt * BN, p);
-                            ++bs;
-                        }
+                    for (int kc = 0; kc < nkc && ok; ++kc) load_b(nt, kc);
             }
             if (!ok) {
                 /* let every load already issued land before the CTA exits */
@@ -202,14 +227,47 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
         /* ------------------------------------------------- MMA issuer ---- */
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f16(BM, BN, 0, 0, 0);
-            uint32_t bs = 0, ts = 0;
+            uint32_t bs = 0, ts = 0, as = 0;
             int lt = 0;
             bool ok = true;
+            /* hi*hi + lo*hi + hi*lo of one 64-deep chunk; the point planes at ah / al */
+            auto chunk = [&](uint32_t d_tmem, uint32_t ah, uint32_t al, uint32_t& accum) {
+                /* centroid hi plane: x_hi * c_hi and x_lo * c_hi */
+                int st = (int)(bs % Cf::B_STAGES);
+                uint32_t bu = bs / Cf::B_STAGES;
+                if (!mbar_wait(&ms.b_full[st], bu & 1u, abort_flag, status)) { ok = false; return; }
+                tc_fence_after();
+                const uint32_t bh = smem_u32(smB + st * Cf::B_STAGE);
+#pragma unroll
+                for (int ks = 0; ks < KC / 16; ++ks) {
+                    umma_f16(d_tmem, sw128_desc(ah + ks * 32, 16, 1024), sw128_desc(bh + ks * 32, 16, 1024), idesc,
+                             accum);
+                    accum = 1;
+                }
+#pragma unroll
+                for (int ks = 0; ks < KC / 16; ++ks)
+                    umma_f16(d_tmem, sw128_desc(al + ks * 32, 16, 1024), sw128_desc(bh + ks * 32, 16, 1024), idesc, 1);
+                umma_commit(&ms.b_empty[st]);
+                ++bs;
+                /* centroid lo plane: x_hi * c_lo */
+                st = (int)(bs % Cf::B_STAGES);
+                bu = bs / Cf::B_STAGES;
+                if (!mbar_wait(&ms.b_full[st], bu & 1u, abort_flag, status)) { ok = false; return; }
+                tc_fence_after();
+                const uint32_t bl = smem_u32(smB + st * Cf::B_STAGE);
+#pragma unroll
+                for (int ks = 0; ks < KC / 16; ++ks)
+                    umma_f16(d_tmem, sw128_desc(ah + ks * 32, 16, 1024), sw128_desc(bl + ks * 32, 16, 1024), idesc, 1);
+                umma_commit(&ms.b_empty[st]);
+                ++bs;
+            };
             for (long long mt = blockIdx.x; mt < num_mt && ok; mt += gridDim.x, ++lt) {
                 const int ab = lt % Cf::A_BUFS;
                 const uint32_t au = (uint32_t)(lt / Cf::A_BUFS);
-                if (!mbar_wait(&ms.a_full[ab], au & 1u, abort_flag, status)) { ok = false; break; }
-                tc_fence_after();
+                if (!Cf::STREAM) {
+                    if (!mbar_wait(&ms.a_full[ab], au & 1u, abort_flag, status)) { ok = false; break; }
+                    tc_fence_after();
+                }
                 const uint32_t a_addr = smem_u32(smA + ab * Cf::A_TILE);
                 for (int nt = 0; nt < NT && ok; ++nt, ++ts) {
                     const int tb = (int)(ts & 1u);
@@ -218,43 +276,23 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + (uint32_t)(tb * BN);
                     uint32_t accum = 0;
-                    for (int kc = 0; kc < NKC && ok; ++kc) {
-                        const uint32_t ah = a_addr + (uint32_t)(kc * Cf::A_CHUNK);
-                        const uint32_t al = a_addr + (uint32_t)((NKC + kc) * Cf::A_CHUNK);
-                        /* centroid hi plane: x_hi * c_hi and x_lo * c_hi */
-                        int st = (int)(bs % Cf::B_STAGES);
-                        uint32_t bu = bs / Cf::B_STAGES;
-                        if (!mbar_wait(&ms.b_full[st], bu & 1u, abort_flag, status)) { ok = false; break; }
-                        tc_fence_after();
-                        const uint32_t bh = smem_u32(smB + st * Cf::B_STAGE);
-#pragma unroll
-                        for (int ks = 0; ks < KC / 16; ++ks) {
-                            umma_f16(d_tmem, sw128_desc(ah + ks * 32, 16, 1024), sw128_desc(bh + ks * 32, 16, 1024),
-                                     idesc, accum);
-                            accum = 1;
+                    for (int kc = 0; kc < nkc && ok; ++kc) {
+                        if (Cf::STREAM) {
+                            const int sa = (int)(as % Cf::A_BUFS);
+                            if (!mbar_wait(&ms.a_full[sa], (as / Cf::A_BUFS) & 1u, abort_flag, status)) { ok = false; break; }
+                            tc_fence_after();
+                            const uint32_t ah = smem_u32(smA + sa * Cf::A_TILE);
+                            chunk(d_tmem, ah, ah + Cf::A_CHUNK, accum);
+                            if (ok) umma_commit(&ms.a_empty[sa]);
+                            ++as;
+                        } else {
+                            chunk(d_tmem, a_addr + (uint32_t)(kc * Cf::A_CHUNK),
+                                  a_addr + (uint32_t)((nkc + kc) * Cf::A_CHUNK), accum);
                         }
-#pragma unroll
-                        for (int ks = 0; ks < KC / 16; ++ks)
-                            umma_f16(d_tmem, sw128_desc(al + ks * 32, 16, 1024), sw128_desc(bh + ks * 32, 16, 1024),
-                                     idesc, 1);
-                        umma_commit(&ms.b_empty[st]);
-                        ++bs;
-                        /* centroid lo plane: x_hi * c_lo */
-                        st = (int)(bs % Cf::B_STAGES);
-                        bu = bs / Cf::B_STAGES;
-                        if (!mbar_wait(&ms.b_full[st], bu & 1u, abort_flag, status)) { ok = false; break; }
-                        tc_fence_after();
-                        const uint32_t bl = smem_u32(smB + st * Cf::B_STAGE);
-#pragma unroll
-                        for (int ks = 0; ks < KC / 16; ++ks)
-                            umma_f16(d_tmem, sw128_desc(ah + ks * 32, 16, 1024), sw128_desc(bl + ks * 32, 16, 1024),
-                                     idesc, 1);
-                        umma_commit(&ms.b_empty[st]);
-                        ++bs;
                     }
                     if (ok) umma_commit(&ms.t_full[tb]);
                 }
-                if (ok) umma_commit(&ms.a_empty[ab]);
+                if (ok && !Cf::STREAM) umma_commit(&ms.a_empty[ab]);
             }
             /* every MMA issued by this thread has completed once fin flips */
             umma_commit(&ms.fin);
@@ -425,8 +463,8 @@ cudaError_t launch_t(const AssignArgs& a, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     const long long num_mt = (a.n + BM - 1) / BM;
     const int grid = (int)(num_mt < a.num_sms ? num_mt : a.num_sms);
-    kern<<<grid, kThreads, Cf::SMEM_BYTES, s>>>(*a.tmX, *a.tmC, a.n, a.k, a.xnorm, a.cn, a.prm, a.labels,
-                                                 a.list, a.refine, a.bc, a.dbg);
+    kern<<<grid, kThreads, Cf::SMEM_BYTES, s>>>(*a.tmX, *a.tmC, a.n, a.k, a.dp / KC, a.xnorm, a.cn, a.prm,
+                                                 a.labels, a.list, a.refine, a.bc, a.dbg);
     return cudaGetLastError();
 }
 
@@ -437,14 +475,14 @@ cudaError_t launch_bn(const AssignArgs& a, cudaStream_t s) {
         case 2: return launch_t<BN, 2>(a, s);
         case 3: return launch_t<BN, 3>(a, s);
         case 4: return launch_t<BN, 4>(a, s);
-        default: return cudaErrorInvalidValue;
+        default: return launch_t<BN, 0>(a, s);      /* d > 256: streaming point chunks */
     }
 }
 
 }  /* namespace */
 
 int assign_bn_for(int k) { return k <= 64 ? 64 : (k <= 128 ? 128 : 256); }
-int assign_supported(int d) { return d >= 1 && d <= 4 * KC; }
+int assign_supported(int d) { return d >= 1 && d <= kMaxDim; }
 
 cudaError_t launch_assign(const AssignArgs& a, cudaStream_t s) {
     if (a.n <= 0) return cudaSuccess;

@@ -9,14 +9,16 @@
  * (op = N for A, op = T for B) in 128-byte swizzle; the instruction
  * descriptor carries the majors.
  *
- * Output tiles are 128 x 256.  Each 64-deep K chunk of each term is
+ * Output tiles are 128 x 256.  Each 512-deep K slice of each term is
  * accumulated by the tensor cores into a fresh TMEM partial (two buffers of
- * 256 columns, so the MMAs of the next chunk overlap the read-out of this
+ * 256 columns, so the MMAs of the next slice overlap the read-out of this
  * one); the epilogue adds every partial into a running FP32 sum held in
  * registers with round-to-nearest.  The tensor cores' own FP32 accumulation
  * (truncating, its error growing with the number of MMA steps that add into
- * one accumulator) therefore only ever spans 4 steps of small partials, and
- * the long sum behaves like an FP32 SGEMM's.  When alpha is a power of two
+ * one accumulator) therefore only ever spans 32 steps of a partial, and the
+ * long sum behaves like an FP32 SGEMM's.  (Measured at M = N = K = 8192 and
+ * 2048: 256- to 512-deep partials give the smallest error; shorter ones add
+ * more round-to-nearest sums, longer ones more truncation.)  When alpha is a power of two
  * and beta is 0 or 1 the sum starts from beta * C / alpha (exact) and alpha *
  * sum is stored (exact): a range continued by another range then reproduces,
  * bit for bit, the single range -- the property the reference's per-term
@@ -40,6 +42,26 @@ constexpr int A_STAGE = BM * BK * 2;             /* 16 KB */
 constexpr int kSmemMax = 232448;
 constexpr int kMisc = 1024;
 constexpr int BOX = 64 * 64 * 2;                 /* one 64 x 64 MN-major box: 8 KB */
+#ifndef GEMM_CHUNKS_PER_PARTIAL
+#define GEMM_CHUNKS_PER_PARTIAL 8
+#endif
+/* 64-deep K chunks the tensor cores accumulate into one TMEM partial before
+ * the epilogue folds it into the round-to-nearest sum (a partial never spans
+ * two terms). */
+constexpr int CPP = GEMM_CHUNKS_PER_PARTIAL;
+constexpr int kGroupM = 16;                      /* tile rows per raster group */
+
+/* Tile order: groups of kGroupM tile rows, column by column inside a group,
+ * so the CTAs resident at one time share a few A row panels and B column
+ * panels (L2 reuse) instead of sweeping all of A for every column. */
+__device__ __forceinline__ void tile_coords(long long tile, int tiles_m, int tiles_n, int& tm, int& tn) {
+    const long long per_group = (long long)kGroupM * tiles_n;
+    const int g = (int)(tile / per_group);
+    const int r = (int)(tile - (long long)g * per_group);
+    const int rows = min(kGroupM, tiles_m - g * kGroupM);
+    tm = g * kGroupM + r % rows;
+    tn = r / rows;
+}
 
 /* Epilogue modes: how C enters and leaves the running sum. */
 enum : int {
@@ -121,7 +143,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
             uint32_t it = 0;
             bool ok = true;
             for (long long tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-                const int tm = (int)(tile % tiles_m), tn = (int)(tile / tiles_m);
+                int tm, tn;
+                tile_coords(tile, tiles_m, tiles_n, tm, tn);
                 for (int t = 0; t < terms.n && ok; ++t)
                     for (int kc = 0; kc < KCH; ++kc, ++it) {
                         const int st = (int)(it % STAGES);
@@ -154,15 +177,18 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
         /* ------------------------------------------------- MMA issuer --- */
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f16(BM, BN, FMT, A_MN ? 1 : 0, B_MN ? 1 : 0);
-            uint32_t it = 0;
+            uint32_t it = 0, pi = 0;                    /* stage counter, partial counter */
             bool ok = true;
             for (long long tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x)
                 for (int t = 0; t < terms.n && ok; ++t)
                     for (int kc = 0; kc < KCH; ++kc, ++it) {
                         const int st = (int)(it % STAGES);
-                        const int pb = (int)(it & 1u);          /* partial buffer of this chunk */
+                        const int pb = (int)(pi & 1u);          /* partial buffer of this chunk */
+                        const int kin = kc % CPP;               /* chunk index inside the partial */
+                        const bool last_of_partial = kin == CPP - 1 || kc == KCH - 1;
                         if (!mbar_wait(&ms.full[st], (it / STAGES) & 1u, abort_flag, status)) { ok = false; break; }
-                        if (!mbar_wait(&ms.p_empty[pb], ((it >> 1) & 1u) ^ 1u, abort_flag, status)) { ok = false; break; }
+                        if (kin == 0 &&
+                            !mbar_wait(&ms.p_empty[pb], ((pi >> 1) & 1u) ^ 1u, abort_flag, status)) { ok = false; break; }
                         tc_fence_after();
                         const uint32_t sa = smem_u32(smem + st * STAGE);
                         const uint32_t sb = sa + A_STAGE;
@@ -173,10 +199,13 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
                                                      : sw128_desc(sa + ks * 32, 16, 1024);
                             const uint64_t bd = B_MN ? sw128_desc(sb + ks * 2048, BOX, 1024)
                                                      : sw128_desc(sb + ks * 32, 16, 1024);
-                            umma_f16(d_tmem, ad, bd, idesc, ks > 0 ? 1u : 0u);
+                            umma_f16(d_tmem, ad, bd, idesc, (kin > 0 || ks > 0) ? 1u : 0u);
                         }
                         umma_commit(&ms.empty[st]);
-                        umma_commit(&ms.p_full[pb]);
+                        if (last_of_partial) {
+                            umma_commit(&ms.p_full[pb]);
+                            ++pi;
+                        }
                     }
             umma_commit(&ms.fin);
             drain_wait(&ms.fin, 0);
@@ -190,9 +219,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
         const uint32_t t_lane = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(half * HALF);
         const float inv_alpha = 1.0f / alpha;     /* exact in EPI_RESUME (alpha a power of two) */
         bool ok = true;
-        uint32_t it = 0;
+        uint32_t pi = 0;
         for (long long tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-            const int tm = (int)(tile % tiles_m), tn = (int)(tile / tiles_m);
+            int tm, tn;
+            tile_coords(tile, tiles_m, tiles_n, tm, tn);
             const int row = tm * BM + q * 32 + lane;
             const int col0 = tn * BN + half * HALF;
             const int ncol = min(HALF, n - col0);
@@ -214,9 +244,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUten
                 for (int e = 0; e < HALF; ++e) S[e] = 0.f;
             }
             for (int t = 0; t < terms.n; ++t)
-                for (int kc = 0; kc < KCH; ++kc, ++it) {
-                    const int pb = (int)(it & 1u);
-                    if (ok) ok = wait_warp(&ms.p_full[pb], (it >> 1) & 1u, abort_flag, status);
+                for (int kc = 0; kc < KCH; kc += CPP, ++pi) {
+                    const int pb = (int)(pi & 1u);
+                    if (ok) ok = wait_warp(&ms.p_full[pb], (pi >> 1) & 1u, abort_flag, status);
                     if (!ok) continue;
                     tc_fence_after();
 #pragma unroll

@@ -133,20 +133,34 @@ __global__ void k_prep_c(const float* __restrict__ C, int k, int d, int dp, DevP
 /* ------------------------------------------------------------- refine ---- */
 
 /* Up to four candidate distances at once, each exactly as the reference's
- * refinement forms it (kmeans/src/kernels.cu:582-602): lane l runs an fmaf chain over l, l+32, ... (the point
- * row is held in registers, pr[i] = p[lane + 32 i]), the shfl_down tree sums
- * the lanes, and D = fmaf(-2, dot, ||c||^2).  The best (smaller index on a
- * tie) is folded into (bv, bj), valid in lane 0. */
-__device__ __forceinline__ void eval4(const float (&pr)[8], const float* __restrict__ C, const float* __restrict__ cn,
-                                      int d, int lane, const int (&j)[4], float& bv, int& bj) {
+ * refinement forms it (kmeans/src/kernels.cu:582-602): lane l runs an fmaf
+ * chain over l, l+32, ..., the shfl_down tree sums the lanes, and
+ * D = fmaf(-2, dot, ||c||^2).  The best (smaller index on a tie) is folded
+ * into (bv, bj), valid in lane 0.  The point row is held in registers,
+ * pr[i] = p[lane + 32 i], when d <= 32 * NR; NR == 0 reads it from memory
+ * (L1) instead, for any d -- the same chain either way. */
+template <int NR>
+__device__ __forceinline__ void eval4(const float (&pr)[NR > 0 ? NR : 1], const float* __restrict__ p,
+                                      const float* __restrict__ C, const float* __restrict__ cn, int d, int lane,
+                                      const int (&j)[4], float& bv, int& bj) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    if (NR > 0) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int t = lane + 32 * i;
-        if (t < d) {
+        for (int i = 0; i < (NR > 0 ? NR : 1); ++i) {
+            const int t = lane + 32 * i;
+            if (t < d) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    if (j[q] >= 0) acc[q] = fmaf(pr[i], __ldg(C + (size_t)j[q] * d + t), acc[q]);
+            }
+        }
+    } else {
+#pragma unroll 4
+        for (int t = lane; t < d; t += 32) {
+            const float pv = __ldg(p + t);
 #pragma unroll
             for (int q = 0; q < 4; ++q)
-                if (j[q] >= 0) acc[q] = fmaf(pr[i], __ldg(C + (size_t)j[q] * d + t), acc[q]);
+                if (j[q] >= 0) acc[q] = fmaf(pv, __ldg(C + (size_t)j[q] * d + t), acc[q]);
         }
     }
 #pragma unroll
@@ -164,10 +178,12 @@ __device__ __forceinline__ void eval4(const float (&pr)[8], const float* __restr
 /* One warp per refinement entry: the listed candidates, then every column of
  * each overflowing class, in batches of four; the label is the smallest FP32
  * distance, the smaller index on a tie.  Control flow is warp uniform (every
- * lane reads the same entry). */
+ * lane reads the same entry).  NR: see eval4. */
+template <int NR>
 __global__ void k_refine(const float* __restrict__ P, const float* __restrict__ C, const float* __restrict__ cn,
                          int d, int k, int bn, const RefineEntry* __restrict__ list, DevParams* __restrict__ prm,
                          int* __restrict__ labels, long long cap, unsigned long long* hist_slot) {
+    constexpr int R = NR > 0 ? NR : 1;
     const int lane = threadIdx.x & 31;
     const long long nf = prm->nflag < (unsigned long long)cap ? (long long)prm->nflag : cap;
     const long long wstride = (long long)gridDim.x * (blockDim.x >> 5);
@@ -177,11 +193,11 @@ __global__ void k_refine(const float* __restrict__ P, const float* __restrict__ 
     for (long long e = w0; e < nf; e += wstride) {
         const RefineEntry E = list[e];
         const float* p = P + (size_t)E.row * d;
-        float pr[8];
+        float pr[R];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < R; ++i) {
             const int t = lane + 32 * i;
-            pr[i] = t < d ? p[t] : 0.f;
+            pr[i] = (NR > 0 && t < d) ? p[t] : 0.f;
         }
         float bv = INFINITY;
         int bj = k;
@@ -190,7 +206,7 @@ __global__ void k_refine(const float* __restrict__ P, const float* __restrict__ 
         auto push = [&](int j) {
             batch[nb++] = j;
             if (nb == 4) {
-                eval4(pr, C, cn, d, lane, batch, bv, bj);
+                eval4<NR>(pr, p, C, cn, d, lane, batch, bv, bj);
                 batch[0] = batch[1] = batch[2] = batch[3] = -1;
                 nb = 0;
             }
@@ -216,7 +232,7 @@ __global__ void k_refine(const float* __restrict__ P, const float* __restrict__ 
                         }
                 }
         }
-        if (nb) eval4(pr, C, cn, d, lane, batch, bv, bj);
+        if (nb) eval4<NR>(pr, p, C, cn, d, lane, batch, bv, bj);
         if (lane == 0) labels[E.row] = bj;   /* lane 0 holds the reduced dots */
     }
     if (lane == 0 && ncand) {
@@ -348,7 +364,8 @@ void launch_prep_c(const float* C, int k, int kpad, int d, int dp, DevParams* pr
 void launch_refine(const float* P, const float* C, const float* cn, int d, int k, int bn, const RefineEntry* list,
                    DevParams* prm, int* labels, long long n_cap, unsigned long long* hist_slot, int num_sms,
                    cudaStream_t s) {
-    k_refine<<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, bn, list, prm, labels, n_cap, hist_slot);
+    if (d <= 256) k_refine<8><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, bn, list, prm, labels, n_cap, hist_slot);
+    else k_refine<0><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, bn, list, prm, labels, n_cap, hist_slot);
 }
 
 void launch_finalize_fixed(const long long* sums, const long long* counts, int k, int d, const DevParams* prm,

@@ -206,7 +206,7 @@ static mpkStatus engine_create(mpkEngine* out, const float* dP, long long n, int
         return MPK_ERR_CUDA;
     }
     if (need_assign && !assign_supported(d)) {
-        fprintf(stderr, "mpkmeans_b200: d = %d is above the assignment kernel's limit of 256\n", d);
+        fprintf(stderr, "mpkmeans_b200: d = %d is above the assignment kernel's limit of 65536\n", d);
         delete e;
         return MPK_ERR_INVALID;
     }

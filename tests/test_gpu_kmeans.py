@@ -59,7 +59,10 @@ def gpu_assign(P, C, **kw):
 
 @pytest.mark.parametrize("n,d,k", [(300, 16, 10), (1000, 32, 64), (2000, 64, 100), (1500, 128, 256),
                                    (1000, 200, 300), (4000, 128, 1024), (999, 256, 17), (129, 1, 3),
-                                   (128, 64, 1), (5000, 96, 640)])
+                                   (128, 64, 1), (5000, 96, 640),
+                                   # d > 256: the point chunks stream through their own ring
+                                   (1000, 300, 100), (2048, 768, 600), (700, 1000, 33), (3000, 512, 1024),
+                                   (257, 320, 257)])
 def test_assign_equals_fp32_oracle(cuda, n, d, k):
     P, C = make_problem(n, d, k, seed=n + d + k)
     lab, st = gpu_assign(P, C)
@@ -112,6 +115,51 @@ def test_assign_error_bound_holds(cuda):
     assert ratio.max() < 0.25, ratio.max()
 
 
+def test_assign_error_bound_holds_unit_sphere_d768(cuda):
+    """Config-4 geometry (unit-norm points around random centres, d = 768) on the
+    streaming variant: the bound still holds with room, and labels are exact."""
+    rng = np.random.default_rng(44)
+    n, d, k = 6000, 768, 384
+    cen = rng.standard_normal((k, d))
+    P = cen[rng.integers(0, k, n)] + rng.standard_normal((n, d))
+    P = (P / np.linalg.norm(P, axis=1, keepdims=True)).astype(np.float32)
+    C = P[rng.choice(n, size=k, replace=False)].copy()
+    dP, dC = dev(P), dev(C)
+    with M.Engine(dP, k, C0=dC) as e:
+        info = e.info()
+        out4 = torch.zeros((n, 4), dtype=torch.float32, device="cuda")
+        lab = torch.empty(n, dtype=torch.int32, device="cuda")
+        e.trace(out4)
+        e.assign(dC, lab, refine=True)
+        torch.cuda.synchronize()
+        e.trace(None)
+    assert np.array_equal(lab.cpu().numpy(), O.assign_fp32(P, C))
+    t = out4.cpu().numpy()
+    v0 = t[:, 0].astype(np.float64)
+    j0 = t[:, 2].view(np.int32)
+    cn = O.row_norms(C).astype(np.float64)
+    exact = cn[j0] - 2.0 * np.einsum("ij,ij->i", P.astype(np.float64), C[j0].astype(np.float64))
+    xn = np.linalg.norm(P.astype(np.float64), axis=1)
+    T = info["c1"] * xn * np.sqrt(cn.max()) + info["c2"] * info["eta"] * (xn + np.sqrt(cn.max())) + \
+        2.0 ** -22 * 2 * np.abs(exact)
+    assert (np.abs(v0 - exact) / T).max() < 0.25
+
+
+def test_lloyd_d768_bit_exact_vs_oracle(cuda):
+    rng = np.random.default_rng(7)
+    n, d, k, iters = 3000, 768, 40, 4
+    P = (rng.standard_normal((n, d)) + 3 * rng.standard_normal((n, 1))).astype(np.float32)
+    C0 = P[rng.choice(n, size=k, replace=False)].copy()
+    dP, dC = dev(P), dev(C0)
+    lab = torch.empty(n, dtype=torch.int32, device="cuda")
+    st = M.means_mixed(dP, dC, lab, M.params_init(max_iter=iters, tol=0.0))
+    torch.cuda.synchronize()
+    lr, Cr, _, it = O.lloyd(P, C0, iters, update_mode=1, frac=O.fixed_frac(float(np.abs(P).max()), n))
+    assert st.iters == iters and it == iters
+    assert np.array_equal(lab.cpu().numpy(), lr)
+    assert np.array_equal(dC.cpu().numpy().view(np.uint32), Cr.view(np.uint32))
+
+
 def test_assign_raw_mode_close(cuda):
     P, C = make_problem(8000, 64, 200, seed=9)
     lab, st = gpu_assign(P, C, use_cond3=0, use_cond6=0)
@@ -129,9 +177,6 @@ def test_assign_rejects_invalid(cuda):
     assert lib.mpkAssign(None, dP.data_ptr(), 0, 8, 4, dC.data_ptr(), lab.data_ptr(), None, None) == M.MPK_ERR_INVALID
     assert lib.mpkAssign(None, dP.data_ptr(), 100, 8, 0, dC.data_ptr(), lab.data_ptr(), None, None) == M.MPK_ERR_INVALID
     assert lib.mpkMeansMixed(None, dP.data_ptr(), 3, 8, 4, dC.data_ptr(), lab.data_ptr(), None, None) == M.MPK_ERR_INVALID
-    P3 = np.zeros((16, 300), np.float32)
-    assert lib.mpkAssign(None, dev(P3).data_ptr(), 16, 300, 4, dev(np.zeros((4, 300), np.float32)).data_ptr(),
-                         lab.data_ptr(), None, None) == M.MPK_ERR_INVALID
 
 
 # ---------------------------------------------------------------- update ----
