@@ -21,6 +21,11 @@ mpkStatus mpkDebugSetAssignTrace(mpkEngine e, float* dOut4);
  * and the two error-bound constants of the assignment filter. */
 mpkStatus mpkDebugEngineInfo(mpkEngine e, float* scale, float* eta, int* frac, float* c1, float* c2);
 
+/* Wide refinement: rows handed to the candidate-listing tensor-core pass over
+ * the engine's life, rows of those that fell back to a scan of all k, and
+ * the per-assignment capacity (0: the engine has no wide path, k <= 256). */
+mpkStatus mpkDebugWideCounters(mpkEngine e, long long* wide_rows, long long* full_scans, long long* capacity);
+
 /* While enabled, the engine records a CUDA event pair on its stream around
  * every assignment kernel and every accumulation (update) kernel launch. */
 mpkStatus mpkDebugProfile(mpkEngine e, int enable);

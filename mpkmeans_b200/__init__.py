@@ -142,6 +142,7 @@ SIGNATURES = {
     "mpkDebugProfile": (_I, [_P, _I]),
     "mpkDebugProfileRead": (_I, [_P, ctypes.POINTER(_D), ctypes.POINTER(_LL), ctypes.POINTER(_D),
                                  ctypes.POINTER(_LL)]),
+    "mpkDebugWideCounters": (_I, [_P, ctypes.POINTER(_LL), ctypes.POINTER(_LL), ctypes.POINTER(_LL)]),
 }
 
 _lib = None
@@ -277,6 +278,12 @@ class Engine:
         check("mpkEngineCounters", lib().mpkEngineCounters(self.h, ctypes.byref(r), ctypes.byref(c),
                                                            ctypes.byref(f), ctypes.byref(s)))
         return {"rows_refined": r.value, "cand_refined": c.value, "rows_full_scan": f.value, "status": s.value}
+
+    def wide_counters(self) -> dict:
+        w, f, c = _LL(), _LL(), _LL()
+        check("mpkDebugWideCounters", lib().mpkDebugWideCounters(self.h, ctypes.byref(w), ctypes.byref(f),
+                                                                 ctypes.byref(c)))
+        return {"wide_rows": w.value, "full_scans": f.value, "capacity": c.value}
 
     def info(self) -> dict:
         sc, eta, c1, c2 = _F(), _F(), _F(), _F()

@@ -118,13 +118,22 @@ __device__ __forceinline__ float thr_of(float T0, float v, float v0) {
     return (T0 + 0x1.0p-22f * (fabsf(v) + fabsf(v0))) * (1.0f + 0x1.0p-20f);
 }
 
-template <int BN, int NKC>
+/* EMIT: the wide-refinement pass.  The rows are the first prm->nwide rows of
+ * tmX (copies of wide rows' planes); instead of an argmin, every column whose
+ * emulated value lies within the row's bound (v0, T0 from its refinement
+ * entry) is written to the row's candidate list. */
+template <int BN, int NKC, bool EMIT>
 __global__ void __launch_bounds__(kThreads, 1)
 k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmC,
             long long n, int k, int nkc_rt, const float* __restrict__ xnorm, const float* __restrict__ cn,
             DevParams* __restrict__ prm, int* __restrict__ labels, RefineEntry* __restrict__ list,
-            int refine, BoundConsts bc, float4* __restrict__ dbg) {
+            int refine, BoundConsts bc, float4* __restrict__ dbg, const int* __restrict__ went,
+            int* __restrict__ cand, int* __restrict__ ccount) {
     using Cf = Cfg<BN, NKC>;
+    if (EMIT) {
+        const long long nw = (long long)*reinterpret_cast<volatile unsigned int*>(&prm->nwide);
+        n = nw < n ? nw : n;
+    }
     static_assert(Cf::A_BUFS <= 4, "A ring");
     const int nkc = Cf::STREAM ? nkc_rt : NKC;   /* K chunks of 64 */
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -316,6 +325,55 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
         bool ok = true;
         /* The loop runs every tile even after a failed wait (ok == false, the
          * kernel is aborting): both halves must reach the same named barriers. */
+        if (EMIT) {
+            for (long long mt = blockIdx.x; mt < num_mt; mt += gridDim.x) {
+                const long long row = mt * BM + r_loc;
+                const bool live = row < n;
+                float v0 = INFINITY, T0 = 0.f;
+                if (live) {
+                    const RefineEntry* E = list + went[row];
+                    v0 = E->v0;
+                    T0 = E->T0;
+                }
+                int* cl = cand + (size_t)(live ? row : 0) * kWideCand + half * (kWideCand / 2);
+                int cnt = 0;
+                for (int nt = 0; nt < NT; ++nt, ++ts) {
+                    const int tb = (int)(ts & 1u);
+                    const uint32_t tu = ts >> 1;
+                    if (ok) ok = wait_warp(&ms.t_full[tb], tu & 1u, abort_flag, status);
+                    if (!ok) continue;
+                    tc_fence_after();
+                    const int col0 = half * Cf::HALF;
+#pragma unroll
+                    for (int cc = 0; cc < Cf::CHUNKS; ++cc) {
+                        uint32_t r[32];
+                        tmem_ld32(t_lane + (uint32_t)(tb * BN + col0 + cc * 32), r);
+                        tmem_ld_wait();
+                        const int jt = col0 + cc * 32;
+                        const float4* cn4 = reinterpret_cast<const float4*>(cn + nt * BN + jt);
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) {
+                            const float4 cv = __ldg(cn4 + u);
+                            float D[4];
+                            fma2(__uint_as_float(r[4 * u]), __uint_as_float(r[4 * u + 1]), ns2, cv.x, cv.y, D[0], D[1]);
+                            fma2(__uint_as_float(r[4 * u + 2]), __uint_as_float(r[4 * u + 3]), ns2, cv.z, cv.w, D[2],
+                                 D[3]);
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const int j = nt * BN + jt + 4 * u + e;
+                                if (live && j < k && (D[e] - v0) <= thr_of(T0, D[e], v0)) {
+                                    if (cnt < kWideCand / 2) cl[cnt] = j;
+                                    ++cnt;
+                                }
+                            }
+                        }
+                    }
+                    tc_fence_before();
+                    mbar_arrive(&ms.t_empty[tb]);
+                }
+                if (ok && live) ccount[row * 2 + half] = cnt;
+            }
+        } else
         for (long long mt = blockIdx.x; mt < num_mt; mt += gridDim.x) {
             float a0[kClasses], a1[kClasses];
             int i0[kClasses];
@@ -422,10 +480,12 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                     for (int c = 0; c < kClasses; ++c) {
                         const bool in0 = i0[c] >= 0 && (a0[c] - v0) <= thr_of(T0, a0[c], v0);
                         E->c[c] = in0 ? i0[c] : -1;
-                        ovf |= (a1[c] - v0) <= thr_of(T0, a1[c], v0) ? (1 << c) : 0;
+                        ovf |= (a1[c] < INFINITY && (a1[c] - v0) <= thr_of(T0, a1[c], v0)) ? (1 << c) : 0;
                     }
                     E->row = (int)row;
-                    E->ovf[0] = ovf;
+                    E->ovf[0] = (unsigned short)ovf;
+                    E->v0 = v0;
+                    E->T0 = T0;
                 }
             }
             named_bar(bar_id, 64);
@@ -439,9 +499,9 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                     for (int c = 0; c < kClasses; ++c) {
                         const bool in0 = i0[c] >= 0 && (a0[c] - v0) <= thr_of(T0, a0[c], v0);
                         E->c[kClasses + c] = in0 ? i0[c] : -1;
-                        ovf |= (a1[c] - v0) <= thr_of(T0, a1[c], v0) ? (1 << c) : 0;
+                        ovf |= (a1[c] < INFINITY && (a1[c] - v0) <= thr_of(T0, a1[c], v0)) ? (1 << c) : 0;
                     }
-                    E->ovf[1] = ovf;
+                    E->ovf[1] = (unsigned short)ovf;
                 }
             }
         }
@@ -455,27 +515,29 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
     }
 }
 
-template <int BN, int NKC>
+template <int BN, int NKC, bool EMIT>
 cudaError_t launch_t(const AssignArgs& a, cudaStream_t s) {
     using Cf = Cfg<BN, NKC>;
-    auto kern = k_assign_tc<BN, NKC>;
+    auto kern = k_assign_tc<BN, NKC, EMIT>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     const long long num_mt = (a.n + BM - 1) / BM;
     const int grid = (int)(num_mt < a.num_sms ? num_mt : a.num_sms);
     kern<<<grid, kThreads, Cf::SMEM_BYTES, s>>>(*a.tmX, *a.tmC, a.n, a.k, a.dp / KC, a.xnorm, a.cn, a.prm,
-                                                 a.labels, a.list, a.refine, a.bc, a.dbg);
+                                                 a.labels, a.list, a.refine, a.bc, a.dbg,
+                                                 EMIT ? a.wide->went : nullptr, EMIT ? a.wide->cand : nullptr,
+                                                 EMIT ? a.wide->ccount : nullptr);
     return cudaGetLastError();
 }
 
-template <int BN>
+template <int BN, bool EMIT>
 cudaError_t launch_bn(const AssignArgs& a, cudaStream_t s) {
     switch (a.dp / KC) {
-        case 1: return launch_t<BN, 1>(a, s);
-        case 2: return launch_t<BN, 2>(a, s);
-        case 3: return launch_t<BN, 3>(a, s);
-        case 4: return launch_t<BN, 4>(a, s);
-        default: return launch_t<BN, 0>(a, s);      /* d > 256: streaming point chunks */
+        case 1: return launch_t<BN, 1, EMIT>(a, s);
+        case 2: return launch_t<BN, 2, EMIT>(a, s);
+        case 3: return launch_t<BN, 3, EMIT>(a, s);
+        case 4: return launch_t<BN, 4, EMIT>(a, s);
+        default: return launch_t<BN, 0, EMIT>(a, s);      /* d > 256: streaming point chunks */
     }
 }
 
@@ -486,10 +548,15 @@ int assign_supported(int d) { return d >= 1 && d <= kMaxDim; }
 
 cudaError_t launch_assign(const AssignArgs& a, cudaStream_t s) {
     if (a.n <= 0) return cudaSuccess;
+    if (a.emit) {
+        /* the wide path exists only for k > kWideRescan, where the tiles are 256 wide */
+        if (assign_bn_for(a.k) != 256 || !a.wide) return cudaErrorInvalidValue;
+        return launch_bn<256, true>(a, s);
+    }
     switch (assign_bn_for(a.k)) {
-        case 64: return launch_bn<64>(a, s);
-        case 128: return launch_bn<128>(a, s);
-        default: return launch_bn<256>(a, s);
+        case 64: return launch_bn<64, false>(a, s);
+        case 128: return launch_bn<128, false>(a, s);
+        default: return launch_bn<256, false>(a, s);
     }
 }
 

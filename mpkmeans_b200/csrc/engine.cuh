@@ -28,19 +28,42 @@ struct DevParams {
     unsigned int nflag;  /* refinement entries written by the last assign      */
     unsigned long long nflag_total;  /* refinement entries over the run       */
     unsigned long long ncand_total;  /* candidate centroids refined, over run */
-    unsigned long long novf_total;   /* rows refined against all k centroids  */
+    unsigned long long novf_total;   /* rows whose class rescans ran, or whose wide list overflowed */
+    unsigned int nwide;              /* rows handed to the wide refinement by the last assign */
+    unsigned int pad0;
+    unsigned long long nwide_total;  /* wide rows over the run */
 };
 
 /* A row to re-decide in FP32.  The assignment epilogue tracks, per column
  * class (tile half h, column mod 8 = c), the best column and the runner-up
  * value; c[8h + c] is that class's best when it lies within the bound of the
  * row's best, and bit c of ovf[h] is set when the class's runner-up does too
- * (the class may then hold more candidates: all its columns are rescanned). */
+ * (the class may then hold more candidates: all its columns are rescanned,
+ * or, when that would visit too many columns, the row goes wide).  v0 is the
+ * row's best emulated value and T0 the base of its bound. */
 struct RefineEntry {
     int row;
-    int ovf[2];
-    int pad;
+    unsigned short ovf[2];
+    float v0;
+    float T0;
     int c[16];
+};
+static_assert(sizeof(RefineEntry) == 80, "refinement entry layout");
+
+/* Wide refinement.  A flagged row whose overflowing classes hold more than
+ * kWideRescan columns in all is not rescanned class by class: its split
+ * planes are copied to Xw, a second tensor-core pass over those rows emits
+ * every column within the row's bound (up to kWideCand / 2 per tile half),
+ * and the FP32 evaluation visits just those -- or all k when a half's list
+ * overflowed. */
+constexpr int kWideCand = 512;
+constexpr int kWideRescan = 256;
+struct WideScratch {
+    __half* Xw;          /* 2 planes x cap x dp FP16 */
+    int* went;           /* cap: refinement-entry index of each wide slot */
+    int* cand;           /* cap x kWideCand candidate columns */
+    int* ccount;         /* cap x 2: columns found by each tile half */
+    long long cap;       /* 0: no wide path (small k) */
 };
 
 /* Error-bound constants of the assignment filter (host computed). */
@@ -73,6 +96,10 @@ struct AssignArgs {
     BoundConsts bc;
     int num_sms;
     float4* dbg;              /* optional: (v0, v1, j0, j1) per row, test hook */
+    /* emit pass (wide refinement): rows are the first min(prm->nwide, n) of
+     * tmX (then Xw, n = its capacity); candidates go to wide->cand */
+    bool emit;
+    const WideScratch* wide;
 };
 int  assign_bn_for(int k);                   /* N tile width chosen for k     */
 int  assign_supported(int d);                /* 1 when d fits the kernel      */
@@ -81,7 +108,10 @@ cudaError_t launch_assign(const AssignArgs& a, cudaStream_t s);
 /* ---- refine / update (kernels.cu) ---- */
 void launch_refine(const float* P, const float* C, const float* cn, int d, int k, int bn,
                    const RefineEntry* list, DevParams* prm, int* labels, long long n_cap,
-                   unsigned long long* hist_slot, int num_sms, cudaStream_t s);
+                   unsigned long long* hist_slot, const __half* Xs, long long n, int dp, const WideScratch& w,
+                   int num_sms, cudaStream_t s);
+void launch_refine_wide(const float* P, const float* C, const float* cn, int d, int k, const RefineEntry* list,
+                        const WideScratch& w, DevParams* prm, int* labels, int num_sms, cudaStream_t s);
 /* Scratch of the sorted update: perm n ints, bin_start k+1, cursor k, hist k. */
 struct UpdateScratch {
     int* perm;

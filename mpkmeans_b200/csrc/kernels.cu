@@ -182,7 +182,8 @@ __device__ __forceinline__ void eval4(const float (&pr)[NR > 0 ? NR : 1], const 
 template <int NR>
 __global__ void k_refine(const float* __restrict__ P, const float* __restrict__ C, const float* __restrict__ cn,
                          int d, int k, int bn, const RefineEntry* __restrict__ list, DevParams* __restrict__ prm,
-                         int* __restrict__ labels, long long cap, unsigned long long* hist_slot) {
+                         int* __restrict__ labels, long long cap, unsigned long long* hist_slot,
+                         const __half* __restrict__ Xs, long long n, int dp, WideScratch w) {
     constexpr int R = NR > 0 ? NR : 1;
     const int lane = threadIdx.x & 31;
     const long long nf = prm->nflag < (unsigned long long)cap ? (long long)prm->nflag : cap;
@@ -192,6 +193,25 @@ __global__ void k_refine(const float* __restrict__ P, const float* __restrict__ 
     unsigned long long ncand = 0, novf = 0;
     for (long long e = w0; e < nf; e += wstride) {
         const RefineEntry E = list[e];
+        if (w.cap > 0 && (E.ovf[0] | E.ovf[1])) {
+            const int classes = __popc((unsigned)E.ovf[0]) + __popc((unsigned)E.ovf[1]);
+            if ((long long)classes * ((k + 15) / 16) > kWideRescan) {
+                unsigned slot = 0;
+                if (lane == 0) slot = atomicAdd(&prm->nwide, 1u);
+                slot = __shfl_sync(FULL, slot, 0);
+                if ((long long)slot < w.cap) {
+                    /* copy the row's split planes to the wide pass's input */
+                    if (lane == 0) w.went[slot] = (int)e;
+                    const int vec = dp / 8;                          /* 16-byte words per plane row */
+                    for (int p = 0; p < 2; ++p) {
+                        const uint4* src = reinterpret_cast<const uint4*>(Xs + (size_t)p * n * dp + (size_t)E.row * dp);
+                        uint4* dst = reinterpret_cast<uint4*>(w.Xw + (size_t)p * w.cap * dp + (size_t)slot * dp);
+                        for (int v = lane; v < vec; v += 32) dst[v] = src[v];
+                    }
+                    continue;
+                }
+            }
+        }
         const float* p = P + (size_t)E.row * d;
         float pr[R];
 #pragma unroll
@@ -243,6 +263,66 @@ __global__ void k_refine(const float* __restrict__ P, const float* __restrict__ 
         atomicAdd(&prm->nflag_total, (unsigned long long)nf);
         if (hist_slot) *hist_slot = (unsigned long long)nf;
     }
+}
+
+/* One warp per wide row: the FP32 evaluation (same order, same tie rule) of
+ * the columns the emit pass listed, or of all k when a tile half found more
+ * than its kWideCand / 2 slots hold. */
+template <int NR>
+__global__ void k_refine_wide(const float* __restrict__ P, const float* __restrict__ C, const float* __restrict__ cn,
+                              int d, int k, const RefineEntry* __restrict__ list, WideScratch w,
+                              DevParams* __restrict__ prm, int* __restrict__ labels) {
+    constexpr int R = NR > 0 ? NR : 1;
+    const int lane = threadIdx.x & 31;
+    const long long nw0 = (long long)*reinterpret_cast<volatile unsigned int*>(&prm->nwide);
+    const long long nw = nw0 < w.cap ? nw0 : w.cap;
+    const long long wstride = (long long)gridDim.x * (blockDim.x >> 5);
+    const long long w0 = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    unsigned long long ncand = 0, nfull = 0;
+    for (long long s = w0; s < nw; s += wstride) {
+        const int row = list[w.went[s]].row;
+        const float* p = P + (size_t)row * d;
+        float pr[R];
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            const int t = lane + 32 * i;
+            pr[i] = (NR > 0 && t < d) ? p[t] : 0.f;
+        }
+        float bv = INFINITY;
+        int bj = k;
+        int batch[4] = {-1, -1, -1, -1};
+        int nb = 0;
+        auto push = [&](int j) {
+            batch[nb++] = j;
+            if (nb == 4) {
+                eval4<NR>(pr, p, C, cn, d, lane, batch, bv, bj);
+                batch[0] = batch[1] = batch[2] = batch[3] = -1;
+                nb = 0;
+            }
+        };
+        const int c0 = w.ccount[2 * s], c1 = w.ccount[2 * s + 1];
+        constexpr int H = kWideCand / 2;
+        if (c0 > H || c1 > H) {
+            ++nfull;
+#pragma unroll 1
+            for (int j = 0; j < k; ++j) push(j);
+            ncand += (unsigned long long)k;
+        } else {
+            const int* cl = w.cand + (size_t)s * kWideCand;
+#pragma unroll 1
+            for (int i = 0; i < c0; ++i) push(cl[i]);
+#pragma unroll 1
+            for (int i = 0; i < c1; ++i) push(cl[H + i]);
+            ncand += (unsigned long long)(c0 + c1);
+        }
+        if (nb) eval4<NR>(pr, p, C, cn, d, lane, batch, bv, bj);
+        if (lane == 0) labels[row] = bj;
+    }
+    if (lane == 0 && ncand) {
+        atomicAdd(&prm->ncand_total, ncand);
+        if (nfull) atomicAdd(&prm->novf_total, nfull);
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(&prm->nwide_total, (unsigned long long)nw);
 }
 
 /* C_j = (float)((S_j * 2^-frac) / count_j); an empty cluster keeps its old
@@ -361,11 +441,19 @@ void launch_prep_c(const float* C, int k, int kpad, int d, int dp, DevParams* pr
     k_prep_c<<<kpad, 256, 0, s>>>(C, k, d, dp, prm, planes, (long long)k * dp, cn);
 }
 
+void launch_refine_wide(const float* P, const float* C, const float* cn, int d, int k, const RefineEntry* list,
+                        const WideScratch& w, DevParams* prm, int* labels, int num_sms, cudaStream_t s) {
+    if (d <= 256) k_refine_wide<8><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, list, w, prm, labels);
+    else k_refine_wide<0><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, list, w, prm, labels);
+}
+
 void launch_refine(const float* P, const float* C, const float* cn, int d, int k, int bn, const RefineEntry* list,
-                   DevParams* prm, int* labels, long long n_cap, unsigned long long* hist_slot, int num_sms,
-                   cudaStream_t s) {
-    if (d <= 256) k_refine<8><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, bn, list, prm, labels, n_cap, hist_slot);
-    else k_refine<0><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, bn, list, prm, labels, n_cap, hist_slot);
+                   DevParams* prm, int* labels, long long n_cap, unsigned long long* hist_slot, const __half* Xs,
+                   long long n, int dp, const WideScratch& w, int num_sms, cudaStream_t s) {
+    if (d <= 256)
+        k_refine<8><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, bn, list, prm, labels, n_cap, hist_slot, Xs, n, dp, w);
+    else
+        k_refine<0><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, bn, list, prm, labels, n_cap, hist_slot, Xs, n, dp, w);
 }
 
 void launch_finalize_fixed(const long long* sums, const long long* counts, int k, int d, const DevParams* prm,

@@ -156,7 +156,8 @@ struct mpkEngine_s {
     double* dInertia = nullptr;
     unsigned long long* hist = nullptr;   /* MPK_MAX_HIST slots */
     UpdateScratch us{nullptr, nullptr, nullptr, nullptr};
-    CUtensorMap tmX, tmC;
+    CUtensorMap tmX, tmC, tmXw;
+    WideScratch wide{nullptr, nullptr, nullptr, nullptr, 0};
     BoundConsts bc;
     float4* dbg = nullptr;                /* test hook, set by mpkDebugSetAssignTrace */
     bool prof = false;                    /* bench hook: events around the hot kernels */
@@ -183,7 +184,8 @@ static void engine_free(mpkEngine e) {
     if (!e) return;
     prof_clear(e);
     void* bufs[] = {e->Xs, e->xnorm, e->Cs, e->cn, e->list, e->prm, e->dInertia, e->hist,
-                    e->us.perm, e->us.bin_start, e->us.cursor, e->us.hist};
+                    e->us.perm, e->us.bin_start, e->us.cursor, e->us.hist,
+                    e->wide.Xw, e->wide.went, e->wide.cand, e->wide.ccount};
     for (void* b : bufs) dev_free(b, e->s);
     delete e;
 }
@@ -240,6 +242,16 @@ static mpkStatus engine_create(mpkEngine* out, const float* dP, long long n, int
         ALLOC(e->Cs, (size_t)2 * k * e->dp * sizeof(__half));
         ALLOC(e->cn, (size_t)e->kpad * sizeof(float));
         ALLOC(e->list, (size_t)(n > 0 ? n : 1) * sizeof(RefineEntry));
+        /* the wide path: only when some row could need more than kWideRescan
+         * class-rescan columns (16 classes of k/16) */
+        if (k > kWideRescan && n > 0) {
+            const long long cap = std::min<long long>(n, std::max<long long>(65536, n / 16));
+            e->wide.cap = cap;
+            ALLOC(e->wide.Xw, (size_t)2 * cap * e->dp * sizeof(__half));
+            ALLOC(e->wide.went, (size_t)cap * sizeof(int));
+            ALLOC(e->wide.cand, (size_t)cap * kWideCand * sizeof(int));
+            ALLOC(e->wide.ccount, (size_t)cap * 2 * sizeof(int));
+        }
     }
 #undef ALLOC
     cudaMemsetAsync(e->prm, 0, sizeof(DevParams), s);
@@ -264,7 +276,8 @@ static mpkStatus engine_create(mpkEngine* out, const float* dP, long long n, int
             return MPK_ERR_CUDA;
         }
         if ((n > 0 && !make_tmap_planes(&e->tmX, e->Xs, n, e->dp, 128)) ||
-            !make_tmap_planes(&e->tmC, e->Cs, k, e->dp, assign_bn_for(k))) {
+            !make_tmap_planes(&e->tmC, e->Cs, k, e->dp, assign_bn_for(k)) ||
+            (e->wide.cap > 0 && !make_tmap_planes(&e->tmXw, e->wide.Xw, e->wide.cap, e->dp, 128))) {
             fprintf(stderr, "mpkmeans_b200: tensor map encoding failed\n");
             engine_free(e);
             return MPK_ERR_CUDA;
@@ -295,6 +308,7 @@ bool make_tmap_planes(CUtensorMap* map, const __half* base, long long rows, int 
 static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int refine, int hist_it) {
     if (!e->can_assign) return MPK_ERR_INVALID;
     cudaMemsetAsync(&e->prm->nflag, 0, sizeof(unsigned int), e->s);
+    cudaMemsetAsync(&e->prm->nwide, 0, sizeof(unsigned int), e->s);
     launch_prep_c(dC, e->k, e->kpad, e->d, e->dp, e->prm, e->Cs, e->cn, e->s);
     if (e->n == 0) return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
     AssignArgs a;
@@ -314,6 +328,8 @@ static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int r
     a.bc = e->bc;
     a.num_sms = e->num_sms;
     a.dbg = e->dbg;
+    a.emit = false;
+    a.wide = &e->wide;
     prof_mark(e, e->ev_assign);
     cudaError_t err = launch_assign(a, e->s);
     prof_mark(e, e->ev_assign);
@@ -321,9 +337,27 @@ static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int r
         fprintf(stderr, "mpkmeans_b200: assignment launch failed: %s\n", cudaGetErrorString(err));
         return MPK_ERR_CUDA;
     }
-    if (refine)
+    if (refine) {
         launch_refine(e->P, dC, e->cn, e->d, e->k, assign_bn_for(e->k), e->list, e->prm, dAssign, e->n,
-                      (hist_it >= 0 && hist_it < MPK_MAX_HIST) ? e->hist + hist_it : nullptr, e->num_sms, e->s);
+                      (hist_it >= 0 && hist_it < MPK_MAX_HIST) ? e->hist + hist_it : nullptr, e->Xs, e->n, e->dp,
+                      e->wide, e->num_sms, e->s);
+        if (e->wide.cap > 0) {
+            /* rows the refinement handed over: a tensor-core pass that lists their candidates,
+             * then the FP32 evaluation of just those (both size themselves from prm->nwide) */
+            AssignArgs w = a;
+            w.tmX = &e->tmXw;
+            w.n = e->wide.cap;
+            w.labels = nullptr;
+            w.dbg = nullptr;
+            w.emit = true;
+            err = launch_assign(w, e->s);
+            if (err != cudaSuccess) {
+                fprintf(stderr, "mpkmeans_b200: wide assignment launch failed: %s\n", cudaGetErrorString(err));
+                return MPK_ERR_CUDA;
+            }
+            launch_refine_wide(e->P, dC, e->cn, e->d, e->k, e->list, e->wide, e->prm, dAssign, e->num_sms, e->s);
+        }
+    }
     return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
 }
 
@@ -458,6 +492,17 @@ mpkStatus mpkDebugEngineInfo(mpkEngine e, float* scale, float* eta, int* frac, f
     if (frac) *frac = h.frac;
     if (c1) *c1 = e->bc.c1;
     if (c2) *c2 = e->bc.c2;
+    return MPK_OK;
+}
+
+mpkStatus mpkDebugWideCounters(mpkEngine e, long long* wide_rows, long long* full_scans, long long* capacity) {
+    if (!e) return MPK_ERR_INVALID;
+    DevParams h;
+    MPK_TRY(cudaMemcpyAsync(&h, e->prm, sizeof(DevParams), cudaMemcpyDeviceToHost, e->s));
+    MPK_TRY(cudaStreamSynchronize(e->s));
+    if (wide_rows) *wide_rows = (long long)h.nwide_total;
+    if (full_scans) *full_scans = (long long)h.novf_total;
+    if (capacity) *capacity = e->wide.cap;
     return MPK_OK;
 }
 

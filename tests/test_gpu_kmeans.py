@@ -160,6 +160,51 @@ def test_lloyd_d768_bit_exact_vs_oracle(cuda):
     assert np.array_equal(dC.cpu().numpy().view(np.uint32), Cr.view(np.uint32))
 
 
+def _offset_problem(n, d, k, seed, offset=1e3):
+    """Config-5 geometry: a shared offset of norm `offset`, means offset + N(0, 4I),
+    points mean + N(0, I); start centroids are k random points."""
+    rng = np.random.default_rng(seed)
+    o = rng.standard_normal(d)
+    o = o / np.linalg.norm(o) * offset
+    means = o + 2.0 * rng.standard_normal((k, d))
+    P = (means[rng.integers(0, k, n)] + rng.standard_normal((n, d))).astype(np.float32)
+    C = P[rng.choice(n, size=k, replace=False)].copy()
+    return P, C
+
+
+def test_wide_refinement_cancellation_stress(cuda):
+    """Rows whose overflowing classes span more than 256 columns take the wide
+    path (a tensor-core pass listing every column within the bound, then FP32
+    over just those): labels stay bit-exact."""
+    P, C = _offset_problem(20000, 64, 4096, seed=55)
+    dP, dC = dev(P), dev(C)
+    lab = torch.empty(len(P), dtype=torch.int32, device="cuda")
+    with M.Engine(dP, 4096, C0=dC) as e:
+        e.assign(dC, lab, refine=True)
+        torch.cuda.synchronize()
+        w = e.wide_counters()
+    assert w["capacity"] > 0 and w["wide_rows"] > 0, w
+    assert np.array_equal(lab.cpu().numpy(), O.assign_fp32(P, C))
+
+
+def test_wide_refinement_list_overflow_full_scan(cuda):
+    """Every centroid within the bound of every row: the wide lists overflow and
+    those rows are scanned against all k in FP32 -- still the exact argmin."""
+    rng = np.random.default_rng(8)
+    n, d, k = 3000, 32, 1024
+    P = rng.standard_normal((n, d)).astype(np.float32)
+    base = rng.standard_normal(d)
+    C = (base + 1e-6 * rng.standard_normal((k, d))).astype(np.float32)
+    dP, dC = dev(P), dev(C)
+    lab = torch.empty(n, dtype=torch.int32, device="cuda")
+    with M.Engine(dP, k, C0=dC) as e:
+        e.assign(dC, lab, refine=True)
+        torch.cuda.synchronize()
+        w = e.wide_counters()
+    assert w["wide_rows"] > 0 and w["full_scans"] > 0, w
+    assert np.array_equal(lab.cpu().numpy(), O.assign_fp32(P, C))
+
+
 def test_assign_raw_mode_close(cuda):
     P, C = make_problem(8000, 64, 200, seed=9)
     lab, st = gpu_assign(P, C, use_cond3=0, use_cond6=0)
