@@ -178,6 +178,15 @@ mpkStatus mpkLoadLibsvm(const char* path, int* out_n, int* out_d, float** out_P,
 void mpkMakeBlobs(int n, int d, int k, float std, float center_box, unsigned seed, float* hP, int* hLabels);
 mpkStatus mpkInitRandomPoints(const float* dP, int n, int d, int k, unsigned seed, float* dC);
 
+/* k-means++ seeding on the device: k rows of dP (n x d, row major) written to
+ * dC (k x d), D^2-weighted, from `seed`.  No reference counterpart (the
+ * reference seeds with mpkInitRandomPoints only; configuration 1 asks for
+ * k-means++).  Distances are FP64 and the sampling uses exact integer
+ * weights, so the picks do not depend on the launch shape: the same seed gives
+ * the same rows on any device.  Synchronous on the default stream.
+ * MPK_ERR_INVALID unless 0 < k <= n and d > 0. */
+mpkStatus mpkInitKMeansPP(const float* dP, int n, int d, int k, unsigned long long seed, float* dC);
+
 /* ------------------------------------------------ new: explicit steps --- */
 
 /* One assignment pass of the engine: dAssign[i] = argmin_j of the FP32

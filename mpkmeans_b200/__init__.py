@@ -92,6 +92,7 @@ SIGNATURES = {
                            ctypes.POINTER(_I)]),
     "mpkMakeBlobs": (None, [_I, _I, _I, _F, _F, ctypes.c_uint, _P, _P]),
     "mpkInitRandomPoints": (_I, [_P, _I, _I, _I, ctypes.c_uint, _P]),
+    "mpkInitKMeansPP": (_I, [_P, _I, _I, _I, ctypes.c_ulonglong, _P]),
     "mpkAssign": (_I, [_P, _P, _I, _I, _I, _P, _P, _PARAMS, _STATS]),
     "mpkUpdate": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
     "mpkMeansMixedMG": (_I, [_I, _P, _P, _P, _I, _I, _P, _P, _PARAMS, _STATS]),
@@ -208,6 +209,17 @@ def _lloyd(fn_name: str, P, C, labels, params: mpkParams | None, blas: int | Non
             ctypes.byref(params) if params is not None else None, ctypes.byref(st))
     check(fn_name, rc)
     return st
+
+
+def kmeanspp(P, k: int, seed: int, C=None):
+    """k-means++ seeding on the device (mpkInitKMeansPP): k rows of P (n x d,
+    row major, device) into C (k x d, device; allocated when None)."""
+    import torch
+    n, d = P.shape
+    if C is None:
+        C = torch.empty((k, d), dtype=torch.float32, device=P.device)
+    check("mpkInitKMeansPP", lib().mpkInitKMeansPP(_ptr(P), n, d, k, seed, _ptr(C)))
+    return C
 
 
 def means_mixed(P, C, labels, params: mpkParams | None = None, blas: int | None = None) -> mpkStats:

@@ -55,6 +55,7 @@ def lib() -> ctypes.CDLL:
             "orc_make_offset": (None, [_LL, _I, _I, _U64, _D, _VP, _VP]),
             "orc_make_uniform": (None, [_LL, _U64, _I, _f32p]),
             "orc_kmeanspp": (None, [_f32p, _LL, _I, _I, _U64, _f32p]),
+            "orc_kmeanspp_int": (None, [_f32p, _LL, _I, _I, _U64, _f32p, _VP]),
             "orc_make_blobs_ref": (None, [_I, _I, _I, _F, _F, ctypes.c_uint, _VP, _VP]),
             "orc_init_random_idx": (None, [_I, _I, ctypes.c_uint, _i32p]),
             "orc_norm2_tree": (_F, [_f32p, _I]),
@@ -130,6 +131,16 @@ def kmeanspp(P, k, seed):
     C = np.empty((k, d), np.float32)
     lib().orc_kmeanspp(np.ascontiguousarray(P), n, d, k, seed, C)
     return C
+
+
+def kmeanspp_int(P, k, seed):
+    """k-means++ with exact integer sampling (the GPU's mpkInitKMeansPP definition).
+    Returns (C, picked row indices)."""
+    n, d = P.shape
+    C = np.empty((k, d), np.float32)
+    idx = np.empty(k, np.int64)
+    lib().orc_kmeanspp_int(np.ascontiguousarray(P, np.float32), n, d, k, seed, C, _vp(idx))
+    return C, idx
 
 
 def make_blobs_ref(n, d, k, std, box, seed):

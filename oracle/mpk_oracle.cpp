@@ -204,6 +204,75 @@ void orc_kmeanspp(const float* P, int64_t n, int d, int k, uint64_t seed, float*
     }
 }
 
+/* k-means++ with exact integer sampling: the definition mpkInitKMeansPP
+ * implements on the GPU (the reference has no k-means++; configuration 1 asks
+ * for one).  Squared distances are FP64 in warp order: lane l sums
+ * (p_t - c_t)^2 over t = l, l+32, ... with a separate multiply and add, then
+ * a shfl_down tree (16, 8, 4, 2, 1) folds the lanes.  Weights are
+ * w_i = floor(D2_i * 2^q), q = 62 - L - e (n < 2^L, max D2 < 2^e), so their
+ * sum W < 2^62 is exact in any order.  Step c draws u = h3(seed, 41, c) >> 11
+ * (53 bits) and picks the first row whose inclusive prefix of w exceeds
+ * floor(u * W / 2^53); the first centre (and any step with W = 0) takes row
+ * floor(u * n / 2^53).  Writes the k picked rows to C and their indices to
+ * idx (may be NULL). */
+static inline double d2_warp_order(const float* p, const float* c, int d) {
+    double part[32];
+    for (int l = 0; l < 32; ++l) {
+        double a = 0.0;
+        for (int t = l; t < d; t += 32) {
+            const double v = (double)p[t] - (double)c[t];
+            const double sq = v * v;
+            a = a + sq;
+        }
+        part[l] = a;
+    }
+    for (int off = 16; off > 0; off >>= 1)
+        for (int l = 0; l < off; ++l) part[l] = part[l] + part[l + off];
+    return part[0];
+}
+
+static inline uint64_t mul_shift53(uint64_t u53, uint64_t x) {
+    return (uint64_t)(((unsigned __int128)u53 * (unsigned __int128)x) >> 53);
+}
+
+void orc_kmeanspp_int(const float* P, int64_t n, int d, int k, uint64_t seed, float* C, int64_t* idx) {
+    std::vector<double> d2((size_t)n, INFINITY);
+    int L = 0;
+    while (L < 63 && ((uint64_t)n >> L) != 0) ++L;            /* n < 2^L */
+    int64_t pick = (int64_t)mul_shift53(h3(seed, 41, 0) >> 11, (uint64_t)n);
+    for (int c = 0; c < k; ++c) {
+        if (c > 0) {
+            const float* cc = C + (size_t)(c - 1) * d;
+            double M = 0.0;
+#pragma omp parallel for schedule(static) reduction(max : M)
+            for (int64_t i = 0; i < n; ++i) {
+                const double s = d2_warp_order(P + (size_t)i * d, cc, d);
+                if (s < d2[i]) d2[i] = s;
+                if (d2[i] > M) M = d2[i];
+            }
+            const uint64_t u = h3(seed, 41, (uint64_t)c) >> 11;
+            if (M > 0.0) {
+                int e = 0;
+                std::frexp(M, &e);
+                const int q = 62 - L - e;
+                uint64_t W = 0;
+                for (int64_t i = 0; i < n; ++i) W += (uint64_t)std::ldexp(d2[i], q);
+                const uint64_t target = mul_shift53(u, W);
+                uint64_t run = 0;
+                pick = n - 1;
+                for (int64_t i = 0; i < n; ++i) {
+                    run += (uint64_t)std::ldexp(d2[i], q);
+                    if (run > target) { pick = i; break; }
+                }
+            } else {
+                pick = (int64_t)mul_shift53(u, (uint64_t)n);
+            }
+        }
+        std::memcpy(C + (size_t)c * d, P + (size_t)pick * d, sizeof(float) * d);
+        if (idx) idx[c] = pick;
+    }
+}
+
 /* mpkMakeBlobs (kmeans/src/data.cu:12-28): same generator, same draw order, so
  * the same seed gives the reference's points bit for bit under libstdc++. */
 void orc_make_blobs_ref(int n, int d, int k, float stdv, float box, unsigned seed, float* P, int* labels) {

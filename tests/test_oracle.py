@@ -236,3 +236,22 @@ def test_golden_mpemu_gemm_error_model():
             for macs, tol in ((1, 2 ** -9), (3, 2 ** -19)):
                 got = g[f"gemm_fp16_{opa}{opb}_{macs}"].reshape(n, m)
                 assert np.all(np.abs(got - D) <= tol * absAB + 1e-30), (opa, opb, macs)
+
+
+def test_kmeanspp_int_definition():
+    """The integer-sampled k-means++ (the device seeding's definition): first
+    pick floor(u * n / 2^53), no re-picks while weight remains, deterministic,
+    and D^2-proportional: far rows are picked far more often than near ones."""
+    rng = np.random.default_rng(3)
+    P = rng.standard_normal((5000, 16)).astype(np.float32)
+    C, idx = O.kmeanspp_int(P, 40, 123)
+    C2, idx2 = O.kmeanspp_int(P, 40, 123)
+    assert np.array_equal(idx, idx2) and np.array_equal(C, P[idx])
+    assert len(set(idx.tolist())) == 40
+    # two tight groups plus one far point: the far point is always the second pick
+    Q = np.zeros((2001, 4), np.float32)
+    Q[1000:2000] += 0.01
+    Q[2000] = 100.0
+    hits = sum(int(O.kmeanspp_int(Q, 2, s)[1][1] == 2000) for s in range(20))
+    first_far = sum(int(O.kmeanspp_int(Q, 1, s)[1][0] == 2000) for s in range(20))
+    assert hits >= 19 - first_far
