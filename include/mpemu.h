@@ -13,8 +13,12 @@
  * [e, f) gives bit for bit the result of [b, f), as in the reference.
  * The cuBLAS handle is used only for its stream.
  *
- * Out of scope here (the reference's Ozaki-I INT8, workspace context,
- * batched and concatenated-k variants, mpemu.h:412-857).
+ * The workspace context, the batched and the concatenated-k variants
+ * (mpemu.h:589-857) are here too, with the same signatures and struct
+ * layouts, and also run the one-launch kernel: a batched call does not write
+ * its temporary slices, a concatenated call issues no per-bin GEMMs.
+ * Out of scope: the Ozaki-I INT8 (FP64) scheme, mpemu.h:412-586, and its
+ * workspace and batched forms.
  */
 #ifndef MPEMU_B200_H
 #define MPEMU_B200_H
@@ -139,6 +143,102 @@ mpemuStatus_t mpemuGemmMultiword(cublasHandle_t handle, cublasOperation_t opA, c
                                  const __half* dSA, int64_t lda, int64_t strideA, float scaleA,
                                  const __half* dSB, int64_t ldb, int64_t strideB, float scaleB,
                                  int nsplits, int nmacs, float beta, float* dC, int64_t ldc);
+
+/* ---------------------------------------------- workspace context ---- */
+
+/* One growable device arena (mpemu.h:625-638): Reserve grows it with one
+ * allocation (a no-op when it fits), views are carved from it without any. */
+typedef struct mpemuContext_s* mpemuContext_t;
+mpemuStatus_t mpemuContextCreate(mpemuContext_t* ctx);
+mpemuStatus_t mpemuContextDestroy(mpemuContext_t ctx);
+mpemuStatus_t mpemuContextReserve(mpemuContext_t ctx, size_t bytes);
+size_t mpemuContextCapacity(mpemuContext_t ctx);
+void* mpemuContextBase(mpemuContext_t ctx);
+int mpemuContextAllocCount(mpemuContext_t ctx);
+
+/* Arena bytes of the split planes of A (m x k) and B (k x n), mpemu.h:641-642. */
+size_t mpemuBf16WorkspaceBytes(int64_t m, int64_t n, int64_t k, int nsplits);
+size_t mpemuFp16WorkspaceBytes(int64_t m, int64_t n, int64_t k, int nsplits);
+
+/* Views of those planes, mpemu.h:645-655 (same layouts). */
+typedef struct {
+    __nv_bfloat16* sA; int64_t ldA, strideA;
+    __nv_bfloat16* sB; int64_t ldB, strideB;
+    int nsplits;
+} mpemuBf16Workspace_t;
+
+typedef struct {
+    __half* sA; int64_t ldA, strideA;
+    __half* sB; int64_t ldB, strideB;
+    int nsplits;
+} mpemuFp16Workspace_t;
+
+/* Carve the views (mpemu.h:670-677); INVALID_VALUE when the arena is short. */
+mpemuStatus_t mpemuBf16WorkspaceInit(mpemuContext_t ctx, int64_t m, int64_t n, int64_t k, int nsplits,
+                                     mpemuBf16Workspace_t* ws);
+mpemuStatus_t mpemuFp16WorkspaceInit(mpemuContext_t ctx, int64_t m, int64_t n, int64_t k, int nsplits,
+                                     mpemuFp16Workspace_t* ws);
+
+/* ------------------------------------------------------ batched ---- */
+
+/* mpemu.h:714-724, same layout.  The plan arrays are filled as the reference
+ * fills them; the product sum itself runs in the one-launch kernel, so the
+ * temporary slices are never written. */
+typedef struct {
+    void*        tmp;
+    int64_t      ldt, strideT;
+    const void** aptr;
+    const void** bptr;
+    void**       cptr;
+    int*         bins;
+    int          capacity;
+    int          planned;
+    int          elemBytes;
+} mpemuBatchWorkspace_t;
+
+/* mpemu.h:727-737 */
+size_t mpemuBatchWorkspaceBytes(int64_t m, int64_t n, int capacity, int elemBytes);
+mpemuStatus_t mpemuBatchWorkspaceInit(mpemuContext_t ctx, int64_t m, int64_t n, int capacity, int elemBytes,
+                                      size_t arenaOffset, mpemuBatchWorkspace_t* bw);
+
+/* Plan schedule positions [macBegin, macEnd) over split planes at dSA / dSB
+ * (mpemu.h:746-751); synchronises `stream`. */
+mpemuStatus_t mpemuBatchPlan(mpemuBatchWorkspace_t* bw, const void* dSA, int64_t strideA, const void* dSB,
+                             int64_t strideB, int splitElemBytes, int nsplits, int macBegin, int macEnd,
+                             cudaStream_t stream);
+
+/* dC := alpha * sum(planned products [planBegin, planBegin + planCount)) +
+ * beta * dC; A planes have leading dimension mpemuSplitLd(m), B planes
+ * mpemuSplitLd(k), as in the reference (mpemu.h:756-771). */
+mpemuStatus_t mpemuGemmEmulatedBatched(cublasHandle_t handle, cublasOperation_t opA, cublasOperation_t opB,
+                                       int64_t m, int64_t n, int64_t k, float alpha, int planBegin, int planCount,
+                                       float beta, float* dC, int64_t ldc, const mpemuBatchWorkspace_t* bw,
+                                       cudaStream_t stream);
+mpemuStatus_t mpemuGemmMultiwordBatched(cublasHandle_t handle, cublasOperation_t opA, cublasOperation_t opB,
+                                        int64_t m, int64_t n, int64_t k, float alpha, float scaleA, float scaleB,
+                                        int planBegin, int planCount, float beta, float* dC, int64_t ldc,
+                                        const mpemuBatchWorkspace_t* bw, cudaStream_t stream);
+
+/* ------------------------------------------------- concatenated-k ---- */
+
+/* Stacked, reversed right operand: word j of B(r, c) at row (nsplits-1-j)*k
+ * + r of a (nsplits*k) x n column-major buffer (mpemu.h:819-831). */
+int64_t mpemuStackedLd(int64_t k, int nsplits);
+size_t mpemuStackedBytes(int64_t k, int64_t n, int nsplits, int elemBytes);
+mpemuStatus_t mpemuSplitBF16Stacked(const float* dB, int64_t ldb, int64_t k, int64_t n, int nsplits,
+                                    __nv_bfloat16* dS, int64_t lds, cudaStream_t stream);
+mpemuStatus_t mpemuSplitFP16Stacked(const float* dB, int64_t ldb, int64_t k, int64_t n, int nsplits, float scale,
+                                    __half* dS, int64_t lds, cudaStream_t stream);
+
+/* dC := alpha * sum of the products in bins [0, nbins) + beta * dC, op N on
+ * both sides; A's planes sit at column blocks i*k of dSA (mpemu.h:837-851). */
+mpemuStatus_t mpemuGemmEmulatedConcat(cublasHandle_t handle, int64_t m, int64_t n, int64_t k, float alpha,
+                                      const __nv_bfloat16* dSA, int64_t lda, const __nv_bfloat16* dSB, int64_t ldsb,
+                                      int nsplits, int nbins, float beta, float* dC, int64_t ldc);
+mpemuStatus_t mpemuGemmMultiwordConcat(cublasHandle_t handle, int64_t m, int64_t n, int64_t k, float alpha,
+                                       float scaleA, float scaleB, const __half* dSA, int64_t lda,
+                                       const __half* dSB, int64_t ldsb, int nsplits, int nbins, float beta,
+                                       float* dC, int64_t ldc);
 
 #ifdef __cplusplus
 }

@@ -40,6 +40,21 @@ class MpkError(RuntimeError):
         self.status = status
 
 
+class mpemuBatchWorkspace(ctypes.Structure):
+    """mpemuBatchWorkspace_t (include/mpemu.h)."""
+    _fields_ = [("tmp", ctypes.c_void_p), ("ldt", ctypes.c_int64), ("strideT", ctypes.c_int64),
+                ("aptr", ctypes.c_void_p), ("bptr", ctypes.c_void_p), ("cptr", ctypes.c_void_p),
+                ("bins", ctypes.c_void_p), ("capacity", ctypes.c_int), ("planned", ctypes.c_int),
+                ("elemBytes", ctypes.c_int)]
+
+
+class mpemuWorkspace(ctypes.Structure):
+    """mpemuBf16Workspace_t / mpemuFp16Workspace_t (same layout)."""
+    _fields_ = [("sA", ctypes.c_void_p), ("ldA", ctypes.c_int64), ("strideA", ctypes.c_int64),
+                ("sB", ctypes.c_void_p), ("ldB", ctypes.c_int64), ("strideB", ctypes.c_int64),
+                ("nsplits", ctypes.c_int)]
+
+
 class mpkParams(ctypes.Structure):
     _fields_ = [("max_iter", ctypes.c_int), ("tol", ctypes.c_float), ("use_cond3", ctypes.c_int),
                 ("use_cond6", ctypes.c_int), ("cascade", ctypes.c_int), ("accum", ctypes.c_int),
@@ -68,6 +83,7 @@ _I = ctypes.c_int
 _LL = ctypes.c_longlong
 _F = ctypes.c_float
 _D = ctypes.c_double
+_I64 = ctypes.c_int64
 _PARAMS = ctypes.POINTER(mpkParams)
 _STATS = ctypes.POINTER(mpkStats)
 
@@ -138,6 +154,27 @@ SIGNATURES = {
     "mpemuGemmMultiword": (_I, [_P, _I, _I, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _F, _P, ctypes.c_int64,
                                 ctypes.c_int64, _F, _P, ctypes.c_int64, ctypes.c_int64, _F, _I, _I, _F, _P,
                                 ctypes.c_int64]),
+    "mpemuContextCreate": (_I, [ctypes.POINTER(_P)]),
+    "mpemuContextDestroy": (_I, [_P]),
+    "mpemuContextReserve": (_I, [_P, ctypes.c_size_t]),
+    "mpemuContextCapacity": (ctypes.c_size_t, [_P]),
+    "mpemuContextBase": (_P, [_P]),
+    "mpemuContextAllocCount": (_I, [_P]),
+    "mpemuBf16WorkspaceBytes": (ctypes.c_size_t, [_I64, _I64, _I64, _I]),
+    "mpemuFp16WorkspaceBytes": (ctypes.c_size_t, [_I64, _I64, _I64, _I]),
+    "mpemuBf16WorkspaceInit": (_I, [_P, _I64, _I64, _I64, _I, _P]),
+    "mpemuFp16WorkspaceInit": (_I, [_P, _I64, _I64, _I64, _I, _P]),
+    "mpemuBatchWorkspaceBytes": (ctypes.c_size_t, [_I64, _I64, _I, _I]),
+    "mpemuBatchWorkspaceInit": (_I, [_P, _I64, _I64, _I, _I, ctypes.c_size_t, _P]),
+    "mpemuBatchPlan": (_I, [_P, _P, _I64, _P, _I64, _I, _I, _I, _I, _P]),
+    "mpemuGemmEmulatedBatched": (_I, [_P, _I, _I, _I64, _I64, _I64, _F, _I, _I, _F, _P, _I64, _P, _P]),
+    "mpemuGemmMultiwordBatched": (_I, [_P, _I, _I, _I64, _I64, _I64, _F, _F, _F, _I, _I, _F, _P, _I64, _P, _P]),
+    "mpemuStackedLd": (_I64, [_I64, _I]),
+    "mpemuStackedBytes": (ctypes.c_size_t, [_I64, _I64, _I, _I]),
+    "mpemuSplitBF16Stacked": (_I, [_P, _I64, _I64, _I64, _I, _P, _I64, _P]),
+    "mpemuSplitFP16Stacked": (_I, [_P, _I64, _I64, _I64, _I, _F, _P, _I64, _P]),
+    "mpemuGemmEmulatedConcat": (_I, [_P, _I64, _I64, _I64, _F, _P, _I64, _P, _I64, _I, _I, _F, _P, _I64]),
+    "mpemuGemmMultiwordConcat": (_I, [_P, _I64, _I64, _I64, _F, _F, _F, _P, _I64, _P, _I64, _I, _I, _F, _P, _I64]),
     "mpkDebugEngineInfo": (_I, [_P, ctypes.POINTER(_F), ctypes.POINTER(_F), ctypes.POINTER(_I),
                                 ctypes.POINTER(_F), ctypes.POINTER(_F)]),
     "mpkDebugProfile": (_I, [_P, _I]),

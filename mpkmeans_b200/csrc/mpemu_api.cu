@@ -17,6 +17,8 @@
 #include <cmath>
 #include <cstdio>
 #include <mutex>
+#include <unordered_map>
+#include <vector>
 
 using namespace mpk;
 
@@ -202,74 +204,50 @@ bool power_of_two(float a) {
     return std::frexp(a, &e) == 0.5f;
 }
 
-/* Shared driver: dC := alpha * sum over schedule positions [b, e) + beta * dC.
- * Checks follow the reference's order and results: bad split count or range
- * -> INVALID_VALUE; an empty range with beta == 1 succeeds untouched; a
- * missing handle -> INVALID_VALUE (gemm.cu:7-18); a leading dimension cuBLAS
- * would reject -> CUBLAS_ERROR. */
-mpemuStatus_t gemm_range(cublasHandle_t handle, cublasOperation_t opA, cublasOperation_t opB, int64_t m, int64_t n,
-                         int64_t k, float alpha, const void* dSA, int64_t lda, int64_t strideA, const void* dSB,
-                         int64_t ldb, int64_t strideB, int nsplits, int b, int e, float beta, float* dC,
-                         int64_t ldc, bool bf16) {
-    if (nsplits < 1 || nsplits > MPEMU_MAX_SPLITS) return MPEMU_STATUS_INVALID_VALUE;
-    const int total = nsplits * nsplits;
-    if (e == MPEMU_ALL_MACS) e = total;
-    if (b < 0 || e > total || b > e) return MPEMU_STATUS_INVALID_VALUE;
-    if (b == e && beta == 1.0f) return MPEMU_STATUS_SUCCESS;
-    if (!handle || !dC) return MPEMU_STATUS_INVALID_VALUE;
-    if (m < 0 || n < 0 || k < 0) return MPEMU_STATUS_INVALID_VALUE;
-    if (b < e && k > 0 && (!dSA || !dSB)) return MPEMU_STATUS_INVALID_VALUE;
-    if (m == 0 || n == 0) return MPEMU_STATUS_SUCCESS;
-    if (ldc < m) return MPEMU_STATUS_CUBLAS_ERROR;
-    if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return MPEMU_STATUS_INVALID_VALUE;
-    const cudaStream_t s = stream_of(handle);
-    if (b == e || k == 0) {
-        if (beta == 1.0f) return MPEMU_STATUS_SUCCESS;
-        k_scale_c<<<grid_for(m * n), kBlock, 0, s>>>(dC, ldc, (int)m, (int)n, beta);
-        return cudaGetLastError() == cudaSuccess ? MPEMU_STATUS_SUCCESS : MPEMU_STATUS_CUDA_ERROR;
-    }
-    mpemuTerm_t sched[MPEMU_MAX_SPLITS * MPEMU_MAX_SPLITS];
-    mpemuTermSchedule(nsplits, e, sched);
-    GemmTerms terms;
-    terms.n = e - b;
-    for (int t = b; t < e; ++t) {
-        terms.ia[t - b] = sched[t].i;
-        terms.ib[t - b] = sched[t].j;
-    }
-    const bool ta = (opA != CUBLAS_OP_N), tb = (opB != CUBLAS_OP_N);
-    /* stored shapes: A is m x k (op N) or k x m (op T); B is k x n (op N) or n x k (op T) */
-    const int64_t a_rows = ta ? k : m, b_rows = tb ? n : k;
-    if (lda < a_rows || ldb < b_rows) return MPEMU_STATUS_CUBLAS_ERROR;
+/* The planes of one operand: plane p starts p * pstride elements after base;
+ * each is a column-major matrix with leading dimension ld. */
+struct Planes {
+    const void* base;
+    int64_t ld, pstride;
+    int nplanes;
+};
+
+/* dC := alpha * sum_t op(A_{ia[t]}) op(B_{ib[t]}) + beta * dC, terms in order,
+ * one launch.  Shapes and leading dimensions are already validated. */
+mpemuStatus_t run_terms(cudaStream_t s, bool ta, bool tb, int64_t m, int64_t n, int64_t k, float alpha,
+                        const Planes& A, const Planes& B, const GemmTerms& terms, float beta, float* dC,
+                        int64_t ldc, bool bf16) {
     const int init_mode = (power_of_two(alpha) && (beta == 0.f || beta == 1.f)) ? 1 : 0;
-    const bool tma_ok = ((reinterpret_cast<uintptr_t>(dSA) | reinterpret_cast<uintptr_t>(dSB)) % 16 == 0) &&
-                        lda % 8 == 0 && ldb % 8 == 0 && strideA % 8 == 0 && strideB % 8 == 0 &&
-                        (nsplits == 1 || (strideA > 0 && strideB > 0));
+    const bool tma_ok = ((reinterpret_cast<uintptr_t>(A.base) | reinterpret_cast<uintptr_t>(B.base)) % 16 == 0) &&
+                        A.ld % 8 == 0 && B.ld % 8 == 0 && A.pstride % 8 == 0 && B.pstride % 8 == 0 &&
+                        (A.nplanes == 1 || A.pstride > 0) && (B.nplanes == 1 || B.pstride > 0);
     int sms = 0;
     int* status = gemm_status(&sms);
     if (!status) return MPEMU_STATUS_CUDA_ERROR;
-    if (!tma_ok) {
+    CUtensorMap tmA, tmB;
+    const bool a_mn = !ta, b_mn = tb;
+    /* stored shapes: A is m x k (op N) or k x m (op T); B is k x n (op N) or n x k (op T) */
+    bool use_tma = tma_ok;
+    if (use_tma) {
+        const int64_t pa = A.pstride > 0 ? A.pstride : A.ld * (a_mn ? k : m);
+        const int64_t pb = B.pstride > 0 ? B.pstride : B.ld * (b_mn ? k : n);
+        use_tma = (a_mn ? plane_map(&tmA, A.base, bf16, m, k, A.ld, pa, A.nplanes, 64, 64)
+                        : plane_map(&tmA, A.base, bf16, k, m, A.ld, pa, A.nplanes, 64, 128)) &&
+                  (b_mn ? plane_map(&tmB, B.base, bf16, n, k, B.ld, pb, B.nplanes, 64, 64)
+                        : plane_map(&tmB, B.base, bf16, k, n, B.ld, pb, B.nplanes, 64,
+                                    mpk::gemm_tile_n(beta, init_mode)));
+    }
+    if (!use_tma) {
         if (bf16)
             k_gemm_simt<__nv_bfloat16><<<grid_for(m * n), kBlock, 0, s>>>(
-                ta, tb, (int)m, (int)n, (int)k, (const __nv_bfloat16*)dSA, lda, strideA, (const __nv_bfloat16*)dSB,
-                ldb, strideB, terms, alpha, beta, init_mode, dC, ldc);
+                ta, tb, (int)m, (int)n, (int)k, (const __nv_bfloat16*)A.base, A.ld, A.pstride,
+                (const __nv_bfloat16*)B.base, B.ld, B.pstride, terms, alpha, beta, init_mode, dC, ldc);
         else
             k_gemm_simt<__half><<<grid_for(m * n), kBlock, 0, s>>>(ta, tb, (int)m, (int)n, (int)k,
-                                                                   (const __half*)dSA, lda, strideA,
-                                                                   (const __half*)dSB, ldb, strideB, terms, alpha,
-                                                                   beta, init_mode, dC, ldc);
+                                                                   (const __half*)A.base, A.ld, A.pstride,
+                                                                   (const __half*)B.base, B.ld, B.pstride, terms,
+                                                                   alpha, beta, init_mode, dC, ldc);
         return cudaGetLastError() == cudaSuccess ? MPEMU_STATUS_SUCCESS : MPEMU_STATUS_CUDA_ERROR;
-    }
-    CUtensorMap tmA, tmB;
-    const int planes = nsplits;
-    const bool a_mn = !ta, b_mn = tb;
-    const bool okA = a_mn ? plane_map(&tmA, dSA, bf16, m, k, lda, strideA > 0 ? strideA : lda * k, planes, 64, 64)
-                          : plane_map(&tmA, dSA, bf16, k, m, lda, strideA > 0 ? strideA : lda * m, planes, 64, 128);
-    const bool okB = b_mn ? plane_map(&tmB, dSB, bf16, n, k, ldb, strideB > 0 ? strideB : ldb * k, planes, 64, 64)
-                          : plane_map(&tmB, dSB, bf16, k, n, ldb, strideB > 0 ? strideB : ldb * n, planes, 64,
-                                      mpk::gemm_tile_n(beta, init_mode));
-    if (!okA || !okB) {
-        fprintf(stderr, "mpemu: tensor map encoding failed\n");
-        return MPEMU_STATUS_CUDA_ERROR;
     }
     GemmArgs g;
     g.tmA = &tmA;
@@ -291,6 +269,50 @@ mpemuStatus_t gemm_range(cublasHandle_t handle, cublasOperation_t opA, cublasOpe
     return launch_gemm_tc(g, s) == cudaSuccess ? MPEMU_STATUS_SUCCESS : MPEMU_STATUS_CUDA_ERROR;
 }
 
+/* C := beta * C for an empty sum (BLAS semantics; beta == 1 leaves C alone). */
+mpemuStatus_t scale_only(cudaStream_t s, int64_t m, int64_t n, float beta, float* dC, int64_t ldc) {
+    if (beta == 1.0f) return MPEMU_STATUS_SUCCESS;
+    k_scale_c<<<grid_for(m * n), kBlock, 0, s>>>(dC, ldc, (int)m, (int)n, beta);
+    return cudaGetLastError() == cudaSuccess ? MPEMU_STATUS_SUCCESS : MPEMU_STATUS_CUDA_ERROR;
+}
+
+/* Shared driver: dC := alpha * sum over schedule positions [b, e) + beta * dC.
+ * Checks follow the reference's order and results: bad split count or range
+ * -> INVALID_VALUE; an empty range with beta == 1 succeeds untouched; a
+ * missing handle -> INVALID_VALUE (gemm.cu:7-18); a leading dimension cuBLAS
+ * would reject -> CUBLAS_ERROR. */
+mpemuStatus_t gemm_range(cublasHandle_t handle, cublasOperation_t opA, cublasOperation_t opB, int64_t m, int64_t n,
+                         int64_t k, float alpha, const void* dSA, int64_t lda, int64_t strideA, const void* dSB,
+                         int64_t ldb, int64_t strideB, int nsplits, int b, int e, float beta, float* dC,
+                         int64_t ldc, bool bf16) {
+    if (nsplits < 1 || nsplits > MPEMU_MAX_SPLITS) return MPEMU_STATUS_INVALID_VALUE;
+    const int total = nsplits * nsplits;
+    if (e == MPEMU_ALL_MACS) e = total;
+    if (b < 0 || e > total || b > e) return MPEMU_STATUS_INVALID_VALUE;
+    if (b == e && beta == 1.0f) return MPEMU_STATUS_SUCCESS;
+    if (!handle || !dC) return MPEMU_STATUS_INVALID_VALUE;
+    if (m < 0 || n < 0 || k < 0) return MPEMU_STATUS_INVALID_VALUE;
+    if (b < e && k > 0 && (!dSA || !dSB)) return MPEMU_STATUS_INVALID_VALUE;
+    if (m == 0 || n == 0) return MPEMU_STATUS_SUCCESS;
+    if (ldc < m) return MPEMU_STATUS_CUBLAS_ERROR;
+    if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return MPEMU_STATUS_INVALID_VALUE;
+    const cudaStream_t s = stream_of(handle);
+    if (b == e || k == 0) return scale_only(s, m, n, beta, dC, ldc);
+    mpemuTerm_t sched[MPEMU_MAX_SPLITS * MPEMU_MAX_SPLITS];
+    mpemuTermSchedule(nsplits, e, sched);
+    GemmTerms terms;
+    terms.n = e - b;
+    for (int t = b; t < e; ++t) {
+        terms.ia[t - b] = sched[t].i;
+        terms.ib[t - b] = sched[t].j;
+    }
+    const bool ta = (opA != CUBLAS_OP_N), tb = (opB != CUBLAS_OP_N);
+    const int64_t a_rows = ta ? k : m, b_rows = tb ? n : k;
+    if (lda < a_rows || ldb < b_rows) return MPEMU_STATUS_CUBLAS_ERROR;
+    return run_terms(s, ta, tb, m, n, k, alpha, Planes{dSA, lda, strideA, nsplits},
+                     Planes{dSB, ldb, strideB, nsplits}, terms, beta, dC, ldc, bf16);
+}
+
 template <typename W>
 mpemuStatus_t split_impl(const float* dA, int64_t lda, int64_t rows, int64_t cols, int nsplits, float scale,
                          W* dS, int64_t lds, int64_t stride, cudaStream_t s) {
@@ -304,7 +326,148 @@ mpemuStatus_t split_impl(const float* dA, int64_t lda, int64_t rows, int64_t col
     return cudaGetLastError() == cudaSuccess ? MPEMU_STATUS_SUCCESS : MPEMU_STATUS_CUDA_ERROR;
 }
 
+/* Stacked, reversed split of B (k x n): word j of B(r, c) goes to row
+ * (nsplits - 1 - j) * k + r of column c. */
+template <typename W>
+__global__ void k_split_stacked(const float* __restrict__ B, long long ldb, long long k, long long n, int nsplits,
+                                float scale, W* __restrict__ S, long long lds) {
+    const long long total = k * n;
+    const long long step = (long long)gridDim.x * blockDim.x;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += step) {
+        const long long c = e / k, r = e - c * k;
+        float a = B[c * ldb + r] * scale;
+        W* col = S + c * lds + r;
+        for (int j = 0; j < nsplits; ++j) {
+            const W w = to_word<W>(a);
+            col[(long long)(nsplits - 1 - j) * k] = w;
+            a = a - from_word(w);
+        }
+    }
+}
+
+template <typename W>
+mpemuStatus_t split_stacked(const float* dB, int64_t ldb, int64_t k, int64_t n, int nsplits, float scale, W* dS,
+                            int64_t lds, cudaStream_t s) {
+    if (!dB || !dS) return MPEMU_STATUS_INVALID_VALUE;
+    if (k < 0 || n < 0) return MPEMU_STATUS_INVALID_VALUE;
+    if (nsplits < 1 || nsplits > MPEMU_MAX_SPLITS) return MPEMU_STATUS_INVALID_VALUE;
+    if (ldb < k) return MPEMU_STATUS_INVALID_VALUE;
+    if (lds < (int64_t)nsplits * k) return MPEMU_STATUS_INVALID_VALUE;
+    if (!(scale > 0.0f)) return MPEMU_STATUS_INVALID_VALUE;
+    if (k == 0 || n == 0) return MPEMU_STATUS_SUCCESS;
+    k_split_stacked<W><<<grid_for(k * n), kBlock, 0, s>>>(dB, ldb, k, n, nsplits, scale, dS, lds);
+    return cudaGetLastError() == cudaSuccess ? MPEMU_STATUS_SUCCESS : MPEMU_STATUS_CUDA_ERROR;
+}
+
+/* Concatenated-k drivers: the products of bins [0, nbins), B in the stacked
+ * reversed layout, both ops N.  The reference validates in this order
+ * (concat.cu concatGemm); cuBLAS's own argument checks become CUBLAS_ERROR. */
+mpemuStatus_t concat_run(cublasHandle_t handle, int64_t m, int64_t n, int64_t k, float alpha, const void* dSA,
+                         int64_t lda, const void* dSB, int64_t ldsb, int nsplits, int nbins, float beta, float* dC,
+                         int64_t ldc, bool bf16) {
+    if (!handle || !dC || !dSA || !dSB) return MPEMU_STATUS_INVALID_VALUE;
+    if (nsplits < 1 || nbins < 1 || nbins > nsplits) return MPEMU_STATUS_INVALID_VALUE;
+    if (nsplits > MPEMU_MAX_SPLITS) return MPEMU_STATUS_INVALID_VALUE;
+    if (m < 0 || n < 0 || k < 0) return MPEMU_STATUS_CUBLAS_ERROR;
+    if (lda < (m > 1 ? m : 1) || ldsb < (nbins * k > 1 ? nbins * k : 1) || ldc < (m > 1 ? m : 1))
+        return MPEMU_STATUS_CUBLAS_ERROR;
+    if (m == 0 || n == 0) return MPEMU_STATUS_SUCCESS;
+    if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return MPEMU_STATUS_INVALID_VALUE;
+    const cudaStream_t s = stream_of(handle);
+    if (k == 0) return scale_only(s, m, n, beta, dC, ldc);
+    mpemuTerm_t sched[MPEMU_MAX_SPLITS * MPEMU_MAX_SPLITS];
+    const int nt = nbins * (nbins + 1) / 2;      /* bins 0..nbins-1: the schedule's first terms */
+    mpemuTermSchedule(nsplits, nt, sched);
+    GemmTerms terms;
+    terms.n = nt;
+    for (int t = 0; t < nt; ++t) {
+        terms.ia[t] = sched[t].i;
+        terms.ib[t] = nsplits - 1 - sched[t].j;  /* B plane j sits at row block nsplits - 1 - j */
+    }
+    return run_terms(s, false, false, m, n, k, alpha, Planes{dSA, lda, lda * k, nsplits},
+                     Planes{dSB, ldsb, k, nsplits}, terms, beta, dC, ldc, bf16);
+}
+
+/* What mpemuBatchPlan recorded for a workspace, keyed by its pointer arrays'
+ * device address: the batched call needs the plane bases and the term range
+ * on the host to build its one launch. */
+struct PlanRecord {
+    const void* dSA;
+    int64_t strideA;
+    const void* dSB;
+    int64_t strideB;
+    int nsplits, macBegin, count, elemBytes;
+};
+std::mutex g_plan_mu;
+std::unordered_map<const void*, PlanRecord>& plans() {
+    static std::unordered_map<const void*, PlanRecord> p;
+    return p;
+}
+
+mpemuStatus_t batched_run(cublasHandle_t handle, cublasOperation_t opA, cublasOperation_t opB, int64_t m, int64_t n,
+                          int64_t k, float alpha, int planBegin, int planCount, float beta, float* dC, int64_t ldc,
+                          const mpemuBatchWorkspace_t* bw, cudaStream_t stream, bool bf16) {
+    if (!bw || !dC) return MPEMU_STATUS_INVALID_VALUE;
+    if (planBegin < 0 || planCount < 1 || planBegin + planCount > bw->planned) return MPEMU_STATUS_INVALID_VALUE;
+    PlanRecord pr;
+    {
+        std::lock_guard<std::mutex> lock(g_plan_mu);
+        auto it = plans().find((const void*)bw->aptr);
+        if (it == plans().end()) return MPEMU_STATUS_INVALID_VALUE;   /* not planned by mpemuBatchPlan */
+        pr = it->second;
+    }
+    if (pr.elemBytes != 2 || planBegin + planCount > pr.count) return MPEMU_STATUS_INVALID_VALUE;
+    if (!handle) return MPEMU_STATUS_CUBLAS_ERROR;
+    const bool ta = (opA != CUBLAS_OP_N), tb = (opB != CUBLAS_OP_N);
+    const int64_t lda = mpemuSplitLd(m), ldb = mpemuSplitLd(k);
+    if (m < 0 || n < 0 || k < 0) return MPEMU_STATUS_CUBLAS_ERROR;
+    if (lda < (ta ? k : m) || ldb < (tb ? n : k) || ldc < m) return MPEMU_STATUS_CUBLAS_ERROR;
+    if (m == 0 || n == 0) return MPEMU_STATUS_SUCCESS;
+    if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return MPEMU_STATUS_INVALID_VALUE;
+    if (k == 0) return scale_only(stream, m, n, beta, dC, ldc);
+    mpemuTerm_t sched[MPEMU_MAX_TERM_SPLITS * MPEMU_MAX_TERM_SPLITS];
+    const int end = pr.macBegin + planBegin + planCount;
+    if (mpemuTermSchedule(pr.nsplits, end, sched) < end || planCount > 16) return MPEMU_STATUS_INVALID_VALUE;
+    GemmTerms terms;
+    terms.n = planCount;
+    int maxa = 0, maxb = 0;
+    for (int t = 0; t < planCount; ++t) {
+        terms.ia[t] = sched[pr.macBegin + planBegin + t].i;
+        terms.ib[t] = sched[pr.macBegin + planBegin + t].j;
+        maxa = terms.ia[t] > maxa ? terms.ia[t] : maxa;
+        maxb = terms.ib[t] > maxb ? terms.ib[t] : maxb;
+    }
+    return run_terms(stream, ta, tb, m, n, k, alpha, Planes{pr.dSA, lda, pr.strideA, maxa + 1},
+                     Planes{pr.dSB, ldb, pr.strideB, maxb + 1}, terms, beta, dC, ldc, bf16);
+}
+
+constexpr size_t kArenaAlign = 256;
+inline size_t align_up(size_t v) { return (v + kArenaAlign - 1) / kArenaAlign * kArenaAlign; }
+
 }  /* namespace */
+
+struct mpemuContext_s {
+    void* arena;
+    size_t capacity;
+    int allocs;
+};
+
+/* Split-plane views of A (m x k) then B (k x n) from the start of the arena. */
+template <typename WS, typename W>
+static mpemuStatus_t carve_planes(mpemuContext_t ctx, int64_t m, int64_t n, int64_t k, int nsplits, WS* ws) {
+    if (!ctx || !ws || nsplits < 1) return MPEMU_STATUS_INVALID_VALUE;
+    ws->ldA = mpemuSplitLd(m);
+    ws->strideA = ws->ldA * k;
+    ws->ldB = mpemuSplitLd(k);
+    ws->strideB = ws->ldB * n;
+    const size_t a = (size_t)ws->strideA * nsplits * sizeof(W), b = (size_t)ws->strideB * nsplits * sizeof(W);
+    const size_t need = align_up(a) + b;
+    if (!ctx->arena || need > ctx->capacity) return MPEMU_STATUS_INVALID_VALUE;
+    ws->sA = reinterpret_cast<W*>(ctx->arena);
+    ws->sB = reinterpret_cast<W*>(static_cast<char*>(ctx->arena) + align_up(a));
+    ws->nsplits = nsplits;
+    return MPEMU_STATUS_SUCCESS;
+}
 
 extern "C" {
 
@@ -436,6 +599,185 @@ mpemuStatus_t mpemuGemmMultiword(cublasHandle_t handle, cublasOperation_t opA, c
                                  int nsplits, int nmacs, float beta, float* dC, int64_t ldc) {
     return mpemuGemmMultiwordRange(handle, opA, opB, m, n, k, alpha, dSA, lda, strideA, scaleA, dSB, ldb, strideB,
                                    scaleB, nsplits, 0, nmacs, beta, dC, ldc);
+}
+
+
+/* ------------------------------------------------------------ context ---- */
+
+mpemuStatus_t mpemuContextCreate(mpemuContext_t* ctx) {
+    if (!ctx) return MPEMU_STATUS_INVALID_VALUE;
+    *ctx = new (std::nothrow) mpemuContext_s{nullptr, 0, 0};
+    return *ctx ? MPEMU_STATUS_SUCCESS : MPEMU_STATUS_CUDA_ERROR;
+}
+
+mpemuStatus_t mpemuContextDestroy(mpemuContext_t ctx) {
+    if (!ctx) return MPEMU_STATUS_SUCCESS;
+    if (ctx->arena) cudaFree(ctx->arena);
+    delete ctx;
+    return MPEMU_STATUS_SUCCESS;
+}
+
+mpemuStatus_t mpemuContextReserve(mpemuContext_t ctx, size_t bytes) {
+    if (!ctx) return MPEMU_STATUS_INVALID_VALUE;
+    if (bytes <= ctx->capacity) return MPEMU_STATUS_SUCCESS;
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return MPEMU_STATUS_CUDA_ERROR;
+    if (ctx->arena) cudaFree(ctx->arena);
+    ctx->arena = p;
+    ctx->capacity = bytes;
+    ++ctx->allocs;
+    return MPEMU_STATUS_SUCCESS;
+}
+
+size_t mpemuContextCapacity(mpemuContext_t ctx) { return ctx ? ctx->capacity : 0; }
+void* mpemuContextBase(mpemuContext_t ctx) { return ctx ? ctx->arena : nullptr; }
+int mpemuContextAllocCount(mpemuContext_t ctx) { return ctx ? ctx->allocs : 0; }
+
+size_t mpemuBf16WorkspaceBytes(int64_t m, int64_t n, int64_t k, int nsplits) {
+    if (nsplits < 1 || m < 0 || n < 0 || k < 0) return 0;
+    const size_t a = (size_t)mpemuSplitLd(m) * (size_t)k * (size_t)nsplits * 2;
+    const size_t b = (size_t)mpemuSplitLd(k) * (size_t)n * (size_t)nsplits * 2;
+    return align_up(a) + align_up(b);
+}
+
+size_t mpemuFp16WorkspaceBytes(int64_t m, int64_t n, int64_t k, int nsplits) {
+    return mpemuBf16WorkspaceBytes(m, n, k, nsplits);    /* both words are 2 bytes, same layout */
+}
+
+mpemuStatus_t mpemuBf16WorkspaceInit(mpemuContext_t ctx, int64_t m, int64_t n, int64_t k, int nsplits,
+                                     mpemuBf16Workspace_t* ws) {
+    return carve_planes<mpemuBf16Workspace_t, __nv_bfloat16>(ctx, m, n, k, nsplits, ws);
+}
+
+mpemuStatus_t mpemuFp16WorkspaceInit(mpemuContext_t ctx, int64_t m, int64_t n, int64_t k, int nsplits,
+                                     mpemuFp16Workspace_t* ws) {
+    return carve_planes<mpemuFp16Workspace_t, __half>(ctx, m, n, k, nsplits, ws);
+}
+
+/* ------------------------------------------------------------ batched ---- */
+
+size_t mpemuBatchWorkspaceBytes(int64_t m, int64_t n, int capacity, int elemBytes) {
+    if (capacity < 1 || m < 0 || n < 0 || elemBytes < 1) return 0;
+    const int64_t ldt = (m + 15) / 16 * 16;
+    const size_t slices = (size_t)ldt * (size_t)n * (size_t)capacity * (size_t)elemBytes;
+    const size_t ptrs = (size_t)capacity * sizeof(void*);
+    return align_up(slices) + 3 * align_up(ptrs) + align_up((size_t)capacity * sizeof(int));
+}
+
+mpemuStatus_t mpemuBatchWorkspaceInit(mpemuContext_t ctx, int64_t m, int64_t n, int capacity, int elemBytes,
+                                      size_t arenaOffset, mpemuBatchWorkspace_t* bw) {
+    if (!ctx || !bw || capacity < 1 || elemBytes < 1) return MPEMU_STATUS_INVALID_VALUE;
+    const size_t need = mpemuBatchWorkspaceBytes(m, n, capacity, elemBytes);
+    const size_t start = align_up(arenaOffset);
+    if (!ctx->arena || start + need > ctx->capacity) return MPEMU_STATUS_INVALID_VALUE;
+    char* base = static_cast<char*>(ctx->arena) + start;
+    bw->ldt = (m + 15) / 16 * 16;
+    bw->strideT = bw->ldt * n;
+    bw->capacity = capacity;
+    bw->planned = 0;
+    bw->elemBytes = elemBytes;
+    size_t off = 0;
+    bw->tmp = base;
+    off = align_up((size_t)bw->strideT * capacity * elemBytes);
+    bw->aptr = reinterpret_cast<const void**>(base + off);
+    off = align_up(off + (size_t)capacity * sizeof(void*));
+    bw->bptr = reinterpret_cast<const void**>(base + off);
+    off = align_up(off + (size_t)capacity * sizeof(void*));
+    bw->cptr = reinterpret_cast<void**>(base + off);
+    off = align_up(off + (size_t)capacity * sizeof(void*));
+    bw->bins = reinterpret_cast<int*>(base + off);
+    return MPEMU_STATUS_SUCCESS;
+}
+
+mpemuStatus_t mpemuBatchPlan(mpemuBatchWorkspace_t* bw, const void* dSA, int64_t strideA, const void* dSB,
+                             int64_t strideB, int splitElemBytes, int nsplits, int macBegin, int macEnd,
+                             cudaStream_t stream) {
+    if (!bw || !dSA || !dSB || splitElemBytes < 1) return MPEMU_STATUS_INVALID_VALUE;
+    if (macEnd == MPEMU_ALL_MACS) macEnd = mpemuTermCount(nsplits);
+    const int count = macEnd - macBegin;
+    if (macBegin < 0 || count < 1 || count > bw->capacity) return MPEMU_STATUS_INVALID_VALUE;
+    std::vector<mpemuTerm_t> sched((size_t)macEnd);
+    if (mpemuTermSchedule(nsplits, macEnd, sched.data()) < macEnd) return MPEMU_STATUS_INVALID_VALUE;
+    /* the same device arrays the reference fills (plane pointers, slice
+     * pointers, bins), for callers that read them */
+    std::vector<const void*> ha((size_t)count), hb((size_t)count);
+    std::vector<void*> hc((size_t)count);
+    std::vector<int> hbin((size_t)count);
+    for (int t = 0; t < count; ++t) {
+        const mpemuTerm_t& tm = sched[(size_t)(macBegin + t)];
+        ha[t] = static_cast<const char*>(dSA) + (size_t)tm.i * strideA * splitElemBytes;
+        hb[t] = static_cast<const char*>(dSB) + (size_t)tm.j * strideB * splitElemBytes;
+        hc[t] = static_cast<char*>(bw->tmp) + (size_t)t * bw->strideT * bw->elemBytes;
+        hbin[t] = tm.i + tm.j;
+    }
+    const size_t pb = (size_t)count * sizeof(void*);
+    if (cudaMemcpyAsync((void*)bw->aptr, ha.data(), pb, cudaMemcpyHostToDevice, stream) != cudaSuccess ||
+        cudaMemcpyAsync((void*)bw->bptr, hb.data(), pb, cudaMemcpyHostToDevice, stream) != cudaSuccess ||
+        cudaMemcpyAsync((void*)bw->cptr, hc.data(), pb, cudaMemcpyHostToDevice, stream) != cudaSuccess ||
+        cudaMemcpyAsync(bw->bins, hbin.data(), (size_t)count * sizeof(int), cudaMemcpyHostToDevice, stream) !=
+            cudaSuccess)
+        return MPEMU_STATUS_CUDA_ERROR;
+    if (cudaStreamSynchronize(stream) != cudaSuccess) return MPEMU_STATUS_CUDA_ERROR;
+    {
+        std::lock_guard<std::mutex> lock(g_plan_mu);
+        plans()[(const void*)bw->aptr] = PlanRecord{dSA, strideA, dSB, strideB, nsplits, macBegin, count,
+                                                    splitElemBytes};
+    }
+    bw->planned = count;
+    return MPEMU_STATUS_SUCCESS;
+}
+
+mpemuStatus_t mpemuGemmEmulatedBatched(cublasHandle_t handle, cublasOperation_t opA, cublasOperation_t opB,
+                                       int64_t m, int64_t n, int64_t k, float alpha, int planBegin, int planCount,
+                                       float beta, float* dC, int64_t ldc, const mpemuBatchWorkspace_t* bw,
+                                       cudaStream_t stream) {
+    return batched_run(handle, opA, opB, m, n, k, alpha, planBegin, planCount, beta, dC, ldc, bw, stream, true);
+}
+
+mpemuStatus_t mpemuGemmMultiwordBatched(cublasHandle_t handle, cublasOperation_t opA, cublasOperation_t opB,
+                                        int64_t m, int64_t n, int64_t k, float alpha, float scaleA, float scaleB,
+                                        int planBegin, int planCount, float beta, float* dC, int64_t ldc,
+                                        const mpemuBatchWorkspace_t* bw, cudaStream_t stream) {
+    if (!(scaleA > 0.0f) || !(scaleB > 0.0f)) return MPEMU_STATUS_INVALID_VALUE;
+    return batched_run(handle, opA, opB, m, n, k, alpha / (scaleA * scaleB), planBegin, planCount, beta, dC, ldc,
+                       bw, stream, false);
+}
+
+/* ----------------------------------------------------- concatenated-k ---- */
+
+int64_t mpemuStackedLd(int64_t k, int nsplits) {
+    if (nsplits < 1) return 0;
+    return ((int64_t)nsplits * k + 7) / 8 * 8;
+}
+
+size_t mpemuStackedBytes(int64_t k, int64_t n, int nsplits, int elemBytes) {
+    if (nsplits < 1 || elemBytes < 1) return 0;
+    return (size_t)mpemuStackedLd(k, nsplits) * (size_t)n * (size_t)elemBytes;
+}
+
+mpemuStatus_t mpemuSplitBF16Stacked(const float* dB, int64_t ldb, int64_t k, int64_t n, int nsplits,
+                                    __nv_bfloat16* dS, int64_t lds, cudaStream_t stream) {
+    return split_stacked<__nv_bfloat16>(dB, ldb, k, n, nsplits, 1.0f, dS, lds, stream);
+}
+
+mpemuStatus_t mpemuSplitFP16Stacked(const float* dB, int64_t ldb, int64_t k, int64_t n, int nsplits, float scale,
+                                    __half* dS, int64_t lds, cudaStream_t stream) {
+    return split_stacked<__half>(dB, ldb, k, n, nsplits, scale, dS, lds, stream);
+}
+
+mpemuStatus_t mpemuGemmEmulatedConcat(cublasHandle_t handle, int64_t m, int64_t n, int64_t k, float alpha,
+                                      const __nv_bfloat16* dSA, int64_t lda, const __nv_bfloat16* dSB, int64_t ldsb,
+                                      int nsplits, int nbins, float beta, float* dC, int64_t ldc) {
+    return concat_run(handle, m, n, k, alpha, dSA, lda, dSB, ldsb, nsplits, nbins, beta, dC, ldc, true);
+}
+
+mpemuStatus_t mpemuGemmMultiwordConcat(cublasHandle_t handle, int64_t m, int64_t n, int64_t k, float alpha,
+                                       float scaleA, float scaleB, const __half* dSA, int64_t lda,
+                                       const __half* dSB, int64_t ldsb, int nsplits, int nbins, float beta,
+                                       float* dC, int64_t ldc) {
+    if (!(scaleA > 0.0f) || !(scaleB > 0.0f)) return MPEMU_STATUS_INVALID_VALUE;
+    return concat_run(handle, m, n, k, alpha / (scaleA * scaleB), dSA, lda, dSB, ldsb, nsplits, nbins, beta, dC,
+                      ldc, false);
 }
 
 }  /* extern "C" */

@@ -314,3 +314,126 @@ def test_emulated_error_within_twice_native_sgemm(cuda, emax):
     fp = float((dC.reshape(N, N).double() - C64).abs().max())
     assert bf <= 2 * native, (bf, native)
     assert fp <= 2 * native, (fp, native)
+
+
+# ------------------------------------ context, concatenated-k, batched ----
+
+def test_context_arena_and_workspace_views(cuda):
+    L = lib()
+    ctx = ctypes.c_void_p()
+    assert L.mpemuContextCreate(ctypes.byref(ctx)) == OK
+    ws = M.mpemuWorkspace()
+    assert L.mpemuBf16WorkspaceInit(ctx, 100, 60, 40, 3, ctypes.byref(ws)) == 1     # nothing reserved yet
+    need = L.mpemuBf16WorkspaceBytes(100, 60, 40, 3)
+    al = lambda v: (v + 255) // 256 * 256                                          # noqa: E731
+    assert need == al(104 * 40 * 3 * 2) + al(40 * 60 * 3 * 2)
+    assert L.mpemuContextReserve(ctx, need) == OK and L.mpemuContextAllocCount(ctx) == 1
+    assert L.mpemuContextReserve(ctx, need // 2) == OK and L.mpemuContextAllocCount(ctx) == 1   # fits: no-op
+    assert L.mpemuContextCapacity(ctx) == need
+    assert L.mpemuBf16WorkspaceInit(ctx, 100, 60, 40, 3, ctypes.byref(ws)) == OK
+    assert ws.sA == L.mpemuContextBase(ctx) and (ws.sB - ws.sA) % 256 == 0
+    assert (ws.ldA, ws.strideA, ws.ldB, ws.strideB, ws.nsplits) == (104, 104 * 40, 40, 40 * 60, 3)
+    assert L.mpemuFp16WorkspaceInit(ctx, 100, 60, 41, 3, ctypes.byref(ws)) == 1     # needs more than reserved
+    assert L.mpemuContextDestroy(ctx) == OK
+
+
+@pytest.mark.parametrize("m,n,k", [(300, 200, 160), (256, 130, 100), (33, 17, 8)])
+def test_concat_equals_range(cuda, m, n, k):
+    """mpemu.h's concatenated-k drivers (gemm-emulation/bench/test_concat.cu:
+    concat == range within 1e-6): stacked words equal the ordinary split's,
+    and the sum over bins [0, nbins) matches the range over the same products."""
+    L = lib()
+    A = O.make_uniform((k, m), 70 + m)        # column-major m x k
+    B = O.make_uniform((n, k), 71 + n)        # column-major k x n
+    dSA, la, sa = split_gpu(A, m, k, m, 3, True)
+    dSB, lb, sb = split_gpu(B, k, n, k, 3, True)
+    ldsb = L.mpemuStackedLd(k, 3)
+    assert L.mpemuStackedBytes(k, n, 3, 2) == ldsb * n * 2
+    dB = torch.from_numpy(B).cuda()
+    dST = torch.zeros(ldsb * n, dtype=torch.int16, device="cuda")
+    assert L.mpemuSplitBF16Stacked(dB.data_ptr(), k, k, n, 3, dST.data_ptr(), ldsb, None) == OK
+    torch.cuda.synchronize()
+    st = dST.cpu().numpy().reshape(n, ldsb)
+    nrm = dSB.cpu().numpy().reshape(3, n, lb)
+    for j in range(3):
+        assert np.array_equal(st[:, (2 - j) * k:(3 - j) * k], nrm[j, :, :k])
+    exact = np.abs(O.gemm_f64(0, 0, m, n, k, np.abs(A), m, np.abs(B), k)).reshape(n, m)
+    # k % 8 != 0: the stacked planes are not 16-byte aligned for TMA, and the
+    # SIMT path (plain FP32 fmaf chains) stands in; both are within 2^-19 of exact
+    tol = 1e-6 if k % 8 == 0 else 2.0 ** -18
+    for nbins in (1, 2, 3):
+        want = torch.zeros(n * m, dtype=torch.float32, device="cuda")
+        assert gemm_bf16(0, 0, m, n, k, dSA, la, sa, dSB, lb, sb, 3, 0, nbins * (nbins + 1) // 2, want) == OK
+        got = torch.zeros(n * m, dtype=torch.float32, device="cuda")
+        assert L.mpemuGemmEmulatedConcat(handle(), m, n, k, 1.0, dSA.data_ptr(), la, dST.data_ptr(), ldsb, 3,
+                                         nbins, 0.0, got.data_ptr(), m) == OK
+        torch.cuda.synchronize()
+        g, w = got.cpu().numpy().reshape(n, m), want.cpu().numpy().reshape(n, m)
+        assert np.all(np.abs(g - w) <= tol * exact + 1e-30), nbins
+        if k % 8 == 0:
+            assert np.array_equal(g, w)          # same kernel, same products, same order
+    # FP16 multiword concat against its range driver
+    sA, sB = autoscale_gpu(A, m, k, m), autoscale_gpu(B, k, n, k)
+    dHA, la2, sa2 = split_gpu(A, m, k, m, 2, False, sA)
+    dHT = torch.zeros(L.mpemuStackedLd(k, 2) * n, dtype=torch.int16, device="cuda")
+    ld2 = L.mpemuStackedLd(k, 2)
+    assert L.mpemuSplitFP16Stacked(dB.data_ptr(), k, k, n, 2, sB, dHT.data_ptr(), ld2, None) == OK
+    dHB, lb2, sb2 = split_gpu(B, k, n, k, 2, False, sB)
+    want = torch.zeros(n * m, dtype=torch.float32, device="cuda")
+    assert gemm_fp16(0, 0, m, n, k, dHA, la2, sa2, sA, dHB, lb2, sb2, sB, 2, 0, 3, want) == OK
+    got = torch.zeros(n * m, dtype=torch.float32, device="cuda")
+    assert L.mpemuGemmMultiwordConcat(handle(), m, n, k, 1.0, sA, sB, dHA.data_ptr(), la2, dHT.data_ptr(), ld2, 2, 2,
+                                      0.0, got.data_ptr(), m) == OK
+    torch.cuda.synchronize()
+    assert np.all(np.abs(got.cpu().numpy() - want.cpu().numpy()).reshape(n, m) <= tol * exact + 1e-30)
+    # argument checks in the reference's order
+    assert L.mpemuGemmEmulatedConcat(handle(), m, n, k, 1.0, dSA.data_ptr(), la, dST.data_ptr(), ldsb, 3, 4, 0.0,
+                                     got.data_ptr(), m) == 1
+    assert L.mpemuGemmEmulatedConcat(None, m, n, k, 1.0, dSA.data_ptr(), la, dST.data_ptr(), ldsb, 3, 1, 0.0,
+                                     got.data_ptr(), m) == 1
+    assert L.mpemuSplitBF16Stacked(dB.data_ptr(), k, k, n, 3, dST.data_ptr(), 3 * k - 1, None) == 1
+
+
+def test_batched_equals_range(cuda):
+    """The batched drivers take their products from mpemuBatchPlan and give
+    the range driver's result for the same products, bit for bit."""
+    L = lib()
+    m, n, k = 200, 96, 120
+    A = O.make_uniform((k, m), 81)
+    B = O.make_uniform((n, k), 82)
+    dSA, la, sa = split_gpu(A, m, k, m, 3, True)
+    dSB, lb, sb = split_gpu(B, k, n, k, 3, True)
+    ctx = ctypes.c_void_p()
+    assert L.mpemuContextCreate(ctypes.byref(ctx)) == OK
+    assert L.mpemuContextReserve(ctx, L.mpemuBatchWorkspaceBytes(m, n, 9, 4) + 4096) == OK
+    bw = M.mpemuBatchWorkspace()
+    assert L.mpemuBatchWorkspaceInit(ctx, m, n, 9, 4, 1000, ctypes.byref(bw)) == OK
+    assert bw.ldt == 208 and bw.capacity == 9 and bw.planned == 0
+    assert L.mpemuGemmEmulatedBatched(handle(), 0, 0, m, n, k, 1.0, 0, 1, 0.0, dSA.data_ptr(), m,
+                                      ctypes.byref(bw), None) == 1                 # nothing planned yet
+    assert L.mpemuBatchPlan(ctypes.byref(bw), dSA.data_ptr(), sa, dSB.data_ptr(), sb, 2, 3, 0, 6, None) == OK
+    assert bw.planned == 6
+    for begin, count in ((0, 6), (2, 3), (5, 1)):
+        want = torch.zeros(n * m, dtype=torch.float32, device="cuda")
+        assert gemm_bf16(0, 0, m, n, k, dSA, la, sa, dSB, lb, sb, 3, begin, begin + count, want) == OK
+        got = torch.full((n * m,), 7.0, dtype=torch.float32, device="cuda")
+        assert L.mpemuGemmEmulatedBatched(handle(), 0, 0, m, n, k, 1.0, begin, count, 0.0, got.data_ptr(), m,
+                                          ctypes.byref(bw), None) == OK
+        torch.cuda.synchronize()
+        assert torch.equal(got, want), (begin, count)
+    assert L.mpemuGemmEmulatedBatched(handle(), 0, 0, m, n, k, 1.0, 4, 3, 0.0, got.data_ptr(), m,
+                                      ctypes.byref(bw), None) == 1                 # beyond the plan
+    assert L.mpemuBatchPlan(ctypes.byref(bw), dSA.data_ptr(), sa, dSB.data_ptr(), sb, 2, 3, 0, 10, None) == 1
+    # FP16 multiword batched against the multiword range driver
+    sA, sB = autoscale_gpu(A, m, k, m), autoscale_gpu(B, k, n, k)
+    dHA, _, _ = split_gpu(A, m, k, m, 2, False, sA)
+    dHB, _, _ = split_gpu(B, k, n, k, 2, False, sB)
+    assert L.mpemuBatchPlan(ctypes.byref(bw), dHA.data_ptr(), sa, dHB.data_ptr(), sb, 2, 2, 0, 3, None) == OK
+    want = torch.zeros(n * m, dtype=torch.float32, device="cuda")
+    assert gemm_fp16(0, 0, m, n, k, dHA, la, sa, sA, dHB, lb, sb, sB, 2, 0, 3, want) == OK
+    got = torch.zeros(n * m, dtype=torch.float32, device="cuda")
+    assert L.mpemuGemmMultiwordBatched(handle(), 0, 0, m, n, k, 1.0, sA, sB, 0, 3, 0.0, got.data_ptr(), m,
+                                       ctypes.byref(bw), None) == OK
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    assert L.mpemuContextDestroy(ctx) == OK
