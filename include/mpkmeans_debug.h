@@ -26,6 +26,12 @@ mpkStatus mpkDebugEngineInfo(mpkEngine e, float* scale, float* eta, int* frac, f
  * the per-assignment capacity (0: the engine has no wide path, k <= 256). */
 mpkStatus mpkDebugWideCounters(mpkEngine e, long long* wide_rows, long long* full_scans, long long* capacity);
 
+/* Test hook: process the queued wide rows in rounds of at most `rows` (down
+ * from the engine's capacity), to exercise several rounds on small inputs
+ * (k >= 4096; with smaller k there is one round and the rows past it rescan
+ * their classes, which this also exercises). */
+mpkStatus mpkDebugWideRoundRows(mpkEngine e, long long rows);
+
 /* While enabled, the engine records a CUDA event pair on its stream around
  * every assignment kernel and every accumulation (update) kernel launch. */
 mpkStatus mpkDebugProfile(mpkEngine e, int enable);

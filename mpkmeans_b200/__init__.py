@@ -181,6 +181,7 @@ SIGNATURES = {
     "mpkDebugProfileRead": (_I, [_P, ctypes.POINTER(_D), ctypes.POINTER(_LL), ctypes.POINTER(_D),
                                  ctypes.POINTER(_LL)]),
     "mpkDebugWideCounters": (_I, [_P, ctypes.POINTER(_LL), ctypes.POINTER(_LL), ctypes.POINTER(_LL)]),
+    "mpkDebugWideRoundRows": (_I, [_P, _LL]),
 }
 
 _lib = None
@@ -333,6 +334,9 @@ class Engine:
         check("mpkDebugWideCounters", lib().mpkDebugWideCounters(self.h, ctypes.byref(w), ctypes.byref(f),
                                                                  ctypes.byref(c)))
         return {"wide_rows": w.value, "full_scans": f.value, "capacity": c.value}
+
+    def wide_round_rows(self, rows: int) -> None:
+        check("mpkDebugWideRoundRows", lib().mpkDebugWideRoundRows(self.h, rows))
 
     def info(self) -> dict:
         sc, eta, c1, c2 = _F(), _F(), _F(), _F()

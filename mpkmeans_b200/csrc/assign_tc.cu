@@ -128,11 +128,12 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
             long long n, int k, int nkc_rt, const float* __restrict__ xnorm, const float* __restrict__ cn,
             DevParams* __restrict__ prm, int* __restrict__ labels, RefineEntry* __restrict__ list,
             int refine, BoundConsts bc, float4* __restrict__ dbg, const int* __restrict__ went,
-            int* __restrict__ cand, int* __restrict__ ccount) {
+            int* __restrict__ cand, int* __restrict__ ccount, long long wbase) {
     using Cf = Cfg<BN, NKC>;
     if (EMIT) {
-        const long long nw = (long long)*reinterpret_cast<volatile unsigned int*>(&prm->nwide);
-        n = nw < n ? nw : n;
+        /* this round's rows: queued rows [wbase, wbase + n) that exist */
+        const long long nw = (long long)*reinterpret_cast<volatile unsigned int*>(&prm->nwide) - wbase;
+        n = nw < n ? (nw > 0 ? nw : 0) : n;
     }
     static_assert(Cf::A_BUFS <= 4, "A ring");
     const int nkc = Cf::STREAM ? nkc_rt : NKC;   /* K chunks of 64 */
@@ -331,7 +332,7 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                 const bool live = row < n;
                 float v0 = INFINITY, T0 = 0.f;
                 if (live) {
-                    const RefineEntry* E = list + went[row];
+                    const RefineEntry* E = list + went[wbase + row];
                     v0 = E->v0;
                     T0 = E->T0;
                 }
@@ -526,7 +527,7 @@ cudaError_t launch_t(const AssignArgs& a, cudaStream_t s) {
     kern<<<grid, kThreads, Cf::SMEM_BYTES, s>>>(*a.tmX, *a.tmC, a.n, a.k, a.dp / KC, a.xnorm, a.cn, a.prm,
                                                  a.labels, a.list, a.refine, a.bc, a.dbg,
                                                  EMIT ? a.wide->went : nullptr, EMIT ? a.wide->cand : nullptr,
-                                                 EMIT ? a.wide->ccount : nullptr);
+                                                 EMIT ? a.wide->ccount : nullptr, EMIT ? a.wbase : 0);
     return cudaGetLastError();
 }
 

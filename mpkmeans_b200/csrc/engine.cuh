@@ -51,19 +51,23 @@ struct RefineEntry {
 static_assert(sizeof(RefineEntry) == 80, "refinement entry layout");
 
 /* Wide refinement.  A flagged row whose overflowing classes hold more than
- * kWideRescan columns in all is not rescanned class by class: its split
- * planes are copied to Xw, a second tensor-core pass over those rows emits
- * every column within the row's bound (up to kWideCand / 2 per tile half),
- * and the FP32 evaluation visits just those -- or all k when a half's list
- * overflowed. */
+ * kWideRescan columns in all is not rescanned class by class: it is queued
+ * (went), and in rounds of `cap` rows its split planes are copied to Xw, a
+ * second tensor-core pass over those rows emits every column within the
+ * row's bound (up to kWideCand / 2 per tile half), and the FP32 evaluation
+ * visits just those -- or all k when a half's list overflowed.  Every round
+ * sizes itself from prm->nwide on the device; rounds past the queue exit at
+ * once. */
 constexpr int kWideCand = 512;
 constexpr int kWideRescan = 256;
 struct WideScratch {
-    __half* Xw;          /* 2 planes x cap x dp FP16 */
-    int* went;           /* cap: refinement-entry index of each wide slot */
+    __half* Xw;          /* 2 planes x cap x dp FP16: one round's rows */
+    int* went;           /* n: refinement-entry index of each queued row */
     int* cand;           /* cap x kWideCand candidate columns */
     int* ccount;         /* cap x 2: columns found by each tile half */
-    long long cap;       /* 0: no wide path (small k) */
+    long long cap;       /* rows Xw holds (its plane stride); 0: no wide path (small k) */
+    long long per_round; /* rows per round, <= cap */
+    int rounds;          /* rounds per assignment; queued rows past them rescan their classes */
 };
 
 /* Error-bound constants of the assignment filter (host computed). */
@@ -100,6 +104,7 @@ struct AssignArgs {
      * tmX (then Xw, n = its capacity); candidates go to wide->cand */
     bool emit;
     const WideScratch* wide;
+    long long wbase;          /* emit pass: first queued row of this round */
 };
 int  assign_bn_for(int k);                   /* N tile width chosen for k     */
 int  assign_supported(int d);                /* 1 when d fits the kernel      */
@@ -110,8 +115,11 @@ void launch_refine(const float* P, const float* C, const float* cn, int d, int k
                    const RefineEntry* list, DevParams* prm, int* labels, long long n_cap,
                    unsigned long long* hist_slot, const __half* Xs, long long n, int dp, const WideScratch& w,
                    int num_sms, cudaStream_t s);
+void launch_wide_gather(const RefineEntry* list, const __half* Xs, long long n, int dp, const WideScratch& w,
+                        long long base, const DevParams* prm, int num_sms, cudaStream_t s);
 void launch_refine_wide(const float* P, const float* C, const float* cn, int d, int k, const RefineEntry* list,
-                        const WideScratch& w, DevParams* prm, int* labels, int num_sms, cudaStream_t s);
+                        const WideScratch& w, long long base, DevParams* prm, int* labels, int num_sms,
+                        cudaStream_t s);
 /* Scratch of the sorted update: perm n ints, bin_start k+1, cursor k, hist k. */
 struct UpdateScratch {
     int* perm;

@@ -175,6 +175,28 @@ __device__ __forceinline__ void eval4(const float (&pr)[NR > 0 ? NR : 1], const 
     }
 }
 
+/* A warp copies row `row`'s two split-plane rows into slot `slot` of Xw. */
+__device__ __forceinline__ void copy_planes(const __half* __restrict__ Xs, long long n, int dp, int row,
+                                            const WideScratch& w, long long slot, int lane) {
+    const int vec = dp / 8;                              /* 16-byte words per plane row */
+    for (int p = 0; p < 2; ++p) {
+        const uint4* src = reinterpret_cast<const uint4*>(Xs + (size_t)p * n * dp + (size_t)row * dp);
+        uint4* dst = reinterpret_cast<uint4*>(w.Xw + (size_t)p * w.cap * dp + (size_t)slot * dp);
+        for (int v = lane; v < vec; v += 32) dst[v] = src[v];
+    }
+}
+
+/* Rounds after the first: copy queued rows [base, base + per_round) to Xw. */
+__global__ void k_wide_gather(const RefineEntry* __restrict__ list, const __half* __restrict__ Xs, long long n,
+                              int dp, WideScratch w, long long base, const DevParams* __restrict__ prm) {
+    const long long nw = (long long)*reinterpret_cast<const volatile unsigned int*>(&prm->nwide);
+    const long long cnt = min(w.per_round, nw - base);
+    const int lane = threadIdx.x & 31;
+    const long long wstride = (long long)gridDim.x * (blockDim.x >> 5);
+    for (long long l = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); l < cnt; l += wstride)
+        copy_planes(Xs, n, dp, list[w.went[base + l]].row, w, l, lane);
+}
+
 /* One warp per refinement entry: the listed candidates, then every column of
  * each overflowing class, in batches of four; the label is the smallest FP32
  * distance, the smaller index on a tie.  Control flow is warp uniform (every
@@ -197,19 +219,14 @@ __global__ void k_refine(const float* __restrict__ P, const float* __restrict__ 
             const int classes = __popc((unsigned)E.ovf[0]) + __popc((unsigned)E.ovf[1]);
             if ((long long)classes * ((k + 15) / 16) > kWideRescan) {
                 unsigned slot = 0;
-                if (lane == 0) slot = atomicAdd(&prm->nwide, 1u);
-                slot = __shfl_sync(FULL, slot, 0);
-                if ((long long)slot < w.cap) {
-                    /* copy the row's split planes to the wide pass's input */
-                    if (lane == 0) w.went[slot] = (int)e;
-                    const int vec = dp / 8;                          /* 16-byte words per plane row */
-                    for (int p = 0; p < 2; ++p) {
-                        const uint4* src = reinterpret_cast<const uint4*>(Xs + (size_t)p * n * dp + (size_t)E.row * dp);
-                        uint4* dst = reinterpret_cast<uint4*>(w.Xw + (size_t)p * w.cap * dp + (size_t)slot * dp);
-                        for (int v = lane; v < vec; v += 32) dst[v] = src[v];
-                    }
-                    continue;
+                if (lane == 0) {
+                    slot = atomicAdd(&prm->nwide, 1u);
+                    w.went[slot] = (int)e;                       /* slot < n: one entry per row at most */
                 }
+                slot = __shfl_sync(FULL, slot, 0);
+                if ((long long)slot < w.per_round) copy_planes(Xs, n, dp, E.row, w, slot, lane);  /* round 0 */
+                if ((long long)slot < w.per_round * w.rounds) continue;
+                /* past the last round: rescan its classes here */
             }
         }
         const float* p = P + (size_t)E.row * d;
@@ -270,17 +287,17 @@ __global__ void k_refine(const float* __restrict__ P, const float* __restrict__ 
  * than its kWideCand / 2 slots hold. */
 template <int NR>
 __global__ void k_refine_wide(const float* __restrict__ P, const float* __restrict__ C, const float* __restrict__ cn,
-                              int d, int k, const RefineEntry* __restrict__ list, WideScratch w,
+                              int d, int k, const RefineEntry* __restrict__ list, WideScratch w, long long base,
                               DevParams* __restrict__ prm, int* __restrict__ labels) {
     constexpr int R = NR > 0 ? NR : 1;
     const int lane = threadIdx.x & 31;
-    const long long nw0 = (long long)*reinterpret_cast<volatile unsigned int*>(&prm->nwide);
-    const long long nw = nw0 < w.cap ? nw0 : w.cap;
+    const long long nw0 = (long long)*reinterpret_cast<volatile unsigned int*>(&prm->nwide) - base;
+    const long long nw = nw0 < w.per_round ? (nw0 > 0 ? nw0 : 0) : w.per_round;
     const long long wstride = (long long)gridDim.x * (blockDim.x >> 5);
     const long long w0 = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     unsigned long long ncand = 0, nfull = 0;
     for (long long s = w0; s < nw; s += wstride) {
-        const int row = list[w.went[s]].row;
+        const int row = list[w.went[base + s]].row;
         const float* p = P + (size_t)row * d;
         float pr[R];
 #pragma unroll
@@ -322,7 +339,7 @@ __global__ void k_refine_wide(const float* __restrict__ P, const float* __restri
         atomicAdd(&prm->ncand_total, ncand);
         if (nfull) atomicAdd(&prm->novf_total, nfull);
     }
-    if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(&prm->nwide_total, (unsigned long long)nw);
+    if (blockIdx.x == 0 && threadIdx.x == 0 && nw > 0) atomicAdd(&prm->nwide_total, (unsigned long long)nw);
 }
 
 /* C_j = (float)((S_j * 2^-frac) / count_j); an empty cluster keeps its old
@@ -441,10 +458,16 @@ void launch_prep_c(const float* C, int k, int kpad, int d, int dp, DevParams* pr
     k_prep_c<<<kpad, 256, 0, s>>>(C, k, d, dp, prm, planes, (long long)k * dp, cn);
 }
 
+void launch_wide_gather(const RefineEntry* list, const __half* Xs, long long n, int dp, const WideScratch& w,
+                        long long base, const DevParams* prm, int num_sms, cudaStream_t s) {
+    k_wide_gather<<<num_sms * 4, 256, 0, s>>>(list, Xs, n, dp, w, base, prm);
+}
+
 void launch_refine_wide(const float* P, const float* C, const float* cn, int d, int k, const RefineEntry* list,
-                        const WideScratch& w, DevParams* prm, int* labels, int num_sms, cudaStream_t s) {
-    if (d <= 256) k_refine_wide<8><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, list, w, prm, labels);
-    else k_refine_wide<0><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, list, w, prm, labels);
+                        const WideScratch& w, long long base, DevParams* prm, int* labels, int num_sms,
+                        cudaStream_t s) {
+    if (d <= 256) k_refine_wide<8><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, list, w, base, prm, labels);
+    else k_refine_wide<0><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, list, w, base, prm, labels);
 }
 
 void launch_refine(const float* P, const float* C, const float* cn, int d, int k, int bn, const RefineEntry* list,

@@ -157,7 +157,7 @@ struct mpkEngine_s {
     unsigned long long* hist = nullptr;   /* MPK_MAX_HIST slots */
     UpdateScratch us{nullptr, nullptr, nullptr, nullptr};
     CUtensorMap tmX, tmC, tmXw;
-    WideScratch wide{nullptr, nullptr, nullptr, nullptr, 0};
+    WideScratch wide{nullptr, nullptr, nullptr, nullptr, 0, 0, 0};
     BoundConsts bc;
     float4* dbg = nullptr;                /* test hook, set by mpkDebugSetAssignTrace */
     bool prof = false;                    /* bench hook: events around the hot kernels */
@@ -245,10 +245,14 @@ static mpkStatus engine_create(mpkEngine* out, const float* dP, long long n, int
         /* the wide path: only when some row could need more than kWideRescan
          * class-rescan columns (16 classes of k/16) */
         if (k > kWideRescan && n > 0) {
-            const long long cap = std::min<long long>(n, std::max<long long>(65536, n / 16));
+            const long long cap = std::min<long long>(n, std::max<long long>(65536, (n + 7) / 8));
             e->wide.cap = cap;
+            e->wide.per_round = cap;
+            /* every queued row gets a round when classes are wide (k >= 4096: 256+ columns a
+             * class); below that one round, and rows past it rescan their classes */
+            e->wide.rounds = k >= 4096 ? (int)((n + cap - 1) / cap) : 1;
             ALLOC(e->wide.Xw, (size_t)2 * cap * e->dp * sizeof(__half));
-            ALLOC(e->wide.went, (size_t)cap * sizeof(int));
+            ALLOC(e->wide.went, (size_t)n * sizeof(int));
             ALLOC(e->wide.cand, (size_t)cap * kWideCand * sizeof(int));
             ALLOC(e->wide.ccount, (size_t)cap * 2 * sizeof(int));
         }
@@ -330,6 +334,7 @@ static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int r
     a.dbg = e->dbg;
     a.emit = false;
     a.wide = &e->wide;
+    a.wbase = 0;
     prof_mark(e, e->ev_assign);
     cudaError_t err = launch_assign(a, e->s);
     prof_mark(e, e->ev_assign);
@@ -341,21 +346,26 @@ static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int r
         launch_refine(e->P, dC, e->cn, e->d, e->k, assign_bn_for(e->k), e->list, e->prm, dAssign, e->n,
                       (hist_it >= 0 && hist_it < MPK_MAX_HIST) ? e->hist + hist_it : nullptr, e->Xs, e->n, e->dp,
                       e->wide, e->num_sms, e->s);
-        if (e->wide.cap > 0) {
-            /* rows the refinement handed over: a tensor-core pass that lists their candidates,
-             * then the FP32 evaluation of just those (both size themselves from prm->nwide) */
+        /* rows the refinement queued: per round, a tensor-core pass that lists their
+         * candidates, then the FP32 evaluation of just those (every launch sizes itself from
+         * prm->nwide; rounds past the queue exit at once) */
+        for (int r = 0; r < e->wide.rounds; ++r) {
+            const long long base = (long long)r * e->wide.per_round;
+            if (r > 0) launch_wide_gather(e->list, e->Xs, e->n, e->dp, e->wide, base, e->prm, e->num_sms, e->s);
             AssignArgs w = a;
             w.tmX = &e->tmXw;
-            w.n = e->wide.cap;
+            w.n = e->wide.per_round;
             w.labels = nullptr;
             w.dbg = nullptr;
             w.emit = true;
+            w.wbase = base;
             err = launch_assign(w, e->s);
             if (err != cudaSuccess) {
                 fprintf(stderr, "mpkmeans_b200: wide assignment launch failed: %s\n", cudaGetErrorString(err));
                 return MPK_ERR_CUDA;
             }
-            launch_refine_wide(e->P, dC, e->cn, e->d, e->k, e->list, e->wide, e->prm, dAssign, e->num_sms, e->s);
+            launch_refine_wide(e->P, dC, e->cn, e->d, e->k, e->list, e->wide, base, e->prm, dAssign, e->num_sms,
+                               e->s);
         }
     }
     return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
@@ -492,6 +502,13 @@ mpkStatus mpkDebugEngineInfo(mpkEngine e, float* scale, float* eta, int* frac, f
     if (frac) *frac = h.frac;
     if (c1) *c1 = e->bc.c1;
     if (c2) *c2 = e->bc.c2;
+    return MPK_OK;
+}
+
+mpkStatus mpkDebugWideRoundRows(mpkEngine e, long long rows) {
+    if (!e || rows < 1 || e->wide.cap == 0) return MPK_ERR_INVALID;
+    e->wide.per_round = std::min(rows, e->wide.cap);
+    e->wide.rounds = e->k >= 4096 ? (int)((e->n + e->wide.per_round - 1) / e->wide.per_round) : 1;
     return MPK_OK;
 }
 

@@ -184,7 +184,17 @@ def test_wide_refinement_cancellation_stress(cuda):
         torch.cuda.synchronize()
         w = e.wide_counters()
     assert w["capacity"] > 0 and w["wide_rows"] > 0, w
-    assert np.array_equal(lab.cpu().numpy(), O.assign_fp32(P, C))
+    ref = O.assign_fp32(P, C)
+    assert np.array_equal(lab.cpu().numpy(), ref)
+    # the same in rounds of 97 queued rows
+    lab2 = torch.empty(len(P), dtype=torch.int32, device="cuda")
+    with M.Engine(dP, 4096, C0=dC) as e:
+        e.wide_round_rows(97)
+        e.assign(dC, lab2, refine=True)
+        torch.cuda.synchronize()
+        w2 = e.wide_counters()
+    assert w2["wide_rows"] == w["wide_rows"] > 97, (w, w2)
+    assert np.array_equal(lab2.cpu().numpy(), ref)
 
 
 def test_wide_refinement_list_overflow_full_scan(cuda):
@@ -202,7 +212,15 @@ def test_wide_refinement_list_overflow_full_scan(cuda):
         torch.cuda.synchronize()
         w = e.wide_counters()
     assert w["wide_rows"] > 0 and w["full_scans"] > 0, w
-    assert np.array_equal(lab.cpu().numpy(), O.assign_fp32(P, C))
+    ref = O.assign_fp32(P, C)
+    assert np.array_equal(lab.cpu().numpy(), ref)
+    # k < 4096: one round of 50 rows; the queued rows past it rescan their classes
+    lab2 = torch.empty(n, dtype=torch.int32, device="cuda")
+    with M.Engine(dP, k, C0=dC) as e:
+        e.wide_round_rows(50)
+        e.assign(dC, lab2, refine=True)
+        torch.cuda.synchronize()
+    assert np.array_equal(lab2.cpu().numpy(), ref)
 
 
 def test_assign_raw_mode_close(cuda):
