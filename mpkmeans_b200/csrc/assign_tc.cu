@@ -330,11 +330,19 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
             for (long long mt = blockIdx.x; mt < num_mt; mt += gridDim.x) {
                 const long long row = mt * BM + r_loc;
                 const bool live = row < n;
-                float v0 = INFINITY, T0 = 0.f;
+                /* Every column the filter could admit, (D - v0) <= thr_of(T0, D, v0), has
+                 * D <= Dmax: with g = D - v0 >= 0 and |D| <= |v0| + g the admission test
+                 * implies g <= (T0 + 2^-21 |v0|)(1 + 2^-20) / (1 - 2^-22 (1 + 2^-20)); the
+                 * 2^-16 inflation and two ulps cover the FP32 evaluation of both sides.
+                 * One compare per element instead of the threshold arithmetic. */
+                float Dmax = -INFINITY;
                 if (live) {
                     const RefineEntry* E = list + went[wbase + row];
-                    v0 = E->v0;
-                    T0 = E->T0;
+                    const float v0 = E->v0, T0 = E->T0;
+                    const float G = (T0 + 0x1.0p-21f * fabsf(v0)) * (1.0f + 0x1.0p-20f) /
+                                    (1.0f - 0x1.0p-22f * (1.0f + 0x1.0p-20f));
+                    Dmax = v0 + G * (1.0f + 0x1.0p-16f);
+                    Dmax = nextafterf(nextafterf(Dmax, INFINITY), INFINITY);
                 }
                 int* cl = cand + (size_t)(live ? row : 0) * kWideCand + half * (kWideCand / 2);
                 int cnt = 0;
@@ -361,10 +369,12 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                                  D[3]);
 #pragma unroll
                             for (int e = 0; e < 4; ++e) {
-                                const int j = nt * BN + jt + 4 * u + e;
-                                if (live && j < k && (D[e] - v0) <= thr_of(T0, D[e], v0)) {
-                                    if (cnt < kWideCand / 2) cl[cnt] = j;
-                                    ++cnt;
+                                if (D[e] <= Dmax) {
+                                    const int j = nt * BN + jt + 4 * u + e;
+                                    if (j < k) {
+                                        if (cnt < kWideCand / 2) cl[cnt] = j;
+                                        ++cnt;
+                                    }
                                 }
                             }
                         }
