@@ -591,7 +591,13 @@ def main():
         u_ms = prof["accum_ms"] / max(1, prof["accum_launches"])
         flops = 2.0 * n_local * K * D * 3
         achieved = flops / (a_ms / 1e3) / 1e12
-        traffic = profile_figure("assign_tc_config3.md", "dram_bytes_per_launch") if args.workload == "config3" else None
+        # DRAM bytes of one assignment launch, from the committed ncu summary of this workload (recorded
+        # for the N = 1 shard; traffic grows with the rows, so it is scaled to this rank's rows)
+        prof_ref = {"config3": ("assign_tc_config3.md", N_FULL), "config4": ("assign_tc_config4.md", 6_250_000)}
+        traffic = None
+        if args.workload in prof_ref:
+            fig = profile_figure(prof_ref[args.workload][0], "dram_bytes_per_launch")
+            traffic = fig * n_local / prof_ref[args.workload][1] if fig else None
         ubytes = n_local * D * 4 + n_local * 4
         u_gbs = ubytes / (u_ms / 1e3) / 1e9
         line = {
