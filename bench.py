@@ -76,8 +76,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--n", type=int, default=None,
-                    help="total points of the configuration (default: the configuration's n)")
+    ap.add_argument("--points", "--n", dest="n", type=int, default=None,
+                    help="total points of the configuration (default: the configuration's n); under torchrun "
+                         "spell it --points (torchrun's parser takes --n for its own --nnodes)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-sgemm", action="store_true", help="skip the config-2 emulated SGEMM section")
