@@ -26,6 +26,23 @@ mpkStatus mpkDebugEngineInfo(mpkEngine e, float* scale, float* eta, int* frac, f
  * the per-assignment capacity (0: the engine has no wide path, k <= 256). */
 mpkStatus mpkDebugWideCounters(mpkEngine e, long long* wide_rows, long long* full_scans, long long* capacity);
 
+/* Failure-path test hooks.  SetWaitLimit bounds every wait of the engine's
+ * assignment kernel by `ns` (0: the default 4 s).  InjectStall makes the
+ * kernel's producer leave centroid-plane stage `stage` (counted per CTA from
+ * 0) unloaded on every later assignment (-1: none), so the MMA issuer's wait
+ * on it runs out: the kernel sets MPK_DEV_TIMEOUT (bit 0 of the status that
+ * mpkEngineCounters reports), winds down and returns, and the context stays
+ * usable.  ClearStatus zeroes the engine's device status word. */
+mpkStatus mpkDebugSetWaitLimit(mpkEngine e, unsigned long long ns);
+mpkStatus mpkDebugInjectStall(mpkEngine e, int stage);
+mpkStatus mpkDebugClearStatus(mpkEngine e);
+
+/* The emulated GEMM's device status word on the current device (bit 0: a
+ * bounded wait inside the kernel ran out and the call's output is invalid);
+ * synchronises the device; clears the word when `clear` is non-zero.
+ * Returns -1 when the word cannot be read.  No reference counterpart. */
+int mpkDebugGemmStatus(int clear);
+
 /* Test hook: process the queued wide rows in rounds of at most `rows` (down
  * from the engine's capacity), to exercise several rounds on small inputs
  * (k >= 4096; with smaller k there is one round and the rows past it rescan

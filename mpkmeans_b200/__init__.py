@@ -182,6 +182,10 @@ SIGNATURES = {
                                  ctypes.POINTER(_LL)]),
     "mpkDebugWideCounters": (_I, [_P, ctypes.POINTER(_LL), ctypes.POINTER(_LL), ctypes.POINTER(_LL)]),
     "mpkDebugWideRoundRows": (_I, [_P, _LL]),
+    "mpkDebugGemmStatus": (_I, [_I]),
+    "mpkDebugSetWaitLimit": (_I, [_P, ctypes.c_ulonglong]),
+    "mpkDebugInjectStall": (_I, [_P, _I]),
+    "mpkDebugClearStatus": (_I, [_P]),
 }
 
 _lib = None
@@ -334,6 +338,15 @@ class Engine:
         check("mpkDebugWideCounters", lib().mpkDebugWideCounters(self.h, ctypes.byref(w), ctypes.byref(f),
                                                                  ctypes.byref(c)))
         return {"wide_rows": w.value, "full_scans": f.value, "capacity": c.value}
+
+    def set_wait_limit(self, ns: int) -> None:
+        check("mpkDebugSetWaitLimit", lib().mpkDebugSetWaitLimit(self.h, ns))
+
+    def inject_stall(self, stage: int) -> None:
+        check("mpkDebugInjectStall", lib().mpkDebugInjectStall(self.h, stage))
+
+    def clear_status(self) -> None:
+        check("mpkDebugClearStatus", lib().mpkDebugClearStatus(self.h))
 
     def wide_round_rows(self, rows: int) -> None:
         check("mpkDebugWideRoundRows", lib().mpkDebugWideRoundRows(self.h, rows))

@@ -87,9 +87,10 @@ struct Misc {
 };
 static_assert(sizeof(Misc) <= kMiscBytes, "misc block");
 
-__device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status) {
+__device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                          uint32_t lim) {
     int ok = 0;
-    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, status) ? 1 : 0;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, status, lim) ? 1 : 0;
     return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
@@ -128,8 +129,10 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
             long long n, int k, int nkc_rt, const float* __restrict__ xnorm, const float* __restrict__ cn,
             DevParams* __restrict__ prm, int* __restrict__ labels, RefineEntry* __restrict__ list,
             int refine, BoundConsts bc, float4* __restrict__ dbg, const int* __restrict__ went,
-            int* __restrict__ cand, int* __restrict__ ccount, long long wbase) {
+            int* __restrict__ cand, int* __restrict__ ccount, long long wbase, int stall_stage) {
     using Cf = Cfg<BN, NKC>;
+    /* limit of one wait (a test may shorten it to make a left-out stage time out quickly) */
+    const uint32_t lim = (uint32_t)((!EMIT && prm->wait_ns ? prm->wait_ns : kWaitLimitNs) / 1000);   /* microseconds */
     if (EMIT) {
         /* this round's rows: queued rows [wbase, wbase + n) that exist */
         const long long nw = (long long)*reinterpret_cast<volatile unsigned int*>(&prm->nwide) - wbase;
@@ -190,7 +193,11 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                 for (int p = 0; p < 2; ++p) {
                     const int st = (int)(bs % Cf::B_STAGES);
                     const uint32_t bu = bs / Cf::B_STAGES;
-                    if (!mbar_wait(&ms.b_empty[st], (bu & 1u) ^ 1u, abort_flag, status)) { ok = false; return; }
+                    if (!mbar_wait(&ms.b_empty[st], (bu & 1u) ^ 1u, abort_flag, status, lim)) { ok = false; return; }
+                    if (!EMIT && (int)bs == stall_stage) {    /* test hook: this stage is never loaded */
+                        ++bs;
+                        continue;
+                    }
                     mbar_expect_tx(&ms.b_full[st], Cf::B_STAGE);
                     b_last[st] = bu;
                     tma_load_3d(&tmC, &ms.b_full[st], smB + st * Cf::B_STAGE, kc * KC, nt * BN, p);
@@ -203,7 +210,7 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                         for (int kc = 0; kc < nkc && ok; ++kc, ++as) {
                             const int ab = (int)(as % Cf::A_BUFS);
                             const uint32_t au = as / Cf::A_BUFS;
-                            if (!mbar_wait(&ms.a_empty[ab], (au & 1u) ^ 1u, abort_flag, status)) { ok = false; break; }
+                            if (!mbar_wait(&ms.a_empty[ab], (au & 1u) ^ 1u, abort_flag, status, lim)) { ok = false; break; }
                             mbar_expect_tx(&ms.a_full[ab], Cf::A_TILE);
                             a_last[ab] = au;
                             for (int p = 0; p < 2; ++p)
@@ -215,7 +222,7 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                 }
                 const int ab = lt % Cf::A_BUFS;
                 const uint32_t au = (uint32_t)(lt / Cf::A_BUFS);
-                if (!mbar_wait(&ms.a_empty[ab], (au & 1u) ^ 1u, abort_flag, status)) { ok = false; break; }
+                if (!mbar_wait(&ms.a_empty[ab], (au & 1u) ^ 1u, abort_flag, status, lim)) { ok = false; break; }
                 mbar_expect_tx(&ms.a_full[ab], Cf::A_TILE);
                 a_last[ab] = au;
                 for (int p = 0; p < 2; ++p)
@@ -245,7 +252,7 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                 /* centroid hi plane: x_hi * c_hi and x_lo * c_hi */
                 int st = (int)(bs % Cf::B_STAGES);
                 uint32_t bu = bs / Cf::B_STAGES;
-                if (!mbar_wait(&ms.b_full[st], bu & 1u, abort_flag, status)) { ok = false; return; }
+                if (!mbar_wait(&ms.b_full[st], bu & 1u, abort_flag, status, lim)) { ok = false; return; }
                 tc_fence_after();
                 const uint32_t bh = smem_u32(smB + st * Cf::B_STAGE);
 #pragma unroll
@@ -262,7 +269,7 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                 /* centroid lo plane: x_hi * c_lo */
                 st = (int)(bs % Cf::B_STAGES);
                 bu = bs / Cf::B_STAGES;
-                if (!mbar_wait(&ms.b_full[st], bu & 1u, abort_flag, status)) { ok = false; return; }
+                if (!mbar_wait(&ms.b_full[st], bu & 1u, abort_flag, status, lim)) { ok = false; return; }
                 tc_fence_after();
                 const uint32_t bl = smem_u32(smB + st * Cf::B_STAGE);
 #pragma unroll
@@ -275,21 +282,21 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                 const int ab = lt % Cf::A_BUFS;
                 const uint32_t au = (uint32_t)(lt / Cf::A_BUFS);
                 if (!Cf::STREAM) {
-                    if (!mbar_wait(&ms.a_full[ab], au & 1u, abort_flag, status)) { ok = false; break; }
+                    if (!mbar_wait(&ms.a_full[ab], au & 1u, abort_flag, status, lim)) { ok = false; break; }
                     tc_fence_after();
                 }
                 const uint32_t a_addr = smem_u32(smA + ab * Cf::A_TILE);
                 for (int nt = 0; nt < NT && ok; ++nt, ++ts) {
                     const int tb = (int)(ts & 1u);
                     const uint32_t tu = ts >> 1;
-                    if (!mbar_wait(&ms.t_empty[tb], (tu & 1u) ^ 1u, abort_flag, status)) { ok = false; break; }
+                    if (!mbar_wait(&ms.t_empty[tb], (tu & 1u) ^ 1u, abort_flag, status, lim)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + (uint32_t)(tb * BN);
                     uint32_t accum = 0;
                     for (int kc = 0; kc < nkc && ok; ++kc) {
                         if (Cf::STREAM) {
                             const int sa = (int)(as % Cf::A_BUFS);
-                            if (!mbar_wait(&ms.a_full[sa], (as / Cf::A_BUFS) & 1u, abort_flag, status)) { ok = false; break; }
+                            if (!mbar_wait(&ms.a_full[sa], (as / Cf::A_BUFS) & 1u, abort_flag, status, lim)) { ok = false; break; }
                             tc_fence_after();
                             const uint32_t ah = smem_u32(smA + sa * Cf::A_TILE);
                             chunk(d_tmem, ah, ah + Cf::A_CHUNK, accum);
@@ -349,7 +356,7 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                 for (int nt = 0; nt < NT; ++nt, ++ts) {
                     const int tb = (int)(ts & 1u);
                     const uint32_t tu = ts >> 1;
-                    if (ok) ok = wait_warp(&ms.t_full[tb], tu & 1u, abort_flag, status);
+                    if (ok) ok = wait_warp(&ms.t_full[tb], tu & 1u, abort_flag, status, lim);
                     if (!ok) continue;
                     tc_fence_after();
                     const int col0 = half * Cf::HALF;
@@ -393,7 +400,7 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
             for (int nt = 0; nt < NT; ++nt, ++ts) {
                 const int tb = (int)(ts & 1u);
                 const uint32_t tu = ts >> 1;
-                if (ok) ok = wait_warp(&ms.t_full[tb], tu & 1u, abort_flag, status);
+                if (ok) ok = wait_warp(&ms.t_full[tb], tu & 1u, abort_flag, status, lim);
                 if (!ok) continue;
                 tc_fence_after();
                 const int col0 = half * Cf::HALF;              /* first column of this warp */
@@ -537,7 +544,8 @@ cudaError_t launch_t(const AssignArgs& a, cudaStream_t s) {
     kern<<<grid, kThreads, Cf::SMEM_BYTES, s>>>(*a.tmX, *a.tmC, a.n, a.k, a.dp / KC, a.xnorm, a.cn, a.prm,
                                                  a.labels, a.list, a.refine, a.bc, a.dbg,
                                                  EMIT ? a.wide->went : nullptr, EMIT ? a.wide->cand : nullptr,
-                                                 EMIT ? a.wide->ccount : nullptr, EMIT ? a.wbase : 0);
+                                                 EMIT ? a.wide->ccount : nullptr, EMIT ? a.wbase : 0,
+                                                 EMIT ? -1 : a.stall);
     return cudaGetLastError();
 }
 

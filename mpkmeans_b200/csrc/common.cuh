@@ -74,13 +74,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
  * timeout bit in *status and the shared abort flag) if the time limit passes
  * or another thread of the CTA has already aborted. */
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* status) {
+                                          int* status, uint32_t limit_us = (uint32_t)(kWaitLimitNs / 1000)) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = globaltimer();
     for (;;) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (globaltimer() - t0 > kWaitLimitNs) {
+        if (globaltimer() - t0 > 1000ull * limit_us) {
             *abort_flag = 1;
             atomicOr(status, MPK_DEV_TIMEOUT);
             return false;

@@ -32,6 +32,7 @@ struct DevParams {
     unsigned int nwide;              /* rows handed to the wide refinement by the last assign */
     unsigned int pad0;
     unsigned long long nwide_total;  /* wide rows over the run */
+    unsigned long long wait_ns;      /* limit of one wait in the assignment kernel (0: 4 s) */
 };
 
 /* A row to re-decide in FP32.  The assignment epilogue tracks, per column
@@ -105,6 +106,7 @@ struct AssignArgs {
     bool emit;
     const WideScratch* wide;
     long long wbase;          /* emit pass: first queued row of this round */
+    int stall;                /* test hook: centroid-plane stage the producer leaves unloaded (-1: none) */
 };
 int  assign_bn_for(int k);                   /* N tile width chosen for k     */
 int  assign_supported(int d);                /* 1 when d fits the kernel      */

@@ -11,6 +11,7 @@
 #include "engine.cuh"
 #include "gemm_tc.cuh"
 #include "mpemu.h"
+#include "mpkmeans_debug.h"
 
 #include <cudaTypedefs.h>
 
@@ -601,6 +602,18 @@ mpemuStatus_t mpemuGemmMultiword(cublasHandle_t handle, cublasOperation_t opA, c
                                    scaleB, nsplits, 0, nmacs, beta, dC, ldc);
 }
 
+
+/* ------------------------------------------------------------- status ---- */
+
+int mpkDebugGemmStatus(int clear) {
+    int sms = 0;
+    int* st = gemm_status(&sms);
+    if (!st || cudaDeviceSynchronize() != cudaSuccess) return -1;
+    int h = 0;
+    if (cudaMemcpy(&h, st, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    if (clear && cudaMemset(st, 0, sizeof(int)) != cudaSuccess) return -1;
+    return h;
+}
 
 /* ------------------------------------------------------------ context ---- */
 

@@ -160,6 +160,7 @@ struct mpkEngine_s {
     WideScratch wide{nullptr, nullptr, nullptr, nullptr, 0, 0, 0};
     BoundConsts bc;
     float4* dbg = nullptr;                /* test hook, set by mpkDebugSetAssignTrace */
+    int stall = -1;                       /* test hook, set by mpkDebugInjectStall */
     bool prof = false;                    /* bench hook: events around the hot kernels */
     std::vector<cudaEvent_t> ev_assign, ev_accum;
 };
@@ -335,6 +336,7 @@ static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int r
     a.emit = false;
     a.wide = &e->wide;
     a.wbase = 0;
+    a.stall = e->stall;
     prof_mark(e, e->ev_assign);
     cudaError_t err = launch_assign(a, e->s);
     prof_mark(e, e->ev_assign);
@@ -502,6 +504,26 @@ mpkStatus mpkDebugEngineInfo(mpkEngine e, float* scale, float* eta, int* frac, f
     if (frac) *frac = h.frac;
     if (c1) *c1 = e->bc.c1;
     if (c2) *c2 = e->bc.c2;
+    return MPK_OK;
+}
+
+mpkStatus mpkDebugSetWaitLimit(mpkEngine e, unsigned long long ns) {
+    if (!e) return MPK_ERR_INVALID;
+    MPK_TRY(cudaMemcpyAsync(&e->prm->wait_ns, &ns, sizeof(ns), cudaMemcpyHostToDevice, e->s));
+    MPK_TRY(cudaStreamSynchronize(e->s));
+    return MPK_OK;
+}
+
+mpkStatus mpkDebugInjectStall(mpkEngine e, int stage) {
+    if (!e) return MPK_ERR_INVALID;
+    e->stall = stage < 0 ? -1 : stage;
+    return MPK_OK;
+}
+
+mpkStatus mpkDebugClearStatus(mpkEngine e) {
+    if (!e) return MPK_ERR_INVALID;
+    MPK_TRY(cudaMemsetAsync(&e->prm->status, 0, sizeof(int), e->s));
+    MPK_TRY(cudaStreamSynchronize(e->s));
     return MPK_OK;
 }
 

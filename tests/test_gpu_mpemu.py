@@ -437,3 +437,8 @@ def test_batched_equals_range(cuda):
     torch.cuda.synchronize()
     assert torch.equal(got, want)
     assert L.mpemuContextDestroy(ctx) == OK
+
+
+def test_zz_gemm_status_word_clean(cuda):
+    """After every GEMM of this module no bounded wait inside the kernel ran out."""
+    assert lib().mpkDebugGemmStatus(1) == 0
