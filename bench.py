@@ -57,6 +57,10 @@ UNIT = "iter/s"
 # on 8 GPUs; each GPU holds an eighth of the rows (one GPU cannot hold all of them), so on N GPUs
 # the run is N eighths of the configuration (weak scaling) and at N = 8 it is the whole of it.
 WORKLOADS = {
+    "config1": {"n": 100_000, "d": 32, "k": 64, "shards": 0, "iters": 20,
+                "metric": "Lloyd iterations/s, config 1 (n=1e5, d=32, k=64, FP32, k-means++ start)",
+                "desc": "config 1: 64-component isotropic mixture (means U[-10,10]^d, sigma 1, equal weights), "
+                        "n=1e5, d=32, k=64, k-means++ start (mpkInitKMeansPP)"},
     "config3": {"n": N_FULL, "d": 128, "k": 1024, "shards": 0, "metric": METRIC, "iters": 25,
                 "desc": "config 3: 1024-component Gaussian mixture, n=1e7, d=128, k=1024"},
     "config4": {"n": 50_000_000, "d": 768, "k": 4096, "shards": 8, "iters": 10,
@@ -82,7 +86,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-sgemm", action="store_true", help="skip the config-2 emulated SGEMM section")
-    ap.add_argument("--workload", choices=["config3", "config4", "config5", "sgemm"], default="config3",
+    ap.add_argument("--workload", choices=["config1", "config3", "config4", "config5", "sgemm"], default="config3",
                     help="config4/config5: 1/8 of the configuration's rows per GPU; sgemm: only the config-2 "
                          "emulated SGEMM measurement, as its own JSON line")
     ap.add_argument("--sgemm-n", type=int, default=8192)
@@ -143,6 +147,12 @@ def gen_shard(n_local, rank, device, wl="config3"):
             P[r0:r1] = means[comp] + sig[comp, None] * torch.randn((r1 - r0, d), generator=g, device=device)
         return P
     gc = torch.Generator().manual_seed(SEED + 17)
+    if wl == "config1":
+        # 64 components, means U[-10, 10]^d, sigma 1, equal weights (mpkMakeBlobs' distribution)
+        means = ((torch.rand((k, d), generator=gc) * 2 - 1) * 10.0).to(device)
+        comp = torch.randint(0, k, (n_local,), generator=g, device=device)
+        P.copy_(means[comp] + torch.randn((n_local, d), generator=g, device=device))
+        return P
     if wl == "config4":
         # N(0, I) draws around k random N(0, I) centres, each point scaled to unit norm
         cen = torch.randn((k, d), generator=gc).to(device)
@@ -221,8 +231,10 @@ def run_ours(args, world, rank, local):
     K, D = WORKLOADS[args.workload]["k"], WORKLOADS[args.workload]["d"]
     n_local, n_total = workload_rows(args, world, rank)
     P = gen_shard(n_local, rank, dev, args.workload)
-    # initial centroids: k distinct rows of rank 0's shard, broadcast
-    if rank == 0:
+    # initial centroids from rank 0's shard, broadcast: k-means++ (config 1) or k distinct rows
+    if rank == 0 and args.workload == "config1":
+        C0 = M.kmeanspp(P, K, SEED)
+    elif rank == 0:
         g = torch.Generator(device=dev).manual_seed(SEED)
         idx = torch.sort(torch.randperm(n_local, generator=g, device=dev)[:K]).values
         C0 = P[idx].clone()
@@ -401,7 +413,11 @@ def run_reference(args, world, rank, local):
                                f"({n * K * 4 / 1e9:.0f} GB at n={n}, k={K}): it does not fit one GPU"}
     P = gen_shard(n, 0, dev, args.workload)
     g = torch.Generator(device=dev).manual_seed(SEED)
-    C0 = P[torch.sort(torch.randperm(n, generator=g, device=dev)[:K]).values].clone()
+    if args.workload == "config1":
+        import mpkmeans_b200 as MB
+        C0 = MB.kmeanspp(P, K, SEED)      # the same start as our arm (the reference has no k-means++)
+    else:
+        C0 = P[torch.sort(torch.randperm(n, generator=g, device=dev)[:K]).values].clone()
     lab = torch.empty(n, dtype=torch.int32, device=dev)
     blas = torch.cuda.current_blas_handle()
     iters = 2
@@ -573,9 +589,11 @@ def main():
                         "higher_is_better": True, "scaling": "weak" if wl["shards"] else "strong", "vs_baseline": None, "dtype": "f32",
                         "data": "synthetic (device-generated, seeded)", "config": cfg,
                         "cpu_baseline": {"kind": "reference", "cores": 1, "value": r["value"], "unit": UNIT,
-                                         "sample": f"full config-3 workload, {r['iters_per_step']} iterations per "
-                                                   "step, through the reference's mpkMeansFP32 (cuBLAS SGEMM + its "
-                                                   "kernels) on one B200; the reference has no CPU k-means"},
+                                         "sample": f"the full {args.workload} workload on one GPU "
+                                                   f"({workload_rows(args, 1, 0)[0]} rows), {r['iters_per_step']} "
+                                                   "iterations per step, through the reference's mpkMeansFP32 "
+                                                   "(cuBLAS SGEMM + its kernels) on one B200; the reference has no "
+                                                   "CPU k-means"},
                         "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
                 print(json.dumps(line))
         if world > 1:
