@@ -8,7 +8,12 @@ files (tolerance pins where the reference's arithmetic is cuBLAS's, exact pins
 where it is its own code).
 
 Usage (GPU machine, from the repository root):
-    python tests/golden/make_golden.py [outdir]
+    python tests/golden/make_golden.py [outdir] [--only kmeans|mpemu|large]
+
+The ``large`` cases (configs 4 and 5 shapes on row samples) also run this
+repository's engine (mpkmeans_b200) for two Lloyd iterations and then let the
+reference assign against those centroids -- the reference's own per-iteration
+check, fed the engine's centroids.
 """
 from __future__ import annotations
 
@@ -25,7 +30,11 @@ sys.path.insert(0, str(ROOT))
 import oracle as O  # noqa: E402
 from mpkmeans_b200 import mpkParams, mpkStats  # noqa: E402  (struct layouts only)
 
-OUT = Path(sys.argv[1]) if len(sys.argv) > 1 else Path(__file__).resolve().parent
+_args = [a for a in sys.argv[1:] if not a.startswith("--")]
+ONLY = sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None
+if ONLY in _args:
+    _args.remove(ONLY)
+OUT = Path(_args[0]) if _args else Path(__file__).resolve().parent
 
 ref = ctypes.CDLL(str(O.REF_LIB_PATH))
 VP = ctypes.c_void_p
@@ -221,7 +230,35 @@ def mpemu_cases():
     print("ref_mpemu done")
 
 
+def large_cases():
+    """Configs 4 and 5 geometries on row samples: the reference's FP32 assignment (a) against random
+    start centroids and (b) against the centroids after two iterations of this engine."""
+    import hashlib
+    import mpkmeans_b200 as M
+    for name, P, k, seed in (
+            ("ref_config4_sample", O.make_sphere(30_000, 768, 4096, 41), 4096, 41),
+            ("ref_config5_sample", O.make_offset(40_000, 256, 16384, 51, 1e3), 16384, 51)):
+        n, d = P.shape
+        idx = np.sort(O.init_random_idx(n, k, seed))
+        C0 = P[idx].copy()
+        lab0, _, _ = run("mpkMeansFP32", P, C0, 1)
+        dP = torch.from_numpy(P).to(dev)
+        dC = torch.from_numpy(C0).to(dev)
+        lab = torch.empty(n, dtype=torch.int32, device=dev)
+        M.means_mixed(dP, dC, lab, M.params_init(max_iter=2))
+        C2 = dC.cpu().numpy()
+        lab2, _, _ = run("mpkMeansFP32", P, C2, 1)
+        np.savez_compressed(OUT / f"{name}.npz", n=n, d=d, k=k, seed=seed, labels_it0=lab0.astype(np.int16),
+                            labels_c2=lab2.astype(np.int16),
+                            c2_sha256=np.frombuffer(hashlib.sha256(C2.tobytes()).digest(), np.uint8))
+        print(name, "done")
+
+
 if __name__ == "__main__":
     OUT.mkdir(parents=True, exist_ok=True)
-    kmeans_cases()
-    mpemu_cases()
+    if ONLY in (None, "kmeans"):
+        kmeans_cases()
+    if ONLY in (None, "mpemu"):
+        mpemu_cases()
+    if ONLY in (None, "large"):
+        large_cases()
