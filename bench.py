@@ -267,11 +267,13 @@ def run_ours(args, world, rank, local):
     clocks = Clocks(local)
     time.sleep(0.3)
     eng.profile(True)
+    launches0 = eng.launches()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
         step()
     e1.record()
+    launches = eng.launches() - launches0
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -288,7 +290,7 @@ def run_ours(args, world, rank, local):
     eng.assign(C_chk, labels)
     torch.cuda.synchronize()
 
-    res = {"t_ms": t_ms, "prof": prof, "clk": clk, "counters": cnt, "n_local": n_local}
+    res = {"t_ms": t_ms, "prof": prof, "clk": clk, "counters": cnt, "n_local": n_local, "launches": launches}
     res["e2e"] = None if args.no_e2e else run_e2e(M, P, C0, world, rank, dev, n_total,
                                                   iters=WORKLOADS[args.workload]["iters"])
     res["n_total"] = n_total
@@ -633,7 +635,7 @@ def main():
             "roofline_update": {"bound": "hbm", "achieved": u_gbs, "peak": hbm, "unit": "GB/s", "frac": u_gbs / hbm,
                                 "kernel": "update: k_label_hist + k_bin_scan + k_label_scatter + k_segsum", "work": "n*d*4 + n*4 bytes per update",
                                 "avg_launch_ms": u_ms},
-            "gpu_launches": 8 * args.steps,
+            "gpu_launches": r["launches"],
             "refined_rows_per_iter": r["counters"]["rows_refined"] / max(1, args.warmup + args.steps + 1),
             "refined_candidates_per_iter": r["counters"]["cand_refined"] / max(1, args.warmup + args.steps + 1),
             "class_rescan_rows_per_iter": r["counters"]["rows_full_scan"] / max(1, args.warmup + args.steps + 1),

@@ -26,6 +26,11 @@ mpkStatus mpkDebugEngineInfo(mpkEngine e, float* scale, float* eta, int* frac, f
  * the per-assignment capacity (0: the engine has no wide path, k <= 256). */
 mpkStatus mpkDebugWideCounters(mpkEngine e, long long* wide_rows, long long* full_scans, long long* capacity);
 
+/* Kernels the engine has launched over its life (its own kernels only: no
+ * memsets or library calls); the bench reports the count inside its timed
+ * region from this. */
+long long mpkDebugEngineLaunches(mpkEngine e);
+
 /* Failure-path test hooks.  SetWaitLimit bounds every wait of the engine's
  * assignment kernel by `ns` (0: the default 4 s).  InjectStall makes the
  * kernel's producer leave centroid-plane stage `stage` (counted per CTA from

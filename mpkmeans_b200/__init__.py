@@ -183,6 +183,7 @@ SIGNATURES = {
     "mpkDebugWideCounters": (_I, [_P, ctypes.POINTER(_LL), ctypes.POINTER(_LL), ctypes.POINTER(_LL)]),
     "mpkDebugWideRoundRows": (_I, [_P, _LL]),
     "mpkDebugGemmStatus": (_I, [_I]),
+    "mpkDebugEngineLaunches": (_LL, [_P]),
     "mpkDebugSetWaitLimit": (_I, [_P, ctypes.c_ulonglong]),
     "mpkDebugInjectStall": (_I, [_P, _I]),
     "mpkDebugClearStatus": (_I, [_P]),
@@ -338,6 +339,9 @@ class Engine:
         check("mpkDebugWideCounters", lib().mpkDebugWideCounters(self.h, ctypes.byref(w), ctypes.byref(f),
                                                                  ctypes.byref(c)))
         return {"wide_rows": w.value, "full_scans": f.value, "capacity": c.value}
+
+    def launches(self) -> int:
+        return int(lib().mpkDebugEngineLaunches(self.h))
 
     def set_wait_limit(self, ns: int) -> None:
         check("mpkDebugSetWaitLimit", lib().mpkDebugSetWaitLimit(self.h, ns))

@@ -129,8 +129,9 @@ struct UpdateScratch {
     int* cursor;
     int* hist;
 };
-/* sums (k*d int64) must be zero on entry; counts (k int64) are written. */
-void launch_update_sorted(const float* P, long long n, int d, const int* labels, int k, DevParams* prm,
+/* sums (k*d int64) must be zero on entry; counts (k int64) are written.
+ * Returns the number of kernels launched. */
+int launch_update_sorted(const float* P, long long n, int d, const int* labels, int k, DevParams* prm,
                           long long* sums, long long* counts, UpdateScratch sc, int num_sms, cudaStream_t s);
 void launch_finalize_fixed(const long long* sums, const long long* counts, int k, int d,
                            const DevParams* prm, float* C, float* moved2, cudaStream_t s);

@@ -161,6 +161,7 @@ struct mpkEngine_s {
     BoundConsts bc;
     float4* dbg = nullptr;                /* test hook, set by mpkDebugSetAssignTrace */
     int stall = -1;                       /* test hook, set by mpkDebugInjectStall */
+    long long launches = 0;               /* kernels this engine has launched */
     bool prof = false;                    /* bench hook: events around the hot kernels */
     std::vector<cudaEvent_t> ev_assign, ev_accum;
 };
@@ -315,6 +316,7 @@ static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int r
     cudaMemsetAsync(&e->prm->nflag, 0, sizeof(unsigned int), e->s);
     cudaMemsetAsync(&e->prm->nwide, 0, sizeof(unsigned int), e->s);
     launch_prep_c(dC, e->k, e->kpad, e->d, e->dp, e->prm, e->Cs, e->cn, e->s);
+    ++e->launches;
     if (e->n == 0) return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
     AssignArgs a;
     a.tmX = &e->tmX;
@@ -340,6 +342,7 @@ static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int r
     prof_mark(e, e->ev_assign);
     cudaError_t err = launch_assign(a, e->s);
     prof_mark(e, e->ev_assign);
+    ++e->launches;
     if (err != cudaSuccess) {
         fprintf(stderr, "mpkmeans_b200: assignment launch failed: %s\n", cudaGetErrorString(err));
         return MPK_ERR_CUDA;
@@ -348,12 +351,16 @@ static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int r
         launch_refine(e->P, dC, e->cn, e->d, e->k, assign_bn_for(e->k), e->list, e->prm, dAssign, e->n,
                       (hist_it >= 0 && hist_it < MPK_MAX_HIST) ? e->hist + hist_it : nullptr, e->Xs, e->n, e->dp,
                       e->wide, e->num_sms, e->s);
+        ++e->launches;
         /* rows the refinement queued: per round, a tensor-core pass that lists their
          * candidates, then the FP32 evaluation of just those (every launch sizes itself from
          * prm->nwide; rounds past the queue exit at once) */
         for (int r = 0; r < e->wide.rounds; ++r) {
             const long long base = (long long)r * e->wide.per_round;
-            if (r > 0) launch_wide_gather(e->list, e->Xs, e->n, e->dp, e->wide, base, e->prm, e->num_sms, e->s);
+            if (r > 0) {
+                launch_wide_gather(e->list, e->Xs, e->n, e->dp, e->wide, base, e->prm, e->num_sms, e->s);
+                ++e->launches;
+            }
             AssignArgs w = a;
             w.tmX = &e->tmXw;
             w.n = e->wide.per_round;
@@ -368,6 +375,7 @@ static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int r
             }
             launch_refine_wide(e->P, dC, e->cn, e->d, e->k, e->list, e->wide, base, e->prm, dAssign, e->num_sms,
                                e->s);
+            e->launches += 2;                 /* the emit pass and the FP32 evaluation */
         }
     }
     return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
@@ -377,14 +385,15 @@ static mpkStatus engine_accumulate(mpkEngine e, const int* dAssign, long long* d
     const long long len = (long long)e->k * e->d + e->k;
     cudaMemsetAsync(dSums, 0, (size_t)len * sizeof(long long), e->s);
     prof_mark(e, e->ev_accum);
-    launch_update_sorted(e->P, e->n, e->d, dAssign, e->k, e->prm, dSums, dSums + (long long)e->k * e->d, e->us,
-                         e->num_sms, e->s);
+    e->launches += launch_update_sorted(e->P, e->n, e->d, dAssign, e->k, e->prm, dSums,
+                                        dSums + (long long)e->k * e->d, e->us, e->num_sms, e->s);
     prof_mark(e, e->ev_accum);
     return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
 }
 
 static mpkStatus engine_finalize(mpkEngine e, const long long* dSums, float* dC, float* dMoved2) {
     launch_finalize_fixed(dSums, dSums + (long long)e->k * e->d, e->k, e->d, e->prm, dC, dMoved2, e->s);
+    ++e->launches;
     return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
 }
 
@@ -506,6 +515,8 @@ mpkStatus mpkDebugEngineInfo(mpkEngine e, float* scale, float* eta, int* frac, f
     if (c2) *c2 = e->bc.c2;
     return MPK_OK;
 }
+
+long long mpkDebugEngineLaunches(mpkEngine e) { return e ? e->launches : -1; }
 
 mpkStatus mpkDebugSetWaitLimit(mpkEngine e, unsigned long long ns) {
     if (!e) return MPK_ERR_INVALID;

@@ -215,19 +215,21 @@ void launch_segsum_window(const float* P, int d, int f0, int ng, const int* perm
 
 /* One launch per window of up to 8 groups of features. */
 template <int VEC>
-void launch_segsum(const float* P, int d, const int* perm, const int* bin_start, int k, const DevParams* prm,
-                   long long* sums, int blocks, cudaStream_t s) {
+int launch_segsum(const float* P, int d, const int* perm, const int* bin_start, int k, const DevParams* prm,
+                  long long* sums, int blocks, cudaStream_t s) {
     constexpr int WIN = 8 * 32 * VEC;
-    for (int f0 = 0; f0 < d; f0 += WIN) {
+    int launches = 0;
+    for (int f0 = 0; f0 < d; f0 += WIN, ++launches) {
         const int ng = ceil_div(min(WIN, d - f0), 32 * VEC);
         launch_segsum_window<VEC>(P, d, f0, ng, perm, bin_start, k, prm, sums, blocks, s);
     }
+    return launches;
 }
 
 }  /* namespace */
 
-void launch_update_sorted(const float* P, long long n, int d, const int* labels, int k, DevParams* prm,
-                          long long* sums, long long* counts, UpdateScratch sc, int num_sms, cudaStream_t s) {
+int launch_update_sorted(const float* P, long long n, int d, const int* labels, int k, DevParams* prm,
+                         long long* sums, long long* counts, UpdateScratch sc, int num_sms, cudaStream_t s) {
     cudaMemsetAsync(sc.hist, 0, sizeof(int) * (size_t)k, s);
     const bool smem = k <= kSmemHistMax;
     const size_t hb = smem ? sizeof(int) * (size_t)k : 0;
@@ -241,14 +243,15 @@ void launch_update_sorted(const float* P, long long n, int d, const int* labels,
         else k_label_hist<false><<<blocks, 512, 0, s>>>(labels, n, k, sc.hist, prm);
     }
     k_bin_scan<<<1, 1024, 0, s>>>(sc.hist, k, sc.bin_start, sc.cursor, counts);
-    if (n <= 0) return;
+    if (n <= 0) return 1;
     const long long rpb = (n + blocks - 1) / blocks;
     if (smem) k_label_scatter<true><<<blocks, 512, hb, s>>>(labels, n, k, sc.cursor, sc.perm, rpb);
     else k_label_scatter<false><<<blocks, 512, 0, s>>>(labels, n, k, sc.cursor, sc.perm, rpb);
     const bool vec = (d % 4 == 0) && ((reinterpret_cast<uintptr_t>(P) & 15) == 0);
     const int sblocks = num_sms * 8;
-    if (vec) launch_segsum<4>(P, d, sc.perm, sc.bin_start, k, prm, sums, sblocks, s);
-    else launch_segsum<1>(P, d, sc.perm, sc.bin_start, k, prm, sums, sblocks, s);
+    const int seg = vec ? launch_segsum<4>(P, d, sc.perm, sc.bin_start, k, prm, sums, sblocks, s)
+                        : launch_segsum<1>(P, d, sc.perm, sc.bin_start, k, prm, sums, sblocks, s);
+    return 3 + seg;                       /* hist, scan, scatter, segmented sums */
 }
 
 }  /* namespace mpk */
