@@ -729,10 +729,19 @@ mpkStatus mpkMeansFP32(cublasHandle_t blas, const float* dP, int n, int d, int k
     return lloyd(blas, dP, n, d, k, dC, dAssign, params, stats, true, "fp32");
 }
 
+/* The reference's double-fp16 driver (kmeans/src/multiword.cu:245-645) refuses
+ * to run with both exclusion conditions off (multiword.cu:256-259); so does
+ * this one.  Otherwise it is the engine: its FP16 hi/lo split is the
+ * double-fp16 scheme, every row's label is the exact FP32 argmin, and the
+ * three cross products are counted in mw_products. */
 mpkStatus mpkMeansMultiword(cublasHandle_t blas, const float* dP, int n, int d, int k, float* dC, int* dAssign,
                             const mpkParams* params, mpkStats* stats) {
     mpkStats local;
     mpkStats* S = stats ? stats : &local;
+    if (params && !params->use_cond3 && !params->use_cond6) {
+        fprintf(stderr, "mpkMeansMultiword: at least one condition must be on\n");
+        return MPK_ERR_INVALID;
+    }
     mpkStatus st = lloyd(blas, dP, n, d, k, dC, dAssign, params, S, true, "mw");
     if (st == MPK_OK) {
         S->mw_products = 3LL * S->iters;

@@ -51,6 +51,25 @@ def test_epsilon_matches_reference_host_code():
             assert O.mpk_epsilon(d, acc) == ref.mpkEpsilon(d, acc)
 
 
+def test_library_host_formulas_match_reference_host_code():
+    """The library's own mpkEpsilon / mpkMultiwordEpsilon (host functions of the
+    product, callable without a GPU) against the reference's, and the
+    optional-backend probe."""
+    import mpkmeans_b200 as M
+    ref = ref_lib()
+    ref.mpkEpsilon.restype = ctypes.c_double
+    ref.mpkMultiwordEpsilon.restype = ctypes.c_double
+    L = M.lib()
+    L.mpkMultiwordEpsilon.restype = ctypes.c_double
+    L.mpkMultiwordEpsilon.argtypes = [ctypes.c_int, ctypes.c_int]
+    for d in (1, 32, 128, 768, 4096, 100000):
+        for acc in (0, 1):
+            assert L.mpkEpsilon(d, acc) == ref.mpkEpsilon(d, acc)
+        for macs in (1, 2, 3, 6):
+            assert L.mpkMultiwordEpsilon(d, macs) == ref.mpkMultiwordEpsilon(d, macs), (d, macs)
+    assert L.mpkHaveCuvs() == 0
+
+
 def test_term_schedule_known_answer():
     # gemm-emulation/bench/test_split.cu:135-145
     want = [(0, 0), (0, 1), (1, 0), (0, 2), (1, 1), (2, 0), (1, 2), (2, 1), (2, 2)]
