@@ -187,6 +187,13 @@ mpkStatus mpkInitRandomPoints(const float* dP, int n, int d, int k, unsigned see
  * MPK_ERR_INVALID unless 0 < k <= n and d > 0. */
 mpkStatus mpkInitKMeansPP(const float* dP, int n, int d, int k, unsigned long long seed, float* dC);
 
+/* Engine scratch comes from one stream-ordered memory pool per device that
+ * keeps freed blocks cached, so repeated fits allocate nothing new.  This
+ * returns the cached blocks of `device` (-1: the current one) to the driver;
+ * it synchronises that device.  No reference counterpart (the reference
+ * mallocs and frees its scratch in every call). */
+mpkStatus mpkTrimMemoryPool(int device);
+
 /* ------------------------------------------------ new: explicit steps --- */
 
 /* One assignment pass of the engine: dAssign[i] = argmin_j of the FP32

@@ -109,6 +109,7 @@ SIGNATURES = {
     "mpkMakeBlobs": (None, [_I, _I, _I, _F, _F, ctypes.c_uint, _P, _P]),
     "mpkInitRandomPoints": (_I, [_P, _I, _I, _I, ctypes.c_uint, _P]),
     "mpkInitKMeansPP": (_I, [_P, _I, _I, _I, ctypes.c_ulonglong, _P]),
+    "mpkTrimMemoryPool": (_I, [_I]),
     "mpkAssign": (_I, [_P, _P, _I, _I, _I, _P, _P, _PARAMS, _STATS]),
     "mpkUpdate": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
     "mpkMeansMixedMG": (_I, [_I, _P, _P, _P, _I, _I, _P, _P, _PARAMS, _STATS]),

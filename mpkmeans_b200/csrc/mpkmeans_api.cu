@@ -138,6 +138,19 @@ void dev_free(void* p, cudaStream_t s) {
 
 }  /* namespace mpk */
 
+extern "C" mpkStatus mpkTrimMemoryPool(int device) {
+    int prev = 0;
+    if (cudaGetDevice(&prev) != cudaSuccess) return MPK_ERR_CUDA;
+    if (device < 0) device = prev;
+    cudaMemPool_t pool = mpk::engine_pool(device);
+    if (!pool) return MPK_ERR_INVALID;
+    if (cudaSetDevice(device) != cudaSuccess) return MPK_ERR_INVALID;
+    const cudaError_t e1 = cudaDeviceSynchronize();
+    const cudaError_t e2 = cudaMemPoolTrimTo(pool, 0);
+    cudaSetDevice(prev);
+    return (e1 == cudaSuccess && e2 == cudaSuccess) ? MPK_OK : MPK_ERR_CUDA;
+}
+
 /* ------------------------------------------------------------ engine ---- */
 
 struct mpkEngine_s {

@@ -129,3 +129,17 @@ def test_absent_backends_report_invalid(cuda):
     lab = torch.zeros(16, dtype=torch.int32, device="cuda")
     for fn in (L.mpkMeansBaselineRT, L.mpkMeansCuvs):
         assert fn(None, z.data_ptr(), 16, 4, 2, z.data_ptr(), lab.data_ptr(), None, None) == M.MPK_ERR_INVALID
+
+
+def test_trim_memory_pool(cuda):
+    """After a fit the engine's pool keeps its blocks; trimming hands them back."""
+    P = torch.randn((200_000, 64), device="cuda")
+    C = P[:256].clone()
+    lab = torch.empty(200_000, dtype=torch.int32, device="cuda")
+    M.means_mixed(P, C, lab, M.params_init(max_iter=2))
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    assert M.lib().mpkTrimMemoryPool(-1) == M.MPK_OK
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 >= free0 + 50 * 2**20          # at least the 51 MB of split planes came back
+    assert M.lib().mpkTrimMemoryPool(999) == M.MPK_ERR_INVALID
