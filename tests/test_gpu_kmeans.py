@@ -356,6 +356,33 @@ def test_engine_shards_equal_whole(cuda):
     assert torch.equal(C_sh, C_whole)
 
 
+def test_engine_empty_and_tiny_shards(cuda):
+    """Shards with no rows and with fewer rows than centroids (as a large-k job
+    split over many GPUs can produce) add up to the one-engine sums."""
+    P, C = make_problem(20000, 32, 300, seed=12)
+    dP, dC = dev(P), dev(C)
+    pmax = float(max(np.abs(P).max(), np.abs(C).max()))
+    with M.Engine(dP, 300, pmax_global=pmax, n_global=20000) as e:
+        lab_all = torch.empty(20000, dtype=torch.int32, device="cuda")
+        sums = torch.empty(e.sums_length, dtype=torch.int64, device="cuda")
+        e.assign(dC, lab_all)
+        e.accumulate(lab_all, sums)
+    tot = torch.zeros_like(sums)
+    labs = []
+    for lo, hi in ((0, 0), (0, 3), (3, 3), (3, 20000)):
+        with M.Engine(dP[lo:hi], 300, pmax_global=pmax, n_global=20000) as e:
+            lab = torch.empty(hi - lo, dtype=torch.int32, device="cuda")
+            s = torch.empty(e.sums_length, dtype=torch.int64, device="cuda")
+            e.assign(dC, lab)
+            e.accumulate(lab, s)
+            torch.cuda.synchronize()
+            assert e.counters()["status"] == 0
+            tot += s
+            labs.append(lab)
+    assert torch.equal(torch.cat(labs), lab_all)
+    assert torch.equal(tot, sums)
+
+
 def test_mg_entry_single_gpu_matches(cuda):
     P = O.make_config1(50_000, 32, seed=5)
     C0 = O.kmeanspp(P, 64, seed=5)
