@@ -2,8 +2,9 @@
 # Build the reference's own k-means and split-GEMM code from its sources, as
 # they lie in the read-only reference tree, into oracle/_ref/libmpkref.so.
 # Only the hot-path sources are compiled (no CMake, no cuVS):
-#   kmeans/src/{mpkmeans,kernels,data,multiword}.cu (multiword with its mpemu
-#   path on, -DMPK_MULTIWORD, as the reference's CMake option does)
+#   kmeans/src/{mpkmeans,kernels,data,multiword,baseline,cuvs_baseline}.cu
+#   (multiword with its mpemu path on, -DMPK_MULTIWORD, as the reference's
+#   CMake option does; cuvs_baseline without MPK_CUVS, i.e. its stub)
 #   gemm-emulation/src/{split,gemm,util,split_fp16,gemm_fp16}.cu
 # MPK_STATS is on so that mpkMeansMixed's per-iteration FP32 verification
 # (mpkmeans.cu:555-582) is available.  The output is git-ignored; it travels to
@@ -22,6 +23,7 @@ FLAGS="-O3 -std=c++17 -Xcompiler -fPIC -gencode arch=compute_100a,code=sm_100a -
 INC="-I$REF/kmeans/include -I$REF/kmeans/src -I$REF/gemm-emulation/include -I$REF/gemm-emulation/src"
 OBJS=()
 for f in kmeans/src/mpkmeans.cu kmeans/src/kernels.cu kmeans/src/data.cu kmeans/src/multiword.cu \
+         kmeans/src/baseline.cu kmeans/src/cuvs_baseline.cu \
          gemm-emulation/src/split.cu gemm-emulation/src/gemm.cu gemm-emulation/src/util.cu \
          gemm-emulation/src/split_fp16.cu gemm-emulation/src/gemm_fp16.cu; do
   o="$OUT/$(echo "$f" | tr '/' '_' ).o"
