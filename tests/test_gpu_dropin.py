@@ -133,3 +133,95 @@ def test_human_readable_report_passes(binaries):
         if ln.split()[0] in SCHEMES:
             pct = float(ln.split("labels == fp32")[1].split("%")[0])
             assert pct >= 99.99, ln
+
+
+# ------------------------------------------------ mpemu driver programs -----
+
+def mpemu_bin(name, side):
+    b = REF_DIR / f"mpemu_{name}_{side}"
+    if not b.exists():
+        pytest.skip(f"{b.name} not built (oracle/build_ref_bench.sh)")
+    return b
+
+
+@pytest.mark.parametrize("name", ["test_split", "test_split_fp16", "test_refine", "test_concat"])
+def test_reference_mpemu_selftest_passes_on_this_library(name):
+    """The reference's own mpemu tests (gemm-emulation/bench/test_*.cu): split
+    exactness and sizing, the term schedule, FP16 normwise bounds,
+    mpemuMultiwordMacs, bitwise range resumability, concat == range."""
+    rc, out, err = run(mpemu_bin(name, "b200"), [])
+    assert rc == 0 and "ALL PASSED" in out, (out[-3000:], err[-2000:])
+    assert "FAIL" not in out.replace("FAILED", ""), out[-3000:]
+
+
+def table(out, first):
+    """Rows of a CSV table printed after a header line starting with `first`."""
+    lines = out.splitlines()
+    start = next(i for i, ln in enumerate(lines) if ln.startswith(first))
+    hdr = lines[start].split(",")
+    return [dict(zip(hdr, ln.split(","))) for ln in lines[start + 1:] if ln.count(",") == len(hdr) - 1]
+
+
+@pytest.mark.parametrize("extra", [[], ["--exp-range", "8"]], ids=["uniform", "exp8"])
+def test_reference_mpemu_bench_accuracy(extra):
+    """gemm-emulation/bench/bench.cu on both libraries: BF16 3-split emulation
+    at 1, 3, 6 and 9 products against cublasDgemm, beside cublasSgemm.  This
+    library's error is at most the reference's at every product count and
+    shape, and within 2x native SGEMM's from 6 products on."""
+    args = ["--square", "--max-dim", "4096", "--reps", "2", "--warmup", "1", *extra]
+    res = {}
+    for side in ("ref", "b200"):
+        rc, out, err = run(mpemu_bin("bench", side), args)
+        assert rc == 0, err[-2000:]
+        res[side] = {(r["m"], r["method"], r["macs"]): r for r in table(out, "shape,")}
+    assert res["b200"].keys() == res["ref"].keys() and res["b200"]
+    for key, r in res["b200"].items():
+        q = res["ref"][key]
+        if key[1] != "mpemu":
+            continue
+        sg = res["b200"][(key[0], "cublasSgemm", "0")]
+        print(key, "ours", r["rel_frob"], r["rel_max"], r["tflops_gemm"], "ref", q["rel_frob"], q["rel_max"],
+              q["tflops_gemm"], "sgemm", sg["rel_frob"], sg["rel_max"])
+        assert float(r["rel_frob"]) <= float(q["rel_frob"]) * 1.05, (key, r["rel_frob"], q["rel_frob"])
+        if int(key[2]) >= 6:
+            assert float(r["rel_frob"]) <= 2 * float(sg["rel_frob"]), (key, r["rel_frob"], sg["rel_frob"])
+            assert float(r["rel_max"]) <= 2 * float(sg["rel_max"]), (key, r["rel_max"], sg["rel_max"])
+
+
+def test_reference_mpemu_bench_mw_accuracy():
+    """gemm-emulation/bench/bench_mw.cu (multiword FP16: 1, 2 and 3 words) on
+    both libraries: this library's error is at most the reference's for every
+    configuration and shape."""
+    args = ["--square", "--max-dim", "4096", "--reps", "2", "--warmup", "1"]
+    res = {}
+    for side in ("ref", "b200"):
+        rc, out, err = run(mpemu_bin("bench_mw", side), args)
+        assert rc == 0, err[-2000:]
+        res[side] = {(r["m"], r["method"], r["macs"]): r for r in table(out, "shape,")}
+    assert res["b200"].keys() == res["ref"].keys() and res["b200"]
+    for key, r in res["b200"].items():
+        q = res["ref"][key]
+        print(key, "ours", r["rel_frob"], r["rel_max"], r["tflops_gemm"], "ref", q["rel_frob"], q["rel_max"],
+              q["tflops_gemm"])
+        if key[1] in ("cublasSgemm", "cublasDgemm") or not r["rel_frob"]:
+            continue
+        assert float(r["rel_frob"]) <= float(q["rel_frob"]) * 1.05, (key, r["rel_frob"], q["rel_frob"])
+
+
+def test_reference_accum_probe():
+    """gemm-emulation/bench/accum_probe.cu: one BF16 product on inputs that are
+    exact in BF16, so all error is accumulation error.  At k = 512 both
+    libraries run one 512-deep tensor-core accumulation and agree (2.9x SGEMM's
+    error); beyond it the reference's cuBLAS GEMM keeps accumulating in the
+    tensor core while this library sums 512-deep partials with round-to-nearest,
+    so its error is at most the reference's at every k."""
+    res = {}
+    for side in ("ref", "b200"):
+        rc, out, err = run(mpemu_bin("accum_probe", side), ["1024"])
+        assert rc == 0, err[-2000:]
+        res[side] = {r["k"]: r for r in table(out, "k,")}
+    assert res["b200"].keys() == res["ref"].keys() and len(res["b200"]) == 6
+    for kk, r in res["b200"].items():
+        q = res["ref"][kk]
+        print(kk, "ours", r["bf16_tc_relfrob"], r["ratio"], "ref", q["bf16_tc_relfrob"], q["ratio"])
+        assert float(r["bf16_tc_relfrob"]) <= float(q["bf16_tc_relfrob"]) * 1.05, (kk, r, q)
