@@ -246,6 +246,10 @@ def run_ours(args, world, rank, local):
         pmax = torch.maximum(P.abs().max(), C0.abs().max()).reshape(1)
         dist.all_reduce(pmax, op=dist.ReduceOp.MAX)
     torch.cuda.synchronize()
+    # one GPU: the engine runs on a side stream, where mpkEngineIterate can capture an iteration
+    # as CUDA graphs and replay it; with ranks, the allreduce sits between accumulate and finalize
+    if world == 1:
+        torch.cuda.set_stream(torch.cuda.Stream(dev))
     stream = torch.cuda.current_stream(dev).cuda_stream
     eng = M.Engine(P, K, pmax_global=float(pmax.item()), n_global=n_total, stream=stream)
     labels = torch.empty(n_local, dtype=torch.int32, device=dev)
@@ -253,10 +257,12 @@ def run_ours(args, world, rank, local):
     C = C0.clone()
 
     def step():
+        if world == 1:
+            eng.iterate(C, labels, sums, 1)
+            return
         eng.assign(C, labels)
         eng.accumulate(labels, sums)
-        if world > 1:
-            dist.all_reduce(sums)
+        dist.all_reduce(sums)
         eng.finalize(sums, C)
 
     for _ in range(args.warmup):
@@ -300,6 +306,8 @@ def run_ours(args, world, rank, local):
     if cnt["status"] != 0:
         raise RuntimeError(f"engine device status {cnt['status']}")
     eng.close()
+    torch.cuda.synchronize()
+    torch.cuda.set_stream(torch.cuda.default_stream(dev))
     return res
 
 
@@ -454,7 +462,8 @@ def run_reference(args, world, rank, local):
 def run_sgemm(n=8192, reps=5):
     """BASELINE config 2 through the mpemu C ABI: C = A B (column major), M = N = K = n, FP32 inputs
     (a) U[-1,1] and (b) u * 2^e with e uniform in {-8..8}, device-generated and seeded.  Times the
-    BF16 3-word split with 3, 6 and 9 products and the scaled FP16 2-word split with 3 products
+    BF16 3-word split with 3, 6 and 9 products and the scaled FP16 split with 2 words / 3 products and
+    3 words / 6 products
     (split words resident; CUDA events; the operands are 3 x 128 MB planes each, larger than the L2),
     native FP32 SGEMM (TF32 off) and cuBLAS BF16 for context; error = max |C - C_fp64|."""
     import mpkmeans_b200 as M
@@ -490,15 +499,15 @@ def run_sgemm(n=8192, reps=5):
         st = lds * n
         SA = torch.empty(st * 3, dtype=torch.int16, device=dev)
         SB = torch.empty_like(SA)
-        HA = torch.empty(st * 2, dtype=torch.int16, device=dev)
+        HA = torch.empty(st * 3, dtype=torch.int16, device=dev)
         HB = torch.empty_like(HA)
         sa, sb = ctypes.c_float(), ctypes.c_float()
         ok = (L.mpemuSplitBF16(A.data_ptr(), n, n, n, 3, SA.data_ptr(), lds, st, None) == 0 and
               L.mpemuSplitBF16(B.data_ptr(), n, n, n, 3, SB.data_ptr(), lds, st, None) == 0 and
               L.mpemuAutoScaleFP16(A.data_ptr(), n, n, n, ctypes.byref(sa), None) == 0 and
               L.mpemuAutoScaleFP16(B.data_ptr(), n, n, n, ctypes.byref(sb), None) == 0 and
-              L.mpemuSplitFP16(A.data_ptr(), n, n, n, 2, sa.value, HA.data_ptr(), lds, st, None) == 0 and
-              L.mpemuSplitFP16(B.data_ptr(), n, n, n, 2, sb.value, HB.data_ptr(), lds, st, None) == 0)
+              L.mpemuSplitFP16(A.data_ptr(), n, n, n, 3, sa.value, HA.data_ptr(), lds, st, None) == 0 and
+              L.mpemuSplitFP16(B.data_ptr(), n, n, n, 3, sb.value, HB.data_ptr(), lds, st, None) == 0)
         if not ok:
             raise RuntimeError("mpemu split failed")
         Am, Bm = A.view(n, n), B.view(n, n)      # column-major A B == row-major (B_rm @ A_rm)
@@ -519,18 +528,22 @@ def run_sgemm(n=8192, reps=5):
             res[name] = {"ms": t, "tflops": flop / t / 1e9, "tensor_tflops": macs * flop / t / 1e9,
                          "max_err": err()}
 
-        def f16():
-            rc = L.mpemuGemmMultiwordRange(h, 0, 0, n, n, n, 1.0, HA.data_ptr(), lds, st, sa.value, HB.data_ptr(),
-                                           lds, st, sb.value, 2, 0, 3, 0.0, C.data_ptr(), n)
-            if rc != 0:
-                raise RuntimeError(f"mpemuGemmMultiwordRange: {rc}")
-        t = timeit(f16)
-        res["fp16x3"] = {"ms": t, "tflops": flop / t / 1e9, "tensor_tflops": 3 * flop / t / 1e9, "max_err": err()}
+        # scaled FP16 words (the 3-word split's first two words are the 2-word split): 2 words with
+        # 3 products (double-fp16) and 3 words with 6 products (triple-fp16)
+        for name, words, macs in (("fp16x3", 2, 3), ("fp16x6", 3, 6)):
+            def f16(words=words, macs=macs):
+                rc = L.mpemuGemmMultiwordRange(h, 0, 0, n, n, n, 1.0, HA.data_ptr(), lds, st, sa.value,
+                                               HB.data_ptr(), lds, st, sb.value, words, 0, macs, 0.0, C.data_ptr(), n)
+                if rc != 0:
+                    raise RuntimeError(f"mpemuGemmMultiwordRange: {rc}")
+            t = timeit(f16)
+            res[name] = {"ms": t, "tflops": flop / t / 1e9, "tensor_tflops": macs * flop / t / 1e9,
+                         "max_err": err()}
         # native SGEMM last: its long calls heat the GPU, and the emulated calls are timed first
         t = timeit(lambda: torch.matmul(Bm, Am, out=C.view(n, n)))
         res["native_sgemm"] = {"ms": t, "tflops": flop / t / 1e9, "max_err": err()}
         nat = res["native_sgemm"]["max_err"]
-        for name in ("bf16x3", "bf16x6", "bf16x9", "fp16x3"):
+        for name in ("bf16x3", "bf16x6", "bf16x9", "fp16x3", "fp16x6"):
             res[name]["err_vs_native"] = res[name]["max_err"] / nat if nat > 0 else None
             res[name]["speedup_vs_native"] = res[name]["tflops"] / res["native_sgemm"]["tflops"]
         out[case] = res

@@ -265,6 +265,13 @@ mpkStatus mpkEngineAssign(mpkEngine e, const float* dC, int* dAssign, int refine
 mpkStatus mpkEngineAccumulate(mpkEngine e, const int* dAssign, long long* dSums);
 /* dC = finalised centroids from (globally reduced) dSums; dMoved2 may be NULL */
 mpkStatus mpkEngineFinalize(mpkEngine e, const long long* dSums, float* dC, float* dMoved2);
+/* iters whole Lloyd iterations of this engine alone -- assign, accumulate,
+ * finalize in turn, no collective between -- with exactly their result.  The
+ * first call for a given (dC, dAssign, dSums, refine) captures one iteration
+ * as two CUDA graphs (assignment; update) and later calls replay them, so
+ * small problems are not held to the host's launch rate.  On the legacy
+ * default stream (not capturable) it launches the kernels directly. */
+mpkStatus mpkEngineIterate(mpkEngine e, float* dC, int* dAssign, long long* dSums, int iters, int refine);
 /* FP64 inertia of this shard, returned to the host (synchronises) */
 mpkStatus mpkEngineInertia(mpkEngine e, const float* dC, const int* dAssign, double* out);
 int mpkEngineFracBits(mpkEngine e);          /* synchronises once */

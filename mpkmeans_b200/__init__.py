@@ -119,6 +119,7 @@ SIGNATURES = {
     "mpkEngineAssign": (_I, [_P, _P, _P, _I]),
     "mpkEngineAccumulate": (_I, [_P, _P, _P]),
     "mpkEngineFinalize": (_I, [_P, _P, _P, _P]),
+    "mpkEngineIterate": (_I, [_P, _P, _P, _P, _I, _I]),
     "mpkEngineInertia": (_I, [_P, _P, _P, ctypes.POINTER(_D)]),
     "mpkEngineFracBits": (_I, [_P]),
     "mpkEngineCounters": (_I, [_P, ctypes.POINTER(_LL), ctypes.POINTER(_LL), ctypes.POINTER(_LL),
@@ -319,6 +320,12 @@ class Engine:
 
     def finalize(self, sums, C, moved2=None) -> None:
         check("mpkEngineFinalize", lib().mpkEngineFinalize(self.h, _ptr(sums), _ptr(C), _ptr(moved2)))
+
+    def iterate(self, C, labels, sums, iters: int = 1, refine: bool = True) -> None:
+        """``iters`` Lloyd iterations of this shard alone (assign, accumulate,
+        finalize), replayed from CUDA graphs after the first call."""
+        check("mpkEngineIterate", lib().mpkEngineIterate(self.h, _ptr(C), _ptr(labels), _ptr(sums), int(iters),
+                                                         int(bool(refine))))
 
     def inertia(self, C, labels) -> float:
         out = ctypes.c_double()

@@ -30,7 +30,7 @@ struct DevParams {
     unsigned long long ncand_total;  /* candidate centroids refined, over run */
     unsigned long long novf_total;   /* rows whose class rescans ran, or whose wide list overflowed */
     unsigned int nwide;              /* rows handed to the wide refinement by the last assign */
-    unsigned int pad0;
+    unsigned int hist_next;          /* next survivor-history slot the refinement writes */
     unsigned long long nwide_total;  /* wide rows over the run */
     unsigned long long wait_ns;      /* limit of one wait in the assignment kernel (0: 4 s) */
 };
@@ -115,8 +115,8 @@ cudaError_t launch_assign(const AssignArgs& a, cudaStream_t s);
 /* ---- refine / update (kernels.cu) ---- */
 void launch_refine(const float* P, const float* C, const float* cn, int d, int k, int bn,
                    const RefineEntry* list, DevParams* prm, int* labels, long long n_cap,
-                   unsigned long long* hist_slot, const __half* Xs, long long n, int dp, const WideScratch& w,
-                   int num_sms, cudaStream_t s);
+                   unsigned long long* hist, int hist_cap, const __half* Xs, long long n, int dp,
+                   const WideScratch& w, int num_sms, cudaStream_t s);
 void launch_wide_gather(const RefineEntry* list, const __half* Xs, long long n, int dp, const WideScratch& w,
                         long long base, const DevParams* prm, int num_sms, cudaStream_t s);
 void launch_refine_wide(const float* P, const float* C, const float* cn, int d, int k, const RefineEntry* list,

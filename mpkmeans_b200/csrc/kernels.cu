@@ -204,7 +204,7 @@ __global__ void k_wide_gather(const RefineEntry* __restrict__ list, const __half
 template <int NR>
 __global__ void k_refine(const float* __restrict__ P, const float* __restrict__ C, const float* __restrict__ cn,
                          int d, int k, int bn, const RefineEntry* __restrict__ list, DevParams* __restrict__ prm,
-                         int* __restrict__ labels, long long cap, unsigned long long* hist_slot,
+                         int* __restrict__ labels, long long cap, unsigned long long* hist, int hist_cap,
                          const __half* __restrict__ Xs, long long n, int dp, WideScratch w) {
     constexpr int R = NR > 0 ? NR : 1;
     const int lane = threadIdx.x & 31;
@@ -278,7 +278,11 @@ __global__ void k_refine(const float* __restrict__ P, const float* __restrict__ 
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         atomicAdd(&prm->nflag_total, (unsigned long long)nf);
-        if (hist_slot) *hist_slot = (unsigned long long)nf;
+        if (hist) {                       /* slot from the device counter: a graph replay records too */
+            const unsigned it = prm->hist_next;
+            if (it < (unsigned)hist_cap) hist[it] = (unsigned long long)nf;
+            prm->hist_next = it + 1;
+        }
     }
 }
 
@@ -471,12 +475,14 @@ void launch_refine_wide(const float* P, const float* C, const float* cn, int d, 
 }
 
 void launch_refine(const float* P, const float* C, const float* cn, int d, int k, int bn, const RefineEntry* list,
-                   DevParams* prm, int* labels, long long n_cap, unsigned long long* hist_slot, const __half* Xs,
-                   long long n, int dp, const WideScratch& w, int num_sms, cudaStream_t s) {
+                   DevParams* prm, int* labels, long long n_cap, unsigned long long* hist, int hist_cap,
+                   const __half* Xs, long long n, int dp, const WideScratch& w, int num_sms, cudaStream_t s) {
     if (d <= 256)
-        k_refine<8><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, bn, list, prm, labels, n_cap, hist_slot, Xs, n, dp, w);
+        k_refine<8><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, bn, list, prm, labels, n_cap, hist, hist_cap, Xs, n,
+                                                 dp, w);
     else
-        k_refine<0><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, bn, list, prm, labels, n_cap, hist_slot, Xs, n, dp, w);
+        k_refine<0><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, bn, list, prm, labels, n_cap, hist, hist_cap, Xs, n,
+                                                 dp, w);
 }
 
 void launch_finalize_fixed(const long long* sums, const long long* counts, int k, int d, const DevParams* prm,

@@ -177,7 +177,27 @@ struct mpkEngine_s {
     long long launches = 0;               /* kernels this engine has launched */
     bool prof = false;                    /* bench hook: events around the hot kernels */
     std::vector<cudaEvent_t> ev_assign, ev_accum;
+    /* mpkEngineIterate: one iteration as two graphs (assignment; update),
+     * captured for these buffers and this refine flag */
+    struct {
+        cudaGraphExec_t assign = nullptr, update = nullptr;
+        const float* C = nullptr;
+        const int* A = nullptr;
+        const long long* S = nullptr;
+        int refine = -1;
+        long long n_assign = 0, n_update = 0;   /* kernels per replay */
+    } g;
 };
+
+static void graphs_release(mpkEngine e) {
+    if (e->g.assign) cudaGraphExecDestroy(e->g.assign);
+    if (e->g.update) cudaGraphExecDestroy(e->g.update);
+    e->g.assign = e->g.update = nullptr;
+    e->g.C = nullptr;
+    e->g.A = nullptr;
+    e->g.S = nullptr;
+    e->g.refine = -1;
+}
 
 static void prof_mark(mpkEngine e, std::vector<cudaEvent_t>& v) {
     if (!e->prof) return;
@@ -198,6 +218,7 @@ static void prof_clear(mpkEngine e) {
 static void engine_free(mpkEngine e) {
     if (!e) return;
     prof_clear(e);
+    graphs_release(e);
     void* bufs[] = {e->Xs, e->xnorm, e->Cs, e->cn, e->list, e->prm, e->dInertia, e->hist,
                     e->us.perm, e->us.bin_start, e->us.cursor, e->us.hist,
                     e->wide.Xw, e->wide.went, e->wide.cand, e->wide.ccount};
@@ -324,7 +345,9 @@ bool make_tmap_planes(CUtensorMap* map, const __half* base, long long rows, int 
 }
 }  /* namespace mpk */
 
-static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int refine, int hist_it) {
+/* record_hist: the refinement writes its entry count to the next slot of the
+ * engine's survivor history (prm->hist_next counts the slots used). */
+static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int refine, bool record_hist) {
     if (!e->can_assign) return MPK_ERR_INVALID;
     cudaMemsetAsync(&e->prm->nflag, 0, sizeof(unsigned int), e->s);
     cudaMemsetAsync(&e->prm->nwide, 0, sizeof(unsigned int), e->s);
@@ -362,7 +385,7 @@ static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int r
     }
     if (refine) {
         launch_refine(e->P, dC, e->cn, e->d, e->k, assign_bn_for(e->k), e->list, e->prm, dAssign, e->n,
-                      (hist_it >= 0 && hist_it < MPK_MAX_HIST) ? e->hist + hist_it : nullptr, e->Xs, e->n, e->dp,
+                      record_hist ? e->hist : nullptr, MPK_MAX_HIST, e->Xs, e->n, e->dp,
                       e->wide, e->num_sms, e->s);
         ++e->launches;
         /* rows the refinement queued: per round, a tensor-core pass that lists their
@@ -392,6 +415,29 @@ static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int r
         }
     }
     return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
+}
+
+/* Capture body() on gs (a non-default stream) into an executable graph.
+ * false, with no graph, when the capture or the instantiation fails. */
+template <typename F>
+static bool capture_graph(cudaStream_t gs, F&& body, cudaGraphExec_t* exec) {
+    *exec = nullptr;
+    cudaGraph_t g = nullptr;
+    if (cudaStreamBeginCapture(gs, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    const mpkStatus st = body();
+    const cudaError_t ec = cudaStreamEndCapture(gs, &g);
+    const bool ok = st == MPK_OK && ec == cudaSuccess && g != nullptr &&
+                    cudaGraphInstantiate(exec, g, 0) == cudaSuccess;
+    if (g) cudaGraphDestroy(g);
+    if (!ok) {
+        if (*exec) cudaGraphExecDestroy(*exec);
+        *exec = nullptr;
+        cudaGetLastError();
+    }
+    return ok;
 }
 
 static mpkStatus engine_accumulate(mpkEngine e, const int* dAssign, long long* dSums) {
@@ -426,7 +472,7 @@ mpkStatus mpkEngineDestroy(mpkEngine e) {
 
 mpkStatus mpkEngineAssign(mpkEngine e, const float* dC, int* dAssign, int refine) {
     if (!e || !dC || (e->n > 0 && !dAssign)) return MPK_ERR_INVALID;
-    return engine_assign(e, dC, dAssign, refine, -1);
+    return engine_assign(e, dC, dAssign, refine, false);
 }
 
 mpkStatus mpkEngineAccumulate(mpkEngine e, const int* dAssign, long long* dSums) {
@@ -437,6 +483,58 @@ mpkStatus mpkEngineAccumulate(mpkEngine e, const int* dAssign, long long* dSums)
 mpkStatus mpkEngineFinalize(mpkEngine e, const long long* dSums, float* dC, float* dMoved2) {
     if (!e || !dSums || !dC) return MPK_ERR_INVALID;
     return engine_finalize(e, dSums, dC, dMoved2);
+}
+
+mpkStatus mpkEngineIterate(mpkEngine e, float* dC, int* dAssign, long long* dSums, int iters, int refine) {
+    if (!e || !dC || !dAssign || !dSums || iters < 0 || !e->can_assign) return MPK_ERR_INVALID;
+    auto assign = [&] { return engine_assign(e, dC, dAssign, refine, false); };
+    auto update = [&] {
+        const mpkStatus a = engine_accumulate(e, dAssign, dSums);
+        return a != MPK_OK ? a : engine_finalize(e, dSums, dC, nullptr);
+    };
+    /* graphs need a capturable stream, and no test hook that a replay would freeze */
+    const bool graphable = e->s != nullptr && e->s != cudaStreamLegacy && e->s != cudaStreamPerThread &&
+                           e->dbg == nullptr && e->stall < 0;
+    bool have = e->g.assign && e->g.C == dC && e->g.A == dAssign && e->g.S == dSums && e->g.refine == refine;
+    if (graphable && !have && iters > 0) {
+        graphs_release(e);
+        const bool prof = e->prof;
+        const long long l0 = e->launches;
+        e->prof = false;
+        bool ok = capture_graph(e->s, assign, &e->g.assign);
+        const long long l1 = e->launches;
+        ok = ok && capture_graph(e->s, update, &e->g.update);
+        const long long l2 = e->launches;
+        e->prof = prof;
+        e->launches = l0;                         /* captured, not yet run */
+        if (ok) {
+            e->g.C = dC;
+            e->g.A = dAssign;
+            e->g.S = dSums;
+            e->g.refine = refine;
+            e->g.n_assign = l1 - l0;
+            e->g.n_update = l2 - l1;
+            have = true;
+        } else {
+            graphs_release(e);
+        }
+    }
+    for (int i = 0; i < iters; ++i) {
+        if (have && graphable) {
+            prof_mark(e, e->ev_assign);
+            if (cudaGraphLaunch(e->g.assign, e->s) != cudaSuccess) return MPK_ERR_CUDA;
+            prof_mark(e, e->ev_assign);
+            prof_mark(e, e->ev_accum);
+            if (cudaGraphLaunch(e->g.update, e->s) != cudaSuccess) return MPK_ERR_CUDA;
+            prof_mark(e, e->ev_accum);
+            e->launches += e->g.n_assign + e->g.n_update;
+        } else {
+            mpkStatus st = assign();
+            if (st == MPK_OK) st = update();
+            if (st != MPK_OK) return st;
+        }
+    }
+    return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
 }
 
 mpkStatus mpkEngineInertia(mpkEngine e, const float* dC, const int* dAssign, double* out) {
@@ -634,6 +732,7 @@ mpkStatus mpkShiftCentroids(float* dC, int k, int d, float delta) {
 
 /* ------------------------------------------------------------ drivers --- */
 
+
 static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k, float* dC, int* dAssign,
                        const mpkParams* params, mpkStats* stats, bool force_refine, const char* tag) {
     if (n <= 0 || d <= 0 || k <= 0 || k > n || !dP || !dC || !dAssign) return MPK_ERR_INVALID;
@@ -664,6 +763,10 @@ static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k
     const int iters_cap = P.max_iter > 0 ? P.max_iter : 0;
     std::vector<cudaEvent_t> ev((size_t)iters_cap * 4, nullptr);
     int it = 0;
+    cudaStream_t gs = nullptr;
+    cudaEvent_t ev_join = nullptr;
+    cudaGraphExec_t g_assign = nullptr, g_update = nullptr;
+    bool try_graphs = true;
     if (dev_alloc((void**)&sums, ((size_t)k * d + k) * sizeof(long long), s) != cudaSuccess ||
         dev_alloc((void**)&moved2, (size_t)k * sizeof(float), s) != cudaSuccess) {
         st = MPK_ERR_ALLOC;
@@ -671,18 +774,48 @@ static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k
     }
     for (auto& x : ev) cudaEventCreate(&x);
 
+    /* The iterations run on a private stream gs, ordered after the caller's
+     * stream and before it again at the end.  Iteration 0 launches its
+     * kernels directly; from iteration 1 on, the assignment and the update
+     * are two CUDA graphs captured once and replayed, so that a small problem
+     * is not held to the host's kernel-launch rate.  (If a capture fails the
+     * iterations keep launching directly.) */
+    if (cudaStreamCreateWithFlags(&gs, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ev_join, cudaEventDisableTiming) != cudaSuccess) {
+        st = MPK_ERR_CUDA;
+        goto done;
+    }
+    cudaEventRecord(ev_join, s);
+    cudaStreamWaitEvent(gs, ev_join, 0);
+    e->s = gs;
     for (it = 0; it < iters_cap; ++it) {
-        cudaEventRecord(ev[4 * it + 0], s);
-        if ((st = engine_assign(e, dC, dAssign, refine, it)) != MPK_OK) goto done;
-        cudaEventRecord(ev[4 * it + 1], s);
-        if ((st = engine_accumulate(e, dAssign, sums)) != MPK_OK) goto done;
-        if ((st = engine_finalize(e, sums, dC, moved2)) != MPK_OK) goto done;
-        cudaEventRecord(ev[4 * it + 2], s);
+        cudaEventRecord(ev[4 * it + 0], gs);
+        if (it == 1 && try_graphs) {
+            try_graphs = capture_graph(gs, [&] { return engine_assign(e, dC, dAssign, refine, true); }, &g_assign) &&
+                         capture_graph(gs, [&] {
+                             const mpkStatus a = engine_accumulate(e, dAssign, sums);
+                             return a != MPK_OK ? a : engine_finalize(e, sums, dC, moved2);
+                         }, &g_update);
+        }
+        const bool replay = it >= 1 && try_graphs;
+        if (replay) {
+            if (cudaGraphLaunch(g_assign, gs) != cudaSuccess) { st = MPK_ERR_CUDA; goto done; }
+        } else if ((st = engine_assign(e, dC, dAssign, refine, true)) != MPK_OK) {
+            goto done;
+        }
+        cudaEventRecord(ev[4 * it + 1], gs);
+        if (replay) {
+            if (cudaGraphLaunch(g_update, gs) != cudaSuccess) { st = MPK_ERR_CUDA; goto done; }
+        } else {
+            if ((st = engine_accumulate(e, dAssign, sums)) != MPK_OK) goto done;
+            if ((st = engine_finalize(e, sums, dC, moved2)) != MPK_OK) goto done;
+        }
+        cudaEventRecord(ev[4 * it + 2], gs);
         S->hp_baseline += (long long)n * k;
         S->tested += (long long)n * (k - 1);
         if (P.tol > 0.f || P.verbose) {
-            cudaMemcpyAsync(h_moved.data(), moved2, (size_t)k * sizeof(float), cudaMemcpyDeviceToHost, s);
-            if (cudaStreamSynchronize(s) != cudaSuccess) { st = MPK_ERR_CUDA; goto done; }
+            cudaMemcpyAsync(h_moved.data(), moved2, (size_t)k * sizeof(float), cudaMemcpyDeviceToHost, gs);
+            if (cudaStreamSynchronize(gs) != cudaSuccess) { st = MPK_ERR_CUDA; goto done; }
             double fro2 = 0.0;
             for (int j = 0; j < k; ++j) fro2 += (double)h_moved[j];
             if (P.verbose) fprintf(stderr, "[%s] iter %3d  ||dC||_F^2 %.6e\n", tag, it, fro2);
@@ -690,6 +823,9 @@ static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k
         }
     }
     S->iters = it;
+    cudaEventRecord(ev_join, gs);
+    cudaStreamWaitEvent(s, ev_join, 0);
+    e->s = s;
     cudaEventRecord(ev_all1, s);
     if (cudaStreamSynchronize(s) != cudaSuccess) { st = MPK_ERR_CUDA; goto done; }
     {
@@ -720,7 +856,15 @@ static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k
         if (mpkEngineInertia(e, dC, dAssign, &S->inertia) != MPK_OK) st = MPK_ERR_CUDA;
     }
 done:
+    if (gs) {
+        cudaStreamSynchronize(gs);
+        if (e) e->s = s;
+    }
     cudaStreamSynchronize(s);
+    if (g_assign) cudaGraphExecDestroy(g_assign);
+    if (g_update) cudaGraphExecDestroy(g_update);
+    if (ev_join) cudaEventDestroy(ev_join);
+    if (gs) cudaStreamDestroy(gs);
     for (auto& x : ev) if (x) cudaEventDestroy(x);
     cudaEventDestroy(ev_all0);
     cudaEventDestroy(ev_all1);
@@ -785,7 +929,7 @@ mpkStatus mpkAssign(cublasHandle_t blas, const float* dP, int n, int d, int k, c
     mpkEngine e = nullptr;
     mpkStatus st = engine_create(&e, dP, n, d, k, dC, 0.f, n, s, true);
     if (st != MPK_OK) return st;
-    st = engine_assign(e, dC, dAssign, refine, 0);
+    st = engine_assign(e, dC, dAssign, refine, false);
     if (st == MPK_OK && stats) {
         std::memset(stats, 0, sizeof(*stats));
         long long rows = 0, cands = 0, full = 0;

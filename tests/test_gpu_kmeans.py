@@ -383,6 +383,64 @@ def test_engine_empty_and_tiny_shards(cuda):
     assert torch.equal(tot, sums)
 
 
+def test_engine_iterate_graphs_equal_steps(cuda):
+    """mpkEngineIterate replays one iteration from two CUDA graphs on a
+    capturable stream; its centroids, labels and sums equal the three steps
+    called in turn, bit for bit, with the wide refinement in the graph too
+    (k = 512 > 256), and a second call with other buffers recaptures."""
+    P, C = make_problem(40000, 48, 512, seed=13)
+    dP = dev(P)
+    pmax = float(max(np.abs(P).max(), np.abs(C).max()))
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        with M.Engine(dP, 512, pmax_global=pmax, stream=side.cuda_stream) as e:
+            lab_a = torch.empty(40000, dtype=torch.int32, device="cuda")
+            sums_a = torch.empty(e.sums_length, dtype=torch.int64, device="cuda")
+            C_a = dev(C)
+            l0 = e.launches()
+            for _ in range(6):
+                e.assign(C_a, lab_a)
+                e.accumulate(lab_a, sums_a)
+                e.finalize(sums_a, C_a)
+            per_iter = (e.launches() - l0) // 6
+            lab_b = torch.empty_like(lab_a)
+            sums_b = torch.empty_like(sums_a)
+            C_b = dev(C)
+            l1 = e.launches()
+            e.iterate(C_b, lab_b, sums_b, 1)
+            e.iterate(C_b, lab_b, sums_b, 5)
+            assert e.launches() - l1 == 6 * per_iter
+            C_c = dev(C)
+            lab_c = torch.empty_like(lab_a)
+            e.iterate(C_c, lab_c, sums_b, 6)
+            side.synchronize()
+            assert e.counters()["status"] == 0
+    assert torch.equal(C_b, C_a) and torch.equal(lab_b, lab_a) and torch.equal(sums_b, sums_a)
+    assert torch.equal(C_c, C_a) and torch.equal(lab_c, lab_a)
+    # the legacy default stream cannot be captured: direct launches, same result
+    with M.Engine(dP, 512, pmax_global=pmax) as e:
+        C_d = dev(C)
+        lab_d = torch.empty_like(lab_a)
+        sums_d = torch.empty_like(sums_a)
+        e.iterate(C_d, lab_d, sums_d, 6)
+        torch.cuda.synchronize()
+    assert torch.equal(C_d, C_a) and torch.equal(lab_d, lab_a)
+
+
+def test_lloyd_graph_replay_survivor_history(cuda):
+    """mpkMeansMixed replays iterations 1.. from graphs: the survivor history,
+    whose slot the refinement takes from a device counter, still holds one
+    entry per iteration and nothing past the last."""
+    P = O.make_config1(60_000, 32, seed=9)
+    C0 = O.kmeanspp(P, 64, seed=9)
+    lab = torch.empty(60_000, dtype=torch.int32, device="cuda")
+    st = M.means_mixed(dev(P), dev(C0), lab, M.params_init(max_iter=12))
+    assert st.iters == 12 and st.n_hist == 12
+    hist = [st.hist_survivors[i] for i in range(12)]
+    assert all(h >= 0 for h in hist) and sum(hist) > 0
+    assert st.hist_survivors[12] == 0
+
+
 def test_mg_entry_single_gpu_matches(cuda):
     P = O.make_config1(50_000, 32, seed=5)
     C0 = O.kmeanspp(P, 64, seed=5)
