@@ -105,6 +105,10 @@ __global__ void k_prep_c(const float* __restrict__ C, int k, int d, int dp, DevP
         if (t == 0) cn[j] = INFINITY;
         return;
     }
+    if (j == 0 && t == 0) {              /* the assignment that follows counts from zero */
+        prm->nflag = 0;
+        prm->nwide = 0;
+    }
     const float* c = C + (size_t)j * d;
     const float s = prm->scale;
     float acc = 0.f;

@@ -349,8 +349,6 @@ bool make_tmap_planes(CUtensorMap* map, const __half* base, long long rows, int 
  * engine's survivor history (prm->hist_next counts the slots used). */
 static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int refine, bool record_hist) {
     if (!e->can_assign) return MPK_ERR_INVALID;
-    cudaMemsetAsync(&e->prm->nflag, 0, sizeof(unsigned int), e->s);
-    cudaMemsetAsync(&e->prm->nwide, 0, sizeof(unsigned int), e->s);
     launch_prep_c(dC, e->k, e->kpad, e->d, e->dp, e->prm, e->Cs, e->cn, e->s);
     ++e->launches;
     if (e->n == 0) return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
