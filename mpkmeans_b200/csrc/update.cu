@@ -115,8 +115,10 @@ __device__ __forceinline__ long long quantise(float x, float sc) {
 
 /* Segmented sum over the label-sorted rows.  VEC = 4: lane l owns features
  * 4l..4l+3 of every 128-feature group (float4 loads); VEC = 1: lane l owns
- * features l, l+32, ...  NG groups per lane cover d. */
-template <int VEC, int NG>
+ * features l, l+32, ...  NG groups per lane cover d.  U rows are loaded at
+ * once; a narrow row (d <= 64: half the lanes or fewer hold a feature) takes
+ * U = 8, since each load then moves little. */
+template <int VEC, int NG, int U = (NG <= 2 ? 4 : (NG <= 4 ? 2 : 1))>
 __global__ void __launch_bounds__(256)
 k_segsum(const float* __restrict__ P, int d, int f0, const int* __restrict__ perm, const int* __restrict__ bin_start,
          int k, const DevParams* __restrict__ prm, long long* __restrict__ sums) {
@@ -158,7 +160,6 @@ k_segsum(const float* __restrict__ P, int d, int f0, const int* __restrict__ per
             }
     };
 
-    constexpr int U = NG <= 2 ? 4 : (NG <= 4 ? 2 : 1);   /* rows in flight per warp */
     for (long long e = e0; e < e1; e += U) {
         float x[U][NG][VEC];
 #pragma unroll
@@ -202,7 +203,10 @@ template <int VEC>
 void launch_segsum_window(const float* P, int d, int f0, int ng, const int* perm, const int* bin_start, int k,
                           const DevParams* prm, long long* sums, int blocks, cudaStream_t s) {
     switch (ng) {
-        case 1: k_segsum<VEC, 1><<<blocks, 256, 0, s>>>(P, d, f0, perm, bin_start, k, prm, sums); break;
+        case 1:
+            if (d <= 64) k_segsum<VEC, 1, 8><<<blocks, 256, 0, s>>>(P, d, f0, perm, bin_start, k, prm, sums);
+            else k_segsum<VEC, 1><<<blocks, 256, 0, s>>>(P, d, f0, perm, bin_start, k, prm, sums);
+            break;
         case 2: k_segsum<VEC, 2><<<blocks, 256, 0, s>>>(P, d, f0, perm, bin_start, k, prm, sums); break;
         case 3: k_segsum<VEC, 3><<<blocks, 256, 0, s>>>(P, d, f0, perm, bin_start, k, prm, sums); break;
         case 4: k_segsum<VEC, 4><<<blocks, 256, 0, s>>>(P, d, f0, perm, bin_start, k, prm, sums); break;
@@ -248,7 +252,9 @@ int launch_update_sorted(const float* P, long long n, int d, const int* labels, 
     if (smem) k_label_scatter<true><<<blocks, 512, hb, s>>>(labels, n, k, sc.cursor, sc.perm, rpb);
     else k_label_scatter<false><<<blocks, 512, 0, s>>>(labels, n, k, sc.cursor, sc.perm, rpb);
     const bool vec = (d % 4 == 0) && ((reinterpret_cast<uintptr_t>(P) & 15) == 0);
-    const int sblocks = num_sms * 8;
+    /* eight warps a block; at least 32 rows a warp, so that a small problem does not pay
+     * a bin search and a flush of atomics for every handful of rows */
+    const int sblocks = (int)std::max<long long>(1, std::min<long long>((long long)num_sms * 8, (n + 255) / 256));
     const int seg = vec ? launch_segsum<4>(P, d, sc.perm, sc.bin_start, k, prm, sums, sblocks, s)
                         : launch_segsum<1>(P, d, sc.perm, sc.bin_start, k, prm, sums, sblocks, s);
     return 3 + seg;                       /* hist, scan, scatter, segmented sums */
