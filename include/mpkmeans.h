@@ -88,9 +88,11 @@ typedef struct {
  * hp_reference (0: no per-row reference entry is needed), hp_update (FP32
  * candidate distances recomputed), tested (n*(k-1) per iteration), n_hist and
  * hist_survivors (rows refined per iteration), and the timings:
- * t_total_ms, t_prep_ms (centroid split), t_gemm_lo_ms (fused split GEMM +
- * argmin kernel), t_hp_update_ms (refinement), t_dist_ms (their sum plus the
- * one-off point split), t_update_ms (centroid update).  Other fields are 0. */
+ * t_total_ms, t_prep_ms (the one-off split of the points), t_gemm_lo_ms (the
+ * assignment steps: centroid split, fused split GEMM + argmin kernel and the
+ * refinement, which run back to back and are timed as one), t_dist_ms
+ * (t_prep_ms + t_gemm_lo_ms), t_update_ms (centroid update).  Other fields
+ * are 0. */
 typedef struct {
     int    iters;
     double inertia;

@@ -839,6 +839,7 @@ static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k
             cudaEventElapsedTime(&ms, ev[4 * t + 1], ev[4 * t + 2]);
             S->t_update_ms += ms;
         }
+        S->t_prep_ms = prep_x;
         S->t_dist_ms = prep_x + S->t_gemm_lo_ms;
         long long rows = 0, cands = 0, full = 0;
         int status = 0;
