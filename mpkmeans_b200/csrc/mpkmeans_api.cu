@@ -651,6 +651,7 @@ mpkStatus mpkDebugWideRoundRows(mpkEngine e, long long rows) {
     if (!e || rows < 1 || e->wide.cap == 0) return MPK_ERR_INVALID;
     e->wide.per_round = std::min(rows, e->wide.cap);
     e->wide.rounds = e->k >= 4096 ? (int)((e->n + e->wide.per_round - 1) / e->wide.per_round) : 1;
+    graphs_release(e);                    /* captured iterations hold the old rounds */
     return MPK_OK;
 }
 

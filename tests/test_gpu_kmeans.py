@@ -427,6 +427,38 @@ def test_engine_iterate_graphs_equal_steps(cuda):
     assert torch.equal(C_d, C_a) and torch.equal(lab_d, lab_a)
 
 
+def test_engine_iterate_graphs_multi_round_wide(cuda):
+    """Graph replay with the wide refinement in several rounds (k = 4096,
+    cancellation stress, rounds of 97 rows): the captured iteration (gather,
+    emit pass and FP32 evaluation per round) equals the steps called in turn."""
+    P, C = _offset_problem(20000, 64, 4096, seed=56)
+    dP = dev(P)
+    side = torch.cuda.Stream()
+    out = []
+    for graphs in (False, True):
+        with torch.cuda.stream(side):
+            with M.Engine(dP, 4096, C0=dev(C), stream=side.cuda_stream) as e:
+                e.wide_round_rows(97)
+                Cw = dev(C)
+                lab = torch.empty(len(P), dtype=torch.int32, device="cuda")
+                sums = torch.empty(e.sums_length, dtype=torch.int64, device="cuda")
+                if graphs:
+                    e.iterate(Cw, lab, sums, 1)
+                    e.iterate(Cw, lab, sums, 2)
+                else:
+                    for _ in range(3):
+                        e.assign(Cw, lab)
+                        e.accumulate(lab, sums)
+                        e.finalize(sums, Cw)
+                side.synchronize()
+                w = e.wide_counters()
+                assert e.counters()["status"] == 0
+        assert w["wide_rows"] > 97, w
+        out.append((Cw, lab, w["wide_rows"]))
+    assert out[0][2] == out[1][2]
+    assert torch.equal(out[0][0], out[1][0]) and torch.equal(out[0][1], out[1][1])
+
+
 def test_lloyd_graph_replay_survivor_history(cuda):
     """mpkMeansMixed replays iterations 1.. from graphs: the survivor history,
     whose slot the refinement takes from a device counter, still holds one
