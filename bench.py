@@ -37,7 +37,7 @@ import subprocess
 import sys
 import tempfile
 import time
-from datetime import timedelta
+from datetime import datetime, timedelta
 from pathlib import Path
 
 import numpy as np
@@ -181,20 +181,22 @@ def shard_rows(n, world, rank):
 # -------------------------------------------------------------- clocks ------
 
 class Clocks:
+    """nvidia-smi sampled every 50 ms while the object lives; stop(window) keeps the samples
+    whose own timestamp falls in the host wall-clock window of the timed region."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,timestamp")
 
     def __init__(self, gpu_index):
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={self.FIELDS}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                       "--format=csv,noheader,nounits", "-lms", "50"],
                                       stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
 
-    def stop(self):
+    def stop(self, window=None):
         if self.p is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.p.terminate()
@@ -203,8 +205,17 @@ class Clocks:
         except subprocess.TimeoutExpired:
             self.p.kill()
         self.f.flush()
-        rows = [l.split(",") for l in Path(self.f.name).read_text().splitlines() if l.count(",") >= 8]
+        rows = [l.split(",") for l in Path(self.f.name).read_text().splitlines() if l.count(",") >= 9]
         os.unlink(self.f.name)
+        if window is not None:
+            def stamp(r):
+                try:
+                    return datetime.strptime(r[9].strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                except ValueError:
+                    return None
+            inside = [r for r in rows if (stamp(r) or 0.0) >= window[0] - 0.025 and (stamp(r) or 0.0) <= window[1] + 0.025]
+            if inside:
+                rows = inside
         sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -275,15 +286,17 @@ def run_ours(args, world, rank, local):
     eng.profile(True)
     launches0 = eng.launches()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.time()
     e0.record()
     for _ in range(args.steps):
         step()
     e1.record()
     launches = eng.launches() - launches0
     torch.cuda.synchronize()
+    w1 = time.time()
     if world > 1:
         dist.barrier()
-    clk = clocks.stop()
+    clk = clocks.stop((w0, w1))
     prof = eng.profile_read()
     t_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
     if world > 1:
