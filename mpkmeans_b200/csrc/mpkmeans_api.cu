@@ -186,6 +186,7 @@ struct mpkEngine_s {
         const long long* S = nullptr;
         int refine = -1;
         long long n_assign = 0, n_update = 0;   /* kernels per replay */
+        bool failed = false;                    /* a capture failed: launch directly from then on */
     } g;
 };
 
@@ -492,7 +493,7 @@ mpkStatus mpkEngineIterate(mpkEngine e, float* dC, int* dAssign, long long* dSum
     };
     /* graphs need a capturable stream, and no test hook that a replay would freeze */
     const bool graphable = e->s != nullptr && e->s != cudaStreamLegacy && e->s != cudaStreamPerThread &&
-                           e->dbg == nullptr && e->stall < 0;
+                           e->dbg == nullptr && e->stall < 0 && !e->g.failed;
     bool have = e->g.assign && e->g.C == dC && e->g.A == dAssign && e->g.S == dSums && e->g.refine == refine;
     if (graphable && !have && iters > 0) {
         graphs_release(e);
@@ -515,6 +516,7 @@ mpkStatus mpkEngineIterate(mpkEngine e, float* dC, int* dAssign, long long* dSum
             have = true;
         } else {
             graphs_release(e);
+            e->g.failed = true;
         }
     }
     for (int i = 0; i < iters; ++i) {
