@@ -192,6 +192,8 @@ def test_golden_config1():
             lab = O.assign_fp32(P, C)
             s = parity.summary(P, C, lab, g["traj_labels"][t].astype(np.int32))
             assert s["max_gap32"] < 1e-5 and s["agree"] >= 0.9999, (t, s)
+            Cn, _, _ = O.update_fp64(P, g["traj_labels"][t].astype(np.int32), C)
+            assert np.allclose(Cn, g["traj_C"][t], rtol=1e-6, atol=1e-6), t
             C = g["traj_C"][t]
     lab, C, ine, _ = O.lloyd(P, C0, 20)
     assert (lab == g["labels"].astype(np.int32)).mean() >= 0.999
