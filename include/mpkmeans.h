@@ -91,8 +91,13 @@ typedef struct {
  * t_total_ms, t_prep_ms (the one-off split of the points), t_gemm_lo_ms (the
  * assignment steps: centroid split, fused split GEMM + argmin kernel and the
  * refinement, which run back to back and are timed as one), t_dist_ms
- * (t_prep_ms + t_gemm_lo_ms), t_update_ms (centroid update).  Other fields
- * are 0. */
+ * (t_prep_ms + t_gemm_lo_ms), t_update_ms (centroid update).  With
+ * params.verify, every iteration's labels are checked (untimed) against the
+ * FP32 argmin over all k in the refinement's order: verify_label_diff counts
+ * the rows that differ, verify_excluded_best the same when the refinement ran
+ * (a violation of the certified bound: 0 when it holds; 0 without the
+ * refinement, which excludes nothing), verify_excess sums D(label) -
+ * D(argmin) over them, and stats_built is 1.  Other fields are 0. */
 typedef struct {
     int    iters;
     double inertia;

@@ -135,6 +135,10 @@ int launch_update_sorted(const float* P, long long n, int d, const int* labels, 
                           long long* sums, long long* counts, UpdateScratch sc, int num_sms, cudaStream_t s);
 void launch_finalize_fixed(const long long* sums, const long long* counts, int k, int d,
                            const DevParams* prm, float* C, float* moved2, cudaStream_t s);
+/* FP32 argmin over all k in the refinement's order, checked against labels
+ * (params.verify): cnt[0] += rows that differ, *excess += D(label) - D(best). */
+void launch_verify(const float* P, const float* C, const float* cn, int d, int k, const int* labels, long long n,
+                   unsigned long long* cnt, double* excess, int num_sms, cudaStream_t s);
 void launch_inertia(const float* P, const float* C, const int* labels, long long n, int d,
                     double* out, cudaStream_t s);
 void launch_count_diff(const int* a, const int* b, long long n, unsigned long long* out, cudaStream_t s);

@@ -350,6 +350,57 @@ __global__ void k_refine_wide(const float* __restrict__ P, const float* __restri
     if (blockIdx.x == 0 && threadIdx.x == 0 && nw > 0) atomicAdd(&prm->nwide_total, (unsigned long long)nw);
 }
 
+/* Verification (params.verify): one warp per row evaluates all k centroids
+ * in the refinement's FP32 order (lane-strided fmaf chains, shfl_down tree,
+ * fmaf(-2, dot, ||c||^2), smaller index on ties) and compares the argmin
+ * with the label the engine produced.  cnt[0] counts rows whose label is not
+ * that argmin, *excess adds D(label) - D(argmin).  Both stay 0 when the
+ * certified bound holds; this is a check, run only when asked for. */
+template <int NR>
+__global__ void k_verify(const float* __restrict__ P, const float* __restrict__ C, const float* __restrict__ cn,
+                         int d, int k, const int* __restrict__ labels, long long n,
+                         unsigned long long* __restrict__ cnt, double* __restrict__ excess) {
+    constexpr int R = NR > 0 ? NR : 1;
+    const int lane = threadIdx.x & 31;
+    const long long wstride = (long long)gridDim.x * (blockDim.x >> 5);
+    unsigned long long bad = 0;
+    double ex = 0.0;
+    for (long long i = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < n; i += wstride) {
+        const float* p = P + (size_t)i * d;
+        float pr[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int t = lane + 32 * r;
+            pr[r] = (NR > 0 && t < d) ? p[t] : 0.f;
+        }
+        const int lab = labels[i];
+        float bv = INFINITY, vl = INFINITY;
+        int bj = k;
+        for (int j0 = 0; j0 < k; j0 += 4) {
+            int j[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) j[q] = j0 + q < k ? j0 + q : -1;
+            /* the label's own value: a batch holding it is evaluated alone first */
+            if (lab >= j0 && lab < j0 + 4) {
+                float v1 = INFINITY;
+                int b1 = k;
+                const int jl[4] = {lab, -1, -1, -1};
+                eval4<NR>(pr, p, C, cn, d, lane, jl, v1, b1);
+                vl = v1;
+            }
+            eval4<NR>(pr, p, C, cn, d, lane, j, bv, bj);
+        }
+        if (lane == 0 && bj != lab) {
+            ++bad;
+            ex += (double)vl - (double)bv;
+        }
+    }
+    if (lane == 0 && bad) {
+        atomicAdd(cnt, bad);
+        atomicAdd(excess, ex);
+    }
+}
+
 /* C_j = (float)((S_j * 2^-frac) / count_j); an empty cluster keeps its old
  * centroid; moved2[j] = ||c_new - c_old||^2 by the reference's 256-wide tree
  * (kmeans/src/kernels.cu:705-723). */
@@ -492,6 +543,13 @@ void launch_refine(const float* P, const float* C, const float* cn, int d, int k
 void launch_finalize_fixed(const long long* sums, const long long* counts, int k, int d, const DevParams* prm,
                            float* C, float* moved2, cudaStream_t s) {
     k_finalize_fixed<<<k, 256, 0, s>>>(sums, counts, k, d, prm, C, moved2);
+}
+
+void launch_verify(const float* P, const float* C, const float* cn, int d, int k, const int* labels, long long n,
+                   unsigned long long* cnt, double* excess, int num_sms, cudaStream_t s) {
+    if (n <= 0) return;
+    if (d <= 256) k_verify<8><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, labels, n, cnt, excess);
+    else k_verify<0><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, labels, n, cnt, excess);
 }
 
 void launch_inertia(const float* P, const float* C, const int* labels, long long n, int d, double* out,

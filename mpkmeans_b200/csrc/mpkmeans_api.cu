@@ -768,11 +768,16 @@ static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k
     cudaEvent_t ev_join = nullptr;
     cudaGraphExec_t g_assign = nullptr, g_update = nullptr;
     bool try_graphs = true;
+    /* params.verify: every iteration's labels checked against the FP32 argmin over all k */
+    const bool verify = P.verify != 0;
+    unsigned long long* vbuf = nullptr;   /* [0] rows that differ, [1] excess (a double) */
     if (dev_alloc((void**)&sums, ((size_t)k * d + k) * sizeof(long long), s) != cudaSuccess ||
-        dev_alloc((void**)&moved2, (size_t)k * sizeof(float), s) != cudaSuccess) {
+        dev_alloc((void**)&moved2, (size_t)k * sizeof(float), s) != cudaSuccess ||
+        (verify && dev_alloc((void**)&vbuf, 2 * sizeof(unsigned long long), s) != cudaSuccess)) {
         st = MPK_ERR_ALLOC;
         goto done;
     }
+    if (verify) cudaMemsetAsync(vbuf, 0, 2 * sizeof(unsigned long long), s);
     for (auto& x : ev) cudaEventCreate(&x);
 
     /* The iterations run on a private stream gs, ordered after the caller's
@@ -805,6 +810,11 @@ static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k
             goto done;
         }
         cudaEventRecord(ev[4 * it + 1], gs);
+        if (verify) {                     /* untimed: between the assignment and the update */
+            launch_verify(e->P, dC, e->cn, d, k, dAssign, n, vbuf, reinterpret_cast<double*>(vbuf + 1),
+                          e->num_sms, gs);
+            cudaEventRecord(ev[4 * it + 3], gs);
+        }
         if (replay) {
             if (cudaGraphLaunch(g_update, gs) != cudaSuccess) { st = MPK_ERR_CUDA; goto done; }
         } else {
@@ -839,7 +849,7 @@ static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k
         for (int t = 0; t < it; ++t) {
             cudaEventElapsedTime(&ms, ev[4 * t + 0], ev[4 * t + 1]);
             S->t_gemm_lo_ms += ms;
-            cudaEventElapsedTime(&ms, ev[4 * t + 1], ev[4 * t + 2]);
+            cudaEventElapsedTime(&ms, ev[4 * t + (verify ? 3 : 1)], ev[4 * t + 2]);
             S->t_update_ms += ms;
         }
         S->t_prep_ms = prep_x;
@@ -850,6 +860,17 @@ static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k
         S->hp_update = cands;
         S->n_hist = it < MPK_MAX_HIST ? it : MPK_MAX_HIST;
         cudaMemcpy(S->hist_survivors, e->hist, sizeof(long long) * S->n_hist, cudaMemcpyDeviceToHost);
+        if (verify) {
+            unsigned long long hv[2] = {0, 0};
+            cudaMemcpy(hv, vbuf, sizeof(hv), cudaMemcpyDeviceToHost);
+            /* with the refinement on, a label off the FP32 argmin is a violation of the
+             * certified bound; without it (no exclusion test, as in the reference's
+             * raw scheme) nothing was excluded and the differences are near-tie misses */
+            S->verify_excluded_best = refine ? (long long)hv[0] : 0;
+            S->verify_label_diff = (long long)hv[0];
+            std::memcpy(&S->verify_excess, &hv[1], sizeof(double));
+            S->stats_built = 1;
+        }
         if (status) {
             fprintf(stderr, "mpkmeans_b200: device status 0x%x (1 timeout, 2 scale, 4 label, 8 list)\n", status);
             st = MPK_ERR_CUDA;
@@ -873,6 +894,7 @@ done:
     cudaEventDestroy(ev_x);
     dev_free(sums, s);
     dev_free(moved2, s);
+    dev_free(vbuf, s);
     engine_free(e);
     cudaStreamSynchronize(s);
     return st;

@@ -459,6 +459,30 @@ def test_engine_iterate_graphs_multi_round_wide(cuda):
     assert torch.equal(out[0][0], out[1][0]) and torch.equal(out[0][1], out[1][1])
 
 
+@pytest.mark.parametrize("kind", ["blobs", "offset"])
+def test_verify_mode_finds_no_violation(cuda, kind):
+    """params.verify: every iteration's labels checked against the FP32 argmin
+    over all k (untimed); the certified engine reports zero rows off it, also
+    under cancellation stress, and the same labels as without the check."""
+    P, C = make_problem(20000, 64, 256, seed=21) if kind == "blobs" else _offset_problem(20000, 64, 1024, seed=22)
+    k = C.shape[0]
+    lab_v = torch.empty(len(P), dtype=torch.int32, device="cuda")
+    dC_v = dev(C)
+    st = M.means_mixed(dev(P), dC_v, lab_v, M.params_init(max_iter=4, verify=1))
+    assert st.stats_built == 1
+    assert st.verify_excluded_best == 0 and st.verify_label_diff == 0 and st.verify_excess == 0.0
+    lab = torch.empty_like(lab_v)
+    dC = dev(C)
+    M.means_mixed(dev(P), dC, lab, M.params_init(max_iter=4))
+    assert torch.equal(lab, lab_v) and torch.equal(dC, dC_v)
+    # without refinement the tensor-core argmin is trusted: verify sees its near-tie misses
+    lab_r = torch.empty_like(lab_v)
+    st_r = M.means_mixed(dev(P), dev(C), lab_r, M.params_init(max_iter=1, verify=1, use_cond3=0, use_cond6=0))
+    want = O.assign_fp32(P, C)
+    assert st_r.verify_label_diff == int((lab_r.cpu().numpy() != want).sum())
+    assert st_r.verify_excluded_best == 0
+
+
 def test_lloyd_graph_replay_survivor_history(cuda):
     """mpkMeansMixed replays iterations 1.. from graphs: the survivor history,
     whose slot the refinement takes from a device counter, still holds one
