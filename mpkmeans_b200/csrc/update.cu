@@ -84,26 +84,26 @@ __global__ void k_label_scatter(const int* __restrict__ labels, long long n, int
     extern __shared__ int h[];
     const long long r0 = (long long)blockIdx.x * rows_per_block;
     const long long r1 = min(n, r0 + rows_per_block);
-    if (!SMEM) {
+    if constexpr (!SMEM) {
         for (long long i = r0 + threadIdx.x; i < r1; i += blockDim.x) {
             const int a = labels[i];
             if ((unsigned)a < (unsigned)k) perm[atomicAdd(&cursor[a], 1)] = (int)i;
         }
-        return;
-    }
-    for (int j = threadIdx.x; j < k; j += blockDim.x) h[j] = 0;
-    __syncthreads();
-    for (long long i = r0 + threadIdx.x; i < r1; i += blockDim.x) {
-        const int a = labels[i];
-        if ((unsigned)a < (unsigned)k) atomicAdd(&h[a], 1);
-    }
-    __syncthreads();
-    for (int j = threadIdx.x; j < k; j += blockDim.x)
-        if (h[j]) h[j] = atomicAdd(&cursor[j], h[j]);
-    __syncthreads();
-    for (long long i = r0 + threadIdx.x; i < r1; i += blockDim.x) {
-        const int a = labels[i];
-        if ((unsigned)a < (unsigned)k) perm[atomicAdd(&h[a], 1)] = (int)i;
+    } else {
+        for (int j = threadIdx.x; j < k; j += blockDim.x) h[j] = 0;
+        __syncthreads();
+        for (long long i = r0 + threadIdx.x; i < r1; i += blockDim.x) {
+            const int a = labels[i];
+            if ((unsigned)a < (unsigned)k) atomicAdd(&h[a], 1);
+        }
+        __syncthreads();
+        for (int j = threadIdx.x; j < k; j += blockDim.x)
+            if (h[j]) h[j] = atomicAdd(&cursor[j], h[j]);
+        __syncthreads();
+        for (long long i = r0 + threadIdx.x; i < r1; i += blockDim.x) {
+            const int a = labels[i];
+            if ((unsigned)a < (unsigned)k) perm[atomicAdd(&h[a], 1)] = (int)i;
+        }
     }
 }
 
