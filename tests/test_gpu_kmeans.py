@@ -62,7 +62,9 @@ def gpu_assign(P, C, **kw):
                                    (128, 64, 1), (5000, 96, 640),
                                    # d > 256: the point chunks stream through their own ring
                                    (1000, 300, 100), (2048, 768, 600), (700, 1000, 33), (3000, 512, 1024),
-                                   (257, 320, 257)])
+                                   (257, 320, 257),
+                                   # past the configurations: k = 32768 (wide rounds), d = 4096
+                                   (40000, 32, 32768), (1500, 4096, 70)])
 def test_assign_equals_fp32_oracle(cuda, n, d, k):
     P, C = make_problem(n, d, k, seed=n + d + k)
     lab, st = gpu_assign(P, C)
