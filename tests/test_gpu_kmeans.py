@@ -246,7 +246,8 @@ def test_assign_rejects_invalid(cuda):
 
 # ---------------------------------------------------------------- update ----
 
-@pytest.mark.parametrize("n,d,k", [(1000, 16, 10), (20000, 128, 1024), (3000, 33, 64), (777, 256, 5000)])
+@pytest.mark.parametrize("n,d,k", [(1000, 16, 10), (20000, 128, 1024), (3000, 33, 64), (777, 256, 5000),
+                                   (70000, 8, 60000)])  # k past the shared-memory histogram
 def test_update_bit_exact(cuda, n, d, k):
     P, C = make_problem(max(n, k), d, k, seed=k)
     P = P[:n] if n >= k else P
