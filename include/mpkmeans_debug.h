@@ -42,6 +42,17 @@ mpkStatus mpkDebugSetWaitLimit(mpkEngine e, unsigned long long ns);
 mpkStatus mpkDebugInjectStall(mpkEngine e, int stage);
 mpkStatus mpkDebugClearStatus(mpkEngine e);
 
+/* Failure injection on the host: the nth device allocation the library makes
+ * from now on (engine scratch, driver buffers) fails once, as if the device
+ * were out of memory; 0 disables.  Every entry point must then return
+ * MPK_ERR_ALLOC and free what it had allocated. */
+mpkStatus mpkDebugFailAlloc(int nth);
+
+/* Failure injection for mpkMeansMixedMG: its next wait on the devices, once
+ * they are idle, reports an asynchronous NCCL error, so the driver aborts its
+ * communicators and returns MPK_ERR_CUDA (no collective is in flight then). */
+mpkStatus mpkDebugMGFailNextWait(void);
+
 /* The emulated GEMM's device status word on the current device (bit 0: a
  * bounded wait inside the kernel ran out and the call's output is invalid);
  * synchronises the device; clears the word when `clear` is non-zero.

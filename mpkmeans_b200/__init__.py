@@ -120,6 +120,8 @@ SIGNATURES = {
     "mpkEngineAccumulate": (_I, [_P, _P, _P]),
     "mpkEngineFinalize": (_I, [_P, _P, _P, _P]),
     "mpkEngineIterate": (_I, [_P, _P, _P, _P, _I, _I]),
+    "mpkDebugFailAlloc": (_I, [_I]),
+    "mpkDebugMGFailNextWait": (_I, []),
     "mpkEngineInertia": (_I, [_P, _P, _P, ctypes.POINTER(_D)]),
     "mpkEngineFracBits": (_I, [_P]),
     "mpkEngineCounters": (_I, [_P, ctypes.POINTER(_LL), ctypes.POINTER(_LL), ctypes.POINTER(_LL),

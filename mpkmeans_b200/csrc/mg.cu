@@ -9,16 +9,26 @@
  * NCCL is resolved at run time (dlopen of libnccl.so.2, or the copy already
  * loaded by the host process), so the library links without it and callers
  * that never use this entry point never load it.
+ *
+ * Failure detection: the host never blocks on a device.  It polls every
+ * stream and every communicator's asynchronous error; on an error, or when a
+ * wait exceeds MPK_MG_TIMEOUT_S seconds (default 600), it aborts the
+ * communicators (ncclCommAbort) and returns MPK_ERR_CUDA.
  */
 #include "engine.cuh"
 #include "mpkmeans.h"
+#include "mpkmeans_debug.h"
 
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <atomic>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
+#include <thread>
 #include <vector>
 
 namespace {
@@ -31,6 +41,8 @@ struct Nccl {
     ncclResult_t (*groupStart)() = nullptr;
     ncclResult_t (*groupEnd)() = nullptr;
     const char* (*errStr)(ncclResult_t) = nullptr;
+    ncclResult_t (*asyncError)(ncclComm_t, ncclResult_t*) = nullptr;   /* optional */
+    ncclResult_t (*abort)(ncclComm_t) = nullptr;                        /* optional */
     bool ok = false;
 };
 
@@ -51,6 +63,8 @@ const Nccl& nccl() {
     n.groupStart = (decltype(n.groupStart))dlsym(h, "ncclGroupStart");
     n.groupEnd = (decltype(n.groupEnd))dlsym(h, "ncclGroupEnd");
     n.errStr = (decltype(n.errStr))dlsym(h, "ncclGetErrorString");
+    n.asyncError = (decltype(n.asyncError))dlsym(h, "ncclCommGetAsyncError");
+    n.abort = (decltype(n.abort))dlsym(h, "ncclCommAbort");
     n.ok = n.commInitAll && n.commDestroy && n.allReduce && n.groupStart && n.groupEnd && n.errStr;
     return n;
 }
@@ -78,7 +92,65 @@ float device_maxabs(const float* A, long long count, cudaStream_t s) {
     return h;
 }
 
+/* Test hook (mpkDebugMGFailNextWait): the next wait that finds every stream
+ * idle reports an asynchronous error anyway, so the abort path runs with no
+ * collective in flight. */
+std::atomic<bool> g_mg_fail{false};
+
+double wait_limit_s() {
+    const char* v = std::getenv("MPK_MG_TIMEOUT_S");
+    const double t = v ? std::atof(v) : 0.0;
+    return t > 0.0 ? t : 600.0;
+}
+
+/* Wait for every device's stream without blocking on any: poll the streams
+ * and the communicators' asynchronous errors.  On an error or a timeout,
+ * abort every communicator (the handles are gone afterwards) and return
+ * MPK_ERR_CUDA. */
+mpkStatus mg_wait(int ngpu, const int* devices, const std::vector<cudaStream_t>& st,
+                  std::vector<ncclComm_t>& comm, const Nccl& N) {
+    const auto t0 = std::chrono::steady_clock::now();
+    const double limit = wait_limit_s();
+    const char* why = nullptr;
+    for (;;) {
+        bool idle = true;
+        for (int g = 0; g < ngpu && !why; ++g) {
+            cudaSetDevice(devices[g]);
+            const cudaError_t q = cudaStreamQuery(st[g]);
+            if (q == cudaErrorNotReady) idle = false;
+            else if (q != cudaSuccess) why = cudaGetErrorString(q);
+            if (!why && comm[g] && N.asyncError) {
+                ncclResult_t ae = ncclSuccess;
+                if (N.asyncError(comm[g], &ae) != ncclSuccess) why = "ncclCommGetAsyncError failed";
+                else if (ae != ncclSuccess && ae != ncclInProgress) why = N.errStr(ae);
+            }
+        }
+        if (!why && idle) {
+            if (!g_mg_fail.exchange(false)) return MPK_OK;
+            why = "injected asynchronous error (test hook)";
+        }
+        if (!why && std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > limit)
+            why = "timed out waiting for the devices";
+        if (why) break;
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+    fprintf(stderr, "mpkMeansMixedMG: %s; aborting the communicators\n", why);
+    for (int g = 0; g < ngpu; ++g)
+        if (comm[g]) {
+            cudaSetDevice(devices[g]);
+            if (N.abort) N.abort(comm[g]);
+            else N.commDestroy(comm[g]);
+            comm[g] = nullptr;
+        }
+    return MPK_ERR_CUDA;
+}
+
 }  /* namespace */
+
+extern "C" mpkStatus mpkDebugMGFailNextWait(void) {
+    g_mg_fail.store(true);
+    return MPK_OK;
+}
 
 extern "C" mpkStatus mpkMeansMixedMG(int ngpu, const int* devices, const float* const* dPshard, const int* nshard,
                                      int d, int k, float* const* dC, int* const* dAssign, const mpkParams* params,
@@ -168,7 +240,7 @@ extern "C" mpkStatus mpkMeansMixedMG(int ngpu, const int* devices, const float* 
         if (P.tol > 0.f || P.verbose) {
             cudaSetDevice(devices[0]);
             cudaMemcpyAsync(h_moved.data(), moved[0], (size_t)k * sizeof(float), cudaMemcpyDeviceToHost, st[0]);
-            if (cudaStreamSynchronize(st[0]) != cudaSuccess) { rc = MPK_ERR_CUDA; goto done; }
+            if ((rc = mg_wait(ngpu, devices, st, comm, N)) != MPK_OK) goto done;
             double fro2 = 0.0;
             for (int j = 0; j < k; ++j) fro2 += (double)h_moved[j];
             if (P.verbose) fprintf(stderr, "[mg] iter %3d  ||dC||_F^2 %.6e\n", it, fro2);
@@ -178,10 +250,7 @@ extern "C" mpkStatus mpkMeansMixedMG(int ngpu, const int* devices, const float* 
     S->iters = it;
     cudaSetDevice(devices[0]);
     cudaEventRecord(e1, st[0]);
-    for (int g = 0; g < ngpu; ++g) {
-        cudaSetDevice(devices[g]);
-        if (cudaStreamSynchronize(st[g]) != cudaSuccess) { rc = MPK_ERR_CUDA; goto done; }
-    }
+    if ((rc = mg_wait(ngpu, devices, st, comm, N)) != MPK_OK) goto done;
     {
         float ms = 0.f;
         cudaSetDevice(devices[0]);

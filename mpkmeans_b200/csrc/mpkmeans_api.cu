@@ -10,6 +10,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <climits>
 #include <cmath>
 #include <cstdio>
@@ -123,7 +124,20 @@ static cudaMemPool_t engine_pool(int dev) {
     return pools[dev];
 }
 
+/* Test hook (mpkDebugFailAlloc): n > 0 makes the n-th device allocation from
+ * now fail, once. */
+static std::atomic<int> g_fail_alloc{0};
+
 cudaError_t dev_alloc(void** p, size_t bytes, cudaStream_t s) {
+    for (int f = g_fail_alloc.load(); f > 0;) {
+        if (g_fail_alloc.compare_exchange_weak(f, f - 1)) {
+            if (f == 1) {
+                *p = nullptr;
+                return cudaErrorMemoryAllocation;
+            }
+            break;
+        }
+    }
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -646,6 +660,11 @@ mpkStatus mpkDebugClearStatus(mpkEngine e) {
     if (!e) return MPK_ERR_INVALID;
     MPK_TRY(cudaMemsetAsync(&e->prm->status, 0, sizeof(int), e->s));
     MPK_TRY(cudaStreamSynchronize(e->s));
+    return MPK_OK;
+}
+
+mpkStatus mpkDebugFailAlloc(int nth) {
+    g_fail_alloc.store(nth > 0 ? nth : 0);
     return MPK_OK;
 }
 
