@@ -486,6 +486,25 @@ def test_verify_mode_finds_no_violation(cuda, kind):
     assert st_r.verify_excluded_best == 0
 
 
+def test_checkpoint_resume_is_bit_identical(cuda):
+    """C is the whole state of a fit: 10 iterations in one call equal 4, then
+    6 more started from the saved centroids (labels and centroids, bit for
+    bit), also on the cancellation-stress geometry where the operand scale of
+    the second call differs from the first's."""
+    for P, C in (make_problem(30000, 64, 200, seed=31), _offset_problem(20000, 64, 512, seed=32)):
+        dP = dev(P)
+        lab_a = torch.empty(len(P), dtype=torch.int32, device="cuda")
+        C_a = dev(C)
+        M.means_mixed(dP, C_a, lab_a, M.params_init(max_iter=10))
+        lab_b = torch.empty_like(lab_a)
+        C_b = dev(C)
+        M.means_mixed(dP, C_b, lab_b, M.params_init(max_iter=4))
+        saved = C_b.cpu().numpy().copy()             # the checkpoint
+        C_r = dev(saved)
+        M.means_mixed(dP, C_r, lab_b, M.params_init(max_iter=6))
+        assert torch.equal(C_r, C_a) and torch.equal(lab_b, lab_a)
+
+
 def test_lloyd_graph_replay_survivor_history(cuda):
     """mpkMeansMixed replays iterations 1.. from graphs: the survivor history,
     whose slot the refinement takes from a device counter, still holds one
