@@ -790,13 +790,20 @@ static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k
     /* params.verify: every iteration's labels checked against the FP32 argmin over all k */
     const bool verify = P.verify != 0;
     unsigned long long* vbuf = nullptr;   /* [0] rows that differ, [1] excess (a double) */
+    /* params.verbose: the previous labels and a changed-label counter, for the
+     * per-iteration line the reference prints (mpkmeans.cu:598-603) */
+    int* prev_lab = nullptr;
+    unsigned long long* dchanged = nullptr;
     if (dev_alloc((void**)&sums, ((size_t)k * d + k) * sizeof(long long), s) != cudaSuccess ||
         dev_alloc((void**)&moved2, (size_t)k * sizeof(float), s) != cudaSuccess ||
-        (verify && dev_alloc((void**)&vbuf, 2 * sizeof(unsigned long long), s) != cudaSuccess)) {
+        (verify && dev_alloc((void**)&vbuf, 2 * sizeof(unsigned long long), s) != cudaSuccess) ||
+        (P.verbose && (dev_alloc((void**)&prev_lab, (size_t)n * sizeof(int), s) != cudaSuccess ||
+                       dev_alloc((void**)&dchanged, sizeof(unsigned long long), s) != cudaSuccess))) {
         st = MPK_ERR_ALLOC;
         goto done;
     }
     if (verify) cudaMemsetAsync(vbuf, 0, 2 * sizeof(unsigned long long), s);
+    if (P.verbose) cudaMemsetAsync(prev_lab, 0xff, (size_t)n * sizeof(int), s);
     for (auto& x : ev) cudaEventCreate(&x);
 
     /* The iterations run on a private stream gs, ordered after the caller's
@@ -829,6 +836,11 @@ static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k
             goto done;
         }
         cudaEventRecord(ev[4 * it + 1], gs);
+        if (P.verbose) {                  /* labels that changed since the last iteration */
+            cudaMemsetAsync(dchanged, 0, sizeof(unsigned long long), gs);
+            launch_count_diff(dAssign, prev_lab, n, dchanged, gs);
+            cudaMemcpyAsync(prev_lab, dAssign, (size_t)n * sizeof(int), cudaMemcpyDeviceToDevice, gs);
+        }
         if (verify) {                     /* untimed: between the assignment and the update */
             launch_verify(e->P, dC, e->cn, d, k, dAssign, n, vbuf, reinterpret_cast<double*>(vbuf + 1),
                           e->num_sms, gs);
@@ -844,11 +856,19 @@ static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k
         S->hp_baseline += (long long)n * k;
         S->tested += (long long)n * (k - 1);
         if (P.tol > 0.f || P.verbose) {
+            unsigned long long hv[2] = {0, 0};   /* changed labels, rows refined this iteration */
             cudaMemcpyAsync(h_moved.data(), moved2, (size_t)k * sizeof(float), cudaMemcpyDeviceToHost, gs);
+            if (P.verbose) {
+                cudaMemcpyAsync(&hv[0], dchanged, sizeof(unsigned long long), cudaMemcpyDeviceToHost, gs);
+                if (refine && it < MPK_MAX_HIST)
+                    cudaMemcpyAsync(&hv[1], e->hist + it, sizeof(unsigned long long), cudaMemcpyDeviceToHost, gs);
+            }
             if (cudaStreamSynchronize(gs) != cudaSuccess) { st = MPK_ERR_CUDA; goto done; }
             double fro2 = 0.0;
             for (int j = 0; j < k; ++j) fro2 += (double)h_moved[j];
-            if (P.verbose) fprintf(stderr, "[%s] iter %3d  ||dC||_F^2 %.6e\n", tag, it, fro2);
+            if (P.verbose)
+                fprintf(stderr, "[%s] iter %3d  changed %8llu  refined %9llu / %lld  ||dC||_F^2 %.6e\n", tag, it,
+                        hv[0], hv[1], (long long)n, fro2);
             if (P.tol > 0.f && fro2 < (double)P.tol * (double)P.tol) { ++it; break; }
         }
     }
@@ -914,6 +934,8 @@ done:
     dev_free(sums, s);
     dev_free(moved2, s);
     dev_free(vbuf, s);
+    dev_free(prev_lab, s);
+    dev_free(dchanged, s);
     engine_free(e);
     cudaStreamSynchronize(s);
     return st;

@@ -505,6 +505,21 @@ def test_checkpoint_resume_is_bit_identical(cuda):
         assert torch.equal(C_r, C_a) and torch.equal(lab_b, lab_a)
 
 
+def test_verbose_lines(cuda, capfd):
+    """params.verbose: one stderr line per iteration with the changed-label
+    count (every row at the first iteration), the rows refined and the
+    centroid movement, as the reference's driver logs (mpkmeans.cu:598-603)."""
+    P, C = make_problem(20000, 32, 100, seed=41)
+    lab = torch.empty(len(P), dtype=torch.int32, device="cuda")
+    st = M.means_mixed(dev(P), dev(C), lab, M.params_init(max_iter=3, verbose=1))
+    lines = [ln for ln in capfd.readouterr().err.splitlines() if ln.startswith("[mixed] iter")]
+    assert len(lines) == 3, lines
+    changed = [int(ln.split("changed")[1].split()[0]) for ln in lines]
+    refined = [int(ln.split("refined")[1].split()[0]) for ln in lines]
+    assert changed[0] == 20000 and changed[2] <= changed[1] <= 20000
+    assert refined == [st.hist_survivors[i] for i in range(3)]
+
+
 def test_lloyd_graph_replay_survivor_history(cuda):
     """mpkMeansMixed replays iterations 1.. from graphs: the survivor history,
     whose slot the refinement takes from a device counter, still holds one
