@@ -276,3 +276,41 @@ def test_kmeanspp_int_definition():
     hits = sum(int(O.kmeanspp_int(Q, 2, s)[1][1] == 2000) for s in range(20))
     first_far = sum(int(O.kmeanspp_int(Q, 1, s)[1][0] == 2000) for s in range(20))
     assert hits >= 19 - first_far
+
+
+# ------------------------------------------------- update invariants -----
+
+def test_fixed_point_update_is_order_and_shard_independent():
+    """The properties the GPU update and the multi-GPU sum rely on, stated on
+    the oracle: integer sums do not depend on the order of the rows, and the
+    sums of two row shards add up to the sums of the whole, bit for bit."""
+    rng = np.random.default_rng(12)
+    n, d, k = 5000, 24, 37
+    P = (rng.standard_normal((n, d)) * rng.uniform(0.1, 50.0, d)).astype(np.float32)
+    C = P[:k].copy()
+    lab = rng.integers(0, k, n).astype(np.int32)
+    lab[lab == 5] = 6                                       # an empty cluster
+    frac = O.fixed_frac(float(np.abs(P).max()), n)
+    Cw, m2w, cw, sw = O.update_fixed(P, lab, C, frac)
+    perm = rng.permutation(n)
+    Cp, m2p, cp, sp = O.update_fixed(P[perm], lab[perm], C, frac)
+    assert np.array_equal(sw, sp) and np.array_equal(cw, cp)
+    assert np.array_equal(Cw.view(np.uint32), Cp.view(np.uint32))
+    assert np.array_equal(m2w.view(np.uint32), m2p.view(np.uint32))
+    _, _, c1, s1 = O.update_fixed(P[:1234], lab[:1234], C, frac)
+    _, _, c2, s2 = O.update_fixed(P[1234:], lab[1234:], C, frac)
+    assert np.array_equal(s1 + s2, sw) and np.array_equal(c1 + c2, cw)
+    assert np.array_equal(Cw[5], C[5])                      # the empty cluster keeps its centroid
+
+
+def test_fp32_assignment_ties_go_to_the_smaller_index():
+    """kernels.cu:19-23: on equal FP32 distances the smaller centroid index
+    wins, however the duplicates are placed."""
+    rng = np.random.default_rng(13)
+    P = rng.standard_normal((400, 16)).astype(np.float32)
+    base = rng.standard_normal((10, 16)).astype(np.float32)
+    C = np.concatenate([base, base[::-1], base])           # every centroid three times
+    lab = O.assign_fp32(P, C)
+    first = {tuple(r): i for i, r in reversed(list(enumerate(map(tuple, C))))}
+    assert all(lab[i] == first[tuple(C[lab[i]])] for i in range(len(P)))
+    assert lab.max() < 10
