@@ -33,6 +33,8 @@ struct DevParams {
     unsigned int hist_next;          /* next survivor-history slot the refinement writes */
     unsigned long long nwide_total;  /* wide rows over the run */
     unsigned long long wait_ns;      /* limit of one wait in the assignment kernel (0: 4 s) */
+    unsigned int nscan;              /* wide rows queued for the tiled full FP32 scan */
+    unsigned int pad1;
 };
 
 /* A row to re-decide in FP32.  The assignment epilogue tracks, per column
@@ -66,10 +68,14 @@ struct WideScratch {
     int* went;           /* n: refinement-entry index of each queued row */
     int* cand;           /* cap x kWideCand candidate columns */
     int* ccount;         /* cap x 2: columns found by each tile half */
+    int* scan;           /* n: rows whose lists overflowed, for the tiled full scan (d <= kScanMaxDim) */
     long long cap;       /* rows Xw holds (its plane stride); 0: no wide path (small k) */
     long long per_round; /* rows per round, <= cap */
     int rounds;          /* rounds per assignment; queued rows past them rescan their classes */
 };
+
+/* Widest row the tiled full scan (k_full_scan) stages in shared memory. */
+constexpr int kScanMaxDim = 1024;
 
 /* Error-bound constants of the assignment filter (host computed). */
 struct BoundConsts {
@@ -139,6 +145,10 @@ void launch_finalize_fixed(const long long* sums, const long long* counts, int k
  * (params.verify): cnt[0] += rows that differ, *excess += D(label) - D(best). */
 void launch_verify(const float* P, const float* C, const float* cn, int d, int k, const int* labels, long long n,
                    unsigned long long* cnt, double* excess, int num_sms, cudaStream_t s);
+/* The tiled full FP32 scan of the rows k_refine_wide queued in `rows` (count
+ * prm->nscan), d <= kScanMaxDim; labels bit-exact with the per-row scan. */
+void launch_full_scan(const float* P, const float* C, const float* cn, int d, int k, const int* rows,
+                      const DevParams* prm, int* labels, int num_sms, cudaStream_t s);
 void launch_inertia(const float* P, const float* C, const int* labels, long long n, int d,
                     double* out, cudaStream_t s);
 void launch_count_diff(const int* a, const int* b, long long n, unsigned long long* out, cudaStream_t s);

@@ -108,6 +108,7 @@ __global__ void k_prep_c(const float* __restrict__ C, int k, int d, int dp, DevP
     if (j == 0 && t == 0) {              /* the assignment that follows counts from zero */
         prm->nflag = 0;
         prm->nwide = 0;
+        prm->nscan = 0;
     }
     const float* c = C + (size_t)j * d;
     const float s = prm->scale;
@@ -329,9 +330,13 @@ __global__ void k_refine_wide(const float* __restrict__ P, const float* __restri
         constexpr int H = kWideCand / 2;
         if (c0 > H || c1 > H) {
             ++nfull;
+            ncand += (unsigned long long)k;
+            if (w.scan) {                 /* all k: queued for the tiled scan (k_full_scan) */
+                if (lane == 0) w.scan[atomicAdd(&prm->nscan, 1u)] = row;
+                continue;
+            }
 #pragma unroll 1
             for (int j = 0; j < k; ++j) push(j);
-            ncand += (unsigned long long)k;
         } else {
             const int* cl = w.cand + (size_t)s * kWideCand;
 #pragma unroll 1
@@ -348,6 +353,239 @@ __global__ void k_refine_wide(const float* __restrict__ P, const float* __restri
         if (nfull) atomicAdd(&prm->novf_total, nfull);
     }
     if (blockIdx.x == 0 && threadIdx.x == 0 && nw > 0) atomicAdd(&prm->nwide_total, (unsigned long long)nw);
+}
+
+/* The full FP32 scan of the wide rows whose candidate lists overflowed: every
+ * centroid, in exactly eval4's arithmetic, but tiled.  A block stages
+ * 32 * NC centroids at a time in shared memory for 16 rows (two per warp), so
+ * a centroid is read from L2 once per 16 rows instead of once per row, and
+ * the scan is arithmetic rather than a chain of dependent loads.
+ *
+ * Lane j owns NC of the tile's centroids.  For each (centroid, row) it forms
+ * the dot eval4 spreads over a warp -- chain u sums fmaf(p[t], c[t], .) over
+ * t = u, u+32, ... < d in increasing t; the 32 chains are added by eval4's
+ * shfl_down tree (offsets 16, 8, 4, 2, 1) -- inside one thread: the chains
+ * are computed one at a time in 5-bit bit-reversed order of u (0, 16, 8, 24,
+ * 4, ...), in which that tree is the left-to-right binary tree over the
+ * leaves, so a stack of five partial sums reproduces its additions in order.
+ * Then fmaf(-2, dot, ||c||^2): the value eval4 leaves in lane 0, bit for bit.
+ * Per-lane bests merge by value, then smaller index.  Rows come from w.scan;
+ * d <= kScanMaxDim. */
+constexpr int kScanRows = 2;           /* rows per warp */
+constexpr int kScanWarps = 8;
+
+__host__ __device__ constexpr int bitrev5(int k) {
+    return ((k & 1) << 4) | ((k & 2) << 2) | (k & 4) | ((k & 8) >> 2) | ((k & 16) >> 4);
+}
+
+template <int NC>
+__global__ void __launch_bounds__(32 * kScanWarps)
+k_full_scan(const float* __restrict__ P, const float* __restrict__ C, const float* __restrict__ cn, int d, int dpad,
+            int k, const int* __restrict__ rows, const DevParams* __restrict__ prm, int* __restrict__ labels) {
+    constexpr int TILE = 32 * NC;                      /* centroids per shared-memory tile */
+    extern __shared__ float sm[];
+    float* tile = sm;                                  /* TILE x dpad */
+    float* prow = sm + (size_t)TILE * dpad;            /* kScanWarps x kScanRows x dpad */
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long cnt = (long long)*reinterpret_cast<const volatile unsigned int*>(&prm->nscan);
+    constexpr long long per_block = (long long)kScanWarps * kScanRows;
+    const int nch = (d + 31) / 32;                     /* products in the longest chain */
+    for (long long g0 = (long long)blockIdx.x * per_block; g0 < cnt; g0 += (long long)gridDim.x * per_block) {
+        int myrow[kScanRows];
+        const float* pr[kScanRows];
+#pragma unroll
+        for (int r = 0; r < kScanRows; ++r) {
+            const long long idx = g0 + warp * kScanRows + r;
+            myrow[r] = idx < cnt ? rows[idx] : -1;
+            float* dst = prow + (size_t)(warp * kScanRows + r) * dpad;
+            for (int t = lane; t < d; t += 32) dst[t] = myrow[r] >= 0 ? P[(size_t)myrow[r] * d + t] : 0.f;
+            pr[r] = dst;
+        }
+        float bv[kScanRows];
+        int bj[kScanRows];
+#pragma unroll
+        for (int r = 0; r < kScanRows; ++r) { bv[r] = INFINITY; bj[r] = k; }
+        for (int j0 = 0; j0 < k; j0 += TILE) {
+            __syncthreads();                           /* the previous tile is consumed; rows are staged */
+            for (int jj = warp; jj < TILE; jj += kScanWarps) {
+                const int j = j0 + jj;
+                for (int t = lane; t < d; t += 32) tile[(size_t)jj * dpad + t] = j < k ? C[(size_t)j * d + t] : 0.f;
+            }
+            __syncthreads();
+            float stk[NC][kScanRows][5];               /* pending left operands, by tree level */
+#pragma unroll
+            for (int leaf = 0; leaf < 32; ++leaf) {
+                const int u = bitrev5(leaf);
+                float a[NC][kScanRows];
+#pragma unroll
+                for (int c = 0; c < NC; ++c)
+#pragma unroll
+                    for (int r = 0; r < kScanRows; ++r) a[c][r] = 0.f;
+#pragma unroll 4
+                for (int i = 0; i < nch; ++i) {             /* unrolled: the next loads overlap these FMAs */
+                    const int t = u + 32 * i;
+                    if (t < d) {
+                        float pv[kScanRows];
+#pragma unroll
+                        for (int r = 0; r < kScanRows; ++r) pv[r] = pr[r][t];
+#pragma unroll
+                        for (int c = 0; c < NC; ++c) {
+                            const float cv = tile[(size_t)(c * 32 + lane) * dpad + t];
+#pragma unroll
+                            for (int r = 0; r < kScanRows; ++r) a[c][r] = fmaf(pv[r], cv, a[c][r]);
+                        }
+                    }
+                }
+                /* binary-counter merge: a completed subtree at level l combines with the
+                 * pending left sibling stk[l] (the earlier leaves), left + right */
+#pragma unroll
+                for (int c = 0; c < NC; ++c)
+#pragma unroll
+                    for (int r = 0; r < kScanRows; ++r) {
+                        float v = a[c][r];
+#pragma unroll
+                        for (int l = 0; l < 5; ++l) {
+                            if (((leaf >> l) & 1) == 0) { stk[c][r][l] = v; break; }
+                            v = stk[c][r][l] + v;
+                            if (l == 4) stk[c][r][0] = v;   /* leaf 31: the root, kept in slot 0 */
+                        }
+                    }
+            }
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                const int j = j0 + c * 32 + lane;
+                if (j < k) {
+                    const float cj = cn[j];
+#pragma unroll
+                    for (int r = 0; r < kScanRows; ++r) {
+                        const float v = fmaf(-2.f, stk[c][r][0], cj);
+                        if (v < bv[r] || (v == bv[r] && j < bj[r])) { bv[r] = v; bj[r] = j; }
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < kScanRows; ++r) {
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+                const float ov = __shfl_xor_sync(FULL, bv[r], off);
+                const int oj = __shfl_xor_sync(FULL, bj[r], off);
+                if (ov < bv[r] || (ov == bv[r] && oj < bj[r])) { bv[r] = ov; bj[r] = oj; }
+            }
+            if (lane == 0 && myrow[r] >= 0) labels[myrow[r]] = bj[r];
+        }
+    }
+}
+
+/* The same scan for d <= 256, with the operands laid out by chain: centroid
+ * and point rows are staged in shared memory as [u][i] = x[u + 32 i] (chain u,
+ * i < 8, zero past d), so a chain's eight operands are two 16-byte loads and
+ * every address is a compile-time offset.  The zero padding only adds
+ * fmaf(0, 0, acc) = acc + 0 steps, which leave a chain's value unchanged (a
+ * -0 chain can turn +0, which no later sum or fmaf(-2, dot, ||c||^2) can
+ * tell apart), so the values are eval4's, bit for bit. */
+constexpr int kScanChain = 8;          /* d <= 32 * kScanChain */
+constexpr int kScanStride = 32 * kScanChain + 4;   /* floats per staged row: 16-byte lanes spread over banks */
+
+template <int NC, int RW>
+__global__ void __launch_bounds__(32 * kScanWarps)
+k_full_scan_c8(const float* __restrict__ P, const float* __restrict__ C, const float* __restrict__ cn, int d, int k,
+               const int* __restrict__ rows, const DevParams* __restrict__ prm, int* __restrict__ labels) {
+    constexpr int TILE = 32 * NC;
+    extern __shared__ __align__(16) float sm[];
+    float* tile = sm;                                          /* TILE x kScanStride */
+    float* prow = sm + (size_t)TILE * kScanStride;             /* kScanWarps x RW x kScanStride */
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long cnt = (long long)*reinterpret_cast<const volatile unsigned int*>(&prm->nscan);
+    constexpr long long per_block = (long long)kScanWarps * RW;
+    /* staging: element x[t] of a row goes to [u][i] with t = u + 32 i */
+    auto stage = [&](float* dst, const float* src, bool live) {
+        for (int e = lane; e < 32 * kScanChain; e += 32) {      /* e = u * 8 + i */
+            const int u = e >> 3, i = e & 7, t = u + 32 * i;
+            dst[e] = (live && t < d) ? src[t] : 0.f;
+        }
+    };
+    for (long long g0 = (long long)blockIdx.x * per_block; g0 < cnt; g0 += (long long)gridDim.x * per_block) {
+        int myrow[RW];
+        const float* pr[RW];
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            const long long idx = g0 + warp * RW + r;
+            myrow[r] = idx < cnt ? rows[idx] : -1;
+            float* dst = prow + (size_t)(warp * RW + r) * kScanStride;
+            stage(dst, P + (size_t)(myrow[r] >= 0 ? myrow[r] : 0) * d, myrow[r] >= 0);
+            pr[r] = dst;
+        }
+        float bv[RW];
+        int bj[RW];
+#pragma unroll
+        for (int r = 0; r < RW; ++r) { bv[r] = INFINITY; bj[r] = k; }
+        for (int j0 = 0; j0 < k; j0 += TILE) {
+            __syncthreads();                                   /* the previous tile is consumed; rows staged */
+            for (int jj = warp; jj < TILE; jj += kScanWarps) {
+                const int j = j0 + jj;
+                stage(tile + (size_t)jj * kScanStride, C + (size_t)(j < k ? j : 0) * d, j < k);
+            }
+            __syncthreads();
+            float stk[NC][RW][5];
+#pragma unroll
+            for (int leaf = 0; leaf < 32; ++leaf) {
+                const int u = bitrev5(leaf);
+                float4 pv[RW][2];
+#pragma unroll
+                for (int r = 0; r < RW; ++r) {
+                    pv[r][0] = *reinterpret_cast<const float4*>(pr[r] + u * kScanChain);
+                    pv[r][1] = *reinterpret_cast<const float4*>(pr[r] + u * kScanChain + 4);
+                }
+#pragma unroll
+                for (int c = 0; c < NC; ++c) {
+                    const float* cr = tile + (size_t)(c * 32 + lane) * kScanStride + u * kScanChain;
+                    const float4 c0 = *reinterpret_cast<const float4*>(cr);
+                    const float4 c1 = *reinterpret_cast<const float4*>(cr + 4);
+#pragma unroll
+                    for (int r = 0; r < RW; ++r) {
+                        float a = fmaf(pv[r][0].x, c0.x, 0.f);
+                        a = fmaf(pv[r][0].y, c0.y, a);
+                        a = fmaf(pv[r][0].z, c0.z, a);
+                        a = fmaf(pv[r][0].w, c0.w, a);
+                        a = fmaf(pv[r][1].x, c1.x, a);
+                        a = fmaf(pv[r][1].y, c1.y, a);
+                        a = fmaf(pv[r][1].z, c1.z, a);
+                        a = fmaf(pv[r][1].w, c1.w, a);
+                        float v = a;
+#pragma unroll
+                        for (int l = 0; l < 5; ++l) {
+                            if (((leaf >> l) & 1) == 0) { stk[c][r][l] = v; break; }
+                            v = stk[c][r][l] + v;
+                            if (l == 4) stk[c][r][0] = v;
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                const int j = j0 + c * 32 + lane;
+                if (j < k) {
+                    const float cj = cn[j];
+#pragma unroll
+                    for (int r = 0; r < RW; ++r) {
+                        const float v = fmaf(-2.f, stk[c][r][0], cj);
+                        if (v < bv[r] || (v == bv[r] && j < bj[r])) { bv[r] = v; bj[r] = j; }
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+                const float ov = __shfl_xor_sync(FULL, bv[r], off);
+                const int oj = __shfl_xor_sync(FULL, bj[r], off);
+                if (ov < bv[r] || (ov == bv[r] && oj < bj[r])) { bv[r] = ov; bj[r] = oj; }
+            }
+            if (lane == 0 && myrow[r] >= 0) labels[myrow[r]] = bj[r];
+        }
+    }
 }
 
 /* Verification (params.verify): one warp per row evaluates all k centroids
@@ -550,6 +788,30 @@ void launch_verify(const float* P, const float* C, const float* cn, int d, int k
     if (n <= 0) return;
     if (d <= 256) k_verify<8><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, labels, n, cnt, excess);
     else k_verify<0><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, labels, n, cnt, excess);
+}
+
+void launch_full_scan(const float* P, const float* C, const float* cn, int d, int k, const int* rows,
+                      const DevParams* prm, int* labels, int num_sms, cudaStream_t s) {
+    const int dpad = ((d + 31) / 32) * 32 + 1;        /* odd stride: lane j's row starts on bank j */
+    /* centroids per lane, as many as the 227 KB of shared memory allow */
+    const int nc = dpad <= 385 ? 4 : (dpad <= 641 ? 2 : 1);
+    const size_t smem = sizeof(float) * (size_t)dpad * (32 * nc + kScanWarps * kScanRows);
+    auto go = [&](auto kern) {
+        if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        kern<<<num_sms, 32 * kScanWarps, smem, s>>>(P, C, cn, d, dpad, k, rows, prm, labels);
+    };
+    if (d <= 32 * kScanChain) {                        /* chain-major staging, 16-byte operand loads */
+        /* two centroids a lane, four rows a warp: 100 KB of shared memory, 107 registers,
+         * two blocks an SM (measured against 1x2, 1x4, 2x2, 4x2 and 2x8) */
+        constexpr int RW = 4;
+        const size_t sm8 = sizeof(float) * (size_t)kScanStride * (32 * 2 + kScanWarps * RW);
+        cudaFuncSetAttribute(k_full_scan_c8<2, RW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm8);
+        k_full_scan_c8<2, RW><<<num_sms * 2, 32 * kScanWarps, sm8, s>>>(P, C, cn, d, k, rows, prm, labels);
+        return;
+    }
+    if (nc == 4) go(k_full_scan<4>);
+    else if (nc == 2) go(k_full_scan<2>);
+    else go(k_full_scan<1>);
 }
 
 void launch_inertia(const float* P, const float* C, const int* labels, long long n, int d, double* out,

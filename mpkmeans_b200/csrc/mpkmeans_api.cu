@@ -184,7 +184,7 @@ struct mpkEngine_s {
     unsigned long long* hist = nullptr;   /* MPK_MAX_HIST slots */
     UpdateScratch us{nullptr, nullptr, nullptr, nullptr};
     CUtensorMap tmX, tmC, tmXw;
-    WideScratch wide{nullptr, nullptr, nullptr, nullptr, 0, 0, 0};
+    WideScratch wide{nullptr, nullptr, nullptr, nullptr, nullptr, 0, 0, 0};
     BoundConsts bc;
     float4* dbg = nullptr;                /* test hook, set by mpkDebugSetAssignTrace */
     int stall = -1;                       /* test hook, set by mpkDebugInjectStall */
@@ -236,7 +236,7 @@ static void engine_free(mpkEngine e) {
     graphs_release(e);
     void* bufs[] = {e->Xs, e->xnorm, e->Cs, e->cn, e->list, e->prm, e->dInertia, e->hist,
                     e->us.perm, e->us.bin_start, e->us.cursor, e->us.hist,
-                    e->wide.Xw, e->wide.went, e->wide.cand, e->wide.ccount};
+                    e->wide.Xw, e->wide.went, e->wide.cand, e->wide.ccount, e->wide.scan};
     for (void* b : bufs) dev_free(b, e->s);
     delete e;
 }
@@ -306,6 +306,7 @@ static mpkStatus engine_create(mpkEngine* out, const float* dP, long long n, int
             ALLOC(e->wide.went, (size_t)n * sizeof(int));
             ALLOC(e->wide.cand, (size_t)cap * kWideCand * sizeof(int));
             ALLOC(e->wide.ccount, (size_t)cap * 2 * sizeof(int));
+            if (d <= kScanMaxDim) ALLOC(e->wide.scan, (size_t)n * sizeof(int));
         }
     }
 #undef ALLOC
@@ -425,6 +426,10 @@ static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int r
             launch_refine_wide(e->P, dC, e->cn, e->d, e->k, e->list, e->wide, base, e->prm, dAssign, e->num_sms,
                                e->s);
             e->launches += 2;                 /* the emit pass and the FP32 evaluation */
+        }
+        if (e->wide.scan) {                   /* rows whose lists overflowed: all k, tiled */
+            launch_full_scan(e->P, dC, e->cn, e->d, e->k, e->wide.scan, e->prm, dAssign, e->num_sms, e->s);
+            ++e->launches;
         }
     }
     return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;

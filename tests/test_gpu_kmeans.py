@@ -430,6 +430,28 @@ def test_engine_iterate_graphs_equal_steps(cuda):
     assert torch.equal(C_d, C_a) and torch.equal(lab_d, lab_a)
 
 
+def test_tiled_full_scan_bit_exact_shifted_offset(cuda):
+    """Cancellation stress with the reference driver's non-negativity shift
+    (P += max|P|) and few points per cluster: most wide rows overflow their
+    lists and take the tiled full FP32 scan (k_full_scan); labels equal the
+    oracle's FP32 argmin bit for bit: the chain-major kernel at d = 256 and 40
+    (ragged), the general one at d = 300 (four centroids a lane) and 700 (one)."""
+    for n, d, k, seed in ((12000, 256, 4096, 61), (9000, 40, 2048, 62), (6000, 300, 2048, 63), (4000, 700, 1024, 64)):
+        P, C = _offset_problem(n, d, k, seed=seed)
+        sh = np.float32(np.abs(P).max())
+        P = (P + sh).astype(np.float32)
+        C = (C + sh).astype(np.float32)
+        dP, dC = dev(P), dev(C)
+        lab = torch.empty(n, dtype=torch.int32, device="cuda")
+        with M.Engine(dP, k, C0=dC) as e:
+            e.assign(dC, lab, refine=True)
+            torch.cuda.synchronize()
+            w = e.wide_counters()
+            assert e.counters()["status"] == 0
+        assert w["full_scans"] > 100, w
+        assert np.array_equal(lab.cpu().numpy(), O.assign_fp32(P, C))
+
+
 def test_engine_iterate_graphs_multi_round_wide(cuda):
     """Graph replay with the wide refinement in several rounds (k = 4096,
     cancellation stress, rounds of 97 rows): the captured iteration (gather,
