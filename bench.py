@@ -90,6 +90,9 @@ def parse():
                     help="config4/config5: 1/8 of the configuration's rows per GPU; sgemm: only the config-2 "
                          "emulated SGEMM measurement, as its own JSON line")
     ap.add_argument("--sgemm-n", type=int, default=8192)
+    ap.add_argument("--shift-nonneg", action="store_true",
+                    help="P += max|P| before the fit, as the reference's driver does for its conditions "
+                         "(mpkShiftNonNegative); a stress variant, not a BASELINE configuration")
     return ap.parse_args()
 
 
@@ -242,6 +245,11 @@ def run_ours(args, world, rank, local):
     K, D = WORKLOADS[args.workload]["k"], WORKLOADS[args.workload]["d"]
     n_local, n_total = workload_rows(args, world, rank)
     P = gen_shard(n_local, rank, dev, args.workload)
+    if args.shift_nonneg:
+        m = P.abs().max().reshape(1)
+        if world > 1:
+            dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        P += m
     # initial centroids from rank 0's shard, broadcast: k-means++ (config 1) or k distinct rows
     if rank == 0 and args.workload == "config1":
         C0 = M.kmeanspp(P, K, SEED)
@@ -636,6 +644,8 @@ def main():
     cfg = {"workload": wl["desc"], "n": n_all, "d": D, "k": K,
            "parallelism": f"rows sharded x{world}, int64 allreduce",
            "l2": "inputs (points) larger than L2; no flush"}
+    if args.shift_nonneg:
+        cfg["preprocessing"] = "P += max|P| (the reference driver's mpkShiftNonNegative): stress variant"
     if args.workload == "sgemm" and args.impl == "reference":
         if rank == 0:
             torch.cuda.set_device(local)
