@@ -42,6 +42,12 @@ mpkStatus mpkDebugSetWaitLimit(mpkEngine e, unsigned long long ns);
 mpkStatus mpkDebugInjectStall(mpkEngine e, int stage);
 mpkStatus mpkDebugClearStatus(mpkEngine e);
 
+/* Assignment kernel choice.  The CTA-pair kernel processes row tiles in pairs
+ * on two SMs that share each tensor-core MMA; it applies when k > 128 and
+ * d <= 256.  mode 0: never; 1 (the default): where it is the faster kernel
+ * (192 < d <= 256); 2: wherever it applies.  Every mode gives the same labels. */
+mpkStatus mpkDebugAssignPair(mpkEngine e, int mode);
+
 /* Failure injection on the host: the nth device allocation the library makes
  * from now on (engine scratch, driver buffers) fails once, as if the device
  * were out of memory; 0 disables.  Every entry point must then return

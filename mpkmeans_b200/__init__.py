@@ -190,6 +190,7 @@ SIGNATURES = {
     "mpkDebugEngineLaunches": (_LL, [_P]),
     "mpkDebugSetWaitLimit": (_I, [_P, ctypes.c_ulonglong]),
     "mpkDebugInjectStall": (_I, [_P, _I]),
+    "mpkDebugAssignPair": (_I, [_P, _I]),
     "mpkDebugClearStatus": (_I, [_P]),
 }
 
@@ -358,6 +359,10 @@ class Engine:
 
     def inject_stall(self, stage: int) -> None:
         check("mpkDebugInjectStall", lib().mpkDebugInjectStall(self.h, stage))
+
+    def assign_pair(self, mode: int) -> None:
+        """CTA-pair assignment kernel: 0 never, 1 where faster (default), 2 wherever it applies."""
+        check("mpkDebugAssignPair", lib().mpkDebugAssignPair(self.h, int(mode)))
 
     def clear_status(self) -> None:
         check("mpkDebugClearStatus", lib().mpkDebugClearStatus(self.h))

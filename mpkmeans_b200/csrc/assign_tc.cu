@@ -50,13 +50,16 @@ constexpr int kMaxDim = 1 << 16;        /* TMA coordinates and the error-bound m
 /* NKC > 0: the point tile (hi, lo planes, NKC chunks of 64) stays resident
  * while every centroid tile streams past it.  NKC == 0 (d > 256): the point
  * chunks stream too, through their own ring of (hi, lo) stages, next to the
- * centroid ring. */
-template <int BN, int NKC>
+ * centroid ring.  PAIR: two CTAs on two SMs share every MMA (M = 256 rows,
+ * 128 per CTA); each CTA stages only its half (BN / 2 centroids) of every
+ * centroid tile, which halves the shared-memory and L2 traffic per MMA. */
+template <int BN, int NKC, bool PAIR = false>
 struct Cfg {
     static constexpr bool STREAM = NKC == 0;
     static constexpr int A_CHUNK = BM * ROW_BYTES;            /* one plane, one K chunk */
     static constexpr int A_TILE = STREAM ? 2 * A_CHUNK : 2 * NKC * A_CHUNK;   /* hi + lo: a tile or a stage */
-    static constexpr int B_STAGE = BN * ROW_BYTES;
+    static constexpr int B_ROWS = PAIR ? BN / 2 : BN;         /* centroid rows a stage holds here */
+    static constexpr int B_STAGE = B_ROWS * ROW_BYTES;
     static constexpr int BUDGET = kSmemMax - kMiscBytes;
     static constexpr int A_BUFS = STREAM ? 3 : ((2 * A_TILE + 3 * B_STAGE <= BUDGET) ? 2 : 1);
     static constexpr int B_RAW = (BUDGET - A_BUFS * A_TILE) / B_STAGE;
@@ -70,6 +73,7 @@ struct Cfg {
     static_assert(SMEM_BYTES <= kSmemMax, "shared memory");
     static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512, "TMEM columns");
     static_assert(HALF % 32 == 0, "epilogue half must be whole 32-column chunks");
+    static_assert(!PAIR || (BN == 256 && !STREAM), "CTA pairs: 256-wide tiles, resident point tile");
 };
 
 /* Shared-memory block after the tiles. */
@@ -123,14 +127,15 @@ __device__ __forceinline__ float thr_of(float T0, float v, float v0) {
  * tmX (copies of wide rows' planes); instead of an argmin, every column whose
  * emulated value lies within the row's bound (v0, T0 from its refinement
  * entry) is written to the row's candidate list. */
-template <int BN, int NKC, bool EMIT>
+template <int BN, int NKC, bool EMIT, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
 k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmC,
             long long n, int k, int nkc_rt, const float* __restrict__ xnorm, const float* __restrict__ cn,
             DevParams* __restrict__ prm, int* __restrict__ labels, RefineEntry* __restrict__ list,
             int refine, BoundConsts bc, float4* __restrict__ dbg, const int* __restrict__ went,
             int* __restrict__ cand, int* __restrict__ ccount, long long wbase, int stall_stage) {
-    using Cf = Cfg<BN, NKC>;
+    using Cf = Cfg<BN, NKC, PAIR>;
+    static_assert(!(EMIT && PAIR), "the wide pass runs on single CTAs");
     /* limit of one wait (a test may shorten it to make a left-out stage time out quickly) */
     const uint32_t lim = (uint32_t)((!EMIT && prm->wait_ns ? prm->wait_ns : kWaitLimitNs) / 1000);   /* microseconds */
     if (EMIT) {
@@ -147,7 +152,12 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
     volatile int* abort_flag = &ms.abort_flag;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long num_mt = (n + BM - 1) / BM;
+    /* PAIR: the unit of work is a pair of 128-row tiles, 2 mt and 2 mt + 1,
+     * the even one in the cluster's CTA 0; tiles go to clusters round robin */
+    const uint32_t rank = PAIR ? cluster_rank() : 0u;
+    const long long num_mt = PAIR ? (n + 2 * BM - 1) / (2 * BM) : (n + BM - 1) / BM;
+    const long long mt0 = PAIR ? (long long)(blockIdx.x >> 1) : (long long)blockIdx.x;
+    const long long mt_step = PAIR ? (long long)(gridDim.x >> 1) : (long long)gridDim.x;
     const int NT = (k + BN - 1) / BN;
     int* status = &prm->status;
 
@@ -159,13 +169,20 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
     if (threadIdx.x == 0) {
         for (int i = 0; i < Cf::A_BUFS; ++i) { mbar_init(&ms.a_full[i], 1); mbar_init(&ms.a_empty[i], 1); }
         for (int i = 0; i < Cf::B_STAGES; ++i) { mbar_init(&ms.b_full[i], 1); mbar_init(&ms.b_empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&ms.t_full[i], 1); mbar_init(&ms.t_empty[i], 32 * kEpiWarps); }
+        /* PAIR: CTA 0's t_empty counts one arrival per epilogue warp of both CTAs */
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&ms.t_full[i], 1);
+            mbar_init(&ms.t_empty[i], PAIR ? 2 * kEpiWarps : 32 * kEpiWarps);
+        }
         mbar_init(&ms.fin, 1);
         ms.abort_flag = 0;
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) { tma_prefetch_desc(&tmX); tma_prefetch_desc(&tmC); }
-    if (warp == 1) tmem_alloc(&ms.tmem_slot, Cf::TMEM_COLS);
+    if (warp == 1) {
+        if (PAIR) tmem_alloc_pair(&ms.tmem_slot, Cf::TMEM_COLS);
+        else tmem_alloc(&ms.tmem_slot, Cf::TMEM_COLS);
+    }
 
     /* max_j ||c_j||, for the error bound; cn holds ||c_j||^2 */
     {
@@ -175,7 +192,8 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
         if (lane == 0) ms.wmax[warp] = m;
     }
     tc_fence_before();
-    __syncthreads();
+    if (PAIR) cluster_sync();       /* the peer's barriers are initialised before any remote signal */
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = ms.tmem_slot;
 
@@ -198,13 +216,20 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                         ++bs;
                         continue;
                     }
-                    mbar_expect_tx(&ms.b_full[st], Cf::B_STAGE);
                     b_last[st] = bu;
-                    tma_load_3d(&tmC, &ms.b_full[st], smB + st * Cf::B_STAGE, kc * KC, nt * BN, p);
+                    if (PAIR) {
+                        /* this CTA's half of the tile; CTA 0's barrier counts both halves */
+                        if (rank == 0) mbar_expect_tx(&ms.b_full[st], 2 * Cf::B_STAGE);
+                        tma_load_3d_pair(&tmC, peer_addr(&ms.b_full[st], 0), smB + st * Cf::B_STAGE, kc * KC,
+                                         nt * BN + (int)rank * Cf::B_ROWS, p);
+                    } else {
+                        mbar_expect_tx(&ms.b_full[st], Cf::B_STAGE);
+                        tma_load_3d(&tmC, &ms.b_full[st], smB + st * Cf::B_STAGE, kc * KC, nt * BN, p);
+                    }
                     ++bs;
                 }
             };
-            for (long long mt = blockIdx.x; mt < num_mt && ok; mt += gridDim.x, ++lt) {
+            for (long long mt = mt0; mt < num_mt && ok; mt += mt_step, ++lt) {
                 if (Cf::STREAM) {
                     for (int nt = 0; nt < NT && ok; ++nt)
                         for (int kc = 0; kc < nkc && ok; ++kc, ++as) {
@@ -223,27 +248,59 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                 const int ab = lt % Cf::A_BUFS;
                 const uint32_t au = (uint32_t)(lt / Cf::A_BUFS);
                 if (!mbar_wait(&ms.a_empty[ab], (au & 1u) ^ 1u, abort_flag, status, lim)) { ok = false; break; }
-                mbar_expect_tx(&ms.a_full[ab], Cf::A_TILE);
                 a_last[ab] = au;
-                for (int p = 0; p < 2; ++p)
-                    for (int kc = 0; kc < nkc; ++kc)
-                        tma_load_3d(&tmX, &ms.a_full[ab], smA + ab * Cf::A_TILE + (p * nkc + kc) * Cf::A_CHUNK,
-                                    kc * KC, (int)(mt * BM), p);
+                if (PAIR) {
+                    /* CTA 1 loads its rows only when the pair's second tile holds any (its
+                     * MMA rows are then never read); CTA 0's barrier counts both tiles */
+                    const bool rows1 = (2 * mt + 1) * BM < n;
+                    if (rank == 0) mbar_expect_tx(&ms.a_full[ab], (rows1 ? 2 : 1) * Cf::A_TILE);
+                    if (rank == 0 || rows1)
+                        for (int p = 0; p < 2; ++p)
+                            for (int kc = 0; kc < nkc; ++kc)
+                                tma_load_3d_pair(&tmX, peer_addr(&ms.a_full[ab], 0),
+                                                 smA + ab * Cf::A_TILE + (p * nkc + kc) * Cf::A_CHUNK, kc * KC,
+                                                 (int)((2 * mt + rank) * BM), p);
+                } else {
+                    mbar_expect_tx(&ms.a_full[ab], Cf::A_TILE);
+                    for (int p = 0; p < 2; ++p)
+                        for (int kc = 0; kc < nkc; ++kc)
+                            tma_load_3d(&tmX, &ms.a_full[ab], smA + ab * Cf::A_TILE + (p * nkc + kc) * Cf::A_CHUNK,
+                                        kc * KC, (int)(mt * BM), p);
+                }
                 for (int nt = 0; nt < NT && ok; ++nt)
                     for (int kc = 0; kc < nkc && ok; ++kc) load_b(nt, kc);
             }
-            if (!ok) {
+            if (!ok && !PAIR) {
                 /* let every load already issued land before the CTA exits */
                 for (int i = 0; i < Cf::A_BUFS; ++i)
                     if (a_last[i] != 0xffffffffu) drain_wait(&ms.a_full[i], a_last[i] & 1u);
                 for (int i = 0; i < Cf::B_STAGES; ++i)
                     if (b_last[i] != 0xffffffffu) drain_wait(&ms.b_full[i], b_last[i] & 1u);
+            } else if (!ok) {
+                /* a pair's loads complete on CTA 0's barriers, which CTA 1 cannot
+                 * wait on, and a phase CTA 0 never armed does not complete: give
+                 * every load in flight a fixed time (each takes microseconds) */
+                const unsigned long long t_end = globaltimer() + 20000000ull;
+                while (globaltimer() < t_end) {
+                }
             }
         }
     } else if (warp == 1) {
         /* ------------------------------------------------- MMA issuer ---- */
-        if (lane == 0) {
-            constexpr uint32_t idesc = idesc_f16(BM, BN, 0, 0, 0);
+        /* PAIR: CTA 0 issues for both; its commits arrive on the barriers of both CTAs */
+        auto mma = [&](uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+            if (PAIR) umma_f16_pair(d_tmem, a, b, idesc_f16(2 * BM, BN, 0, 0, 0), accumulate);
+            else umma_f16(d_tmem, a, b, idesc_f16(BM, BN, 0, 0, 0), accumulate);
+        };
+        auto commit = [&](uint64_t* bar) {
+            if (PAIR) {
+                umma_commit_pair(peer_addr(bar, 0));
+                umma_commit_pair(peer_addr(bar, 1));
+            } else {
+                umma_commit(bar);
+            }
+        };
+        if (lane == 0 && rank == 0) {
             uint32_t bs = 0, ts = 0, as = 0;
             int lt = 0;
             bool ok = true;
@@ -257,14 +314,13 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                 const uint32_t bh = smem_u32(smB + st * Cf::B_STAGE);
 #pragma unroll
                 for (int ks = 0; ks < KC / 16; ++ks) {
-                    umma_f16(d_tmem, sw128_desc(ah + ks * 32, 16, 1024), sw128_desc(bh + ks * 32, 16, 1024), idesc,
-                             accum);
+                    mma(d_tmem, sw128_desc(ah + ks * 32, 16, 1024), sw128_desc(bh + ks * 32, 16, 1024), accum);
                     accum = 1;
                 }
 #pragma unroll
                 for (int ks = 0; ks < KC / 16; ++ks)
-                    umma_f16(d_tmem, sw128_desc(al + ks * 32, 16, 1024), sw128_desc(bh + ks * 32, 16, 1024), idesc, 1);
-                umma_commit(&ms.b_empty[st]);
+                    mma(d_tmem, sw128_desc(al + ks * 32, 16, 1024), sw128_desc(bh + ks * 32, 16, 1024), 1);
+                commit(&ms.b_empty[st]);
                 ++bs;
                 /* centroid lo plane: x_hi * c_lo */
                 st = (int)(bs % Cf::B_STAGES);
@@ -274,11 +330,11 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                 const uint32_t bl = smem_u32(smB + st * Cf::B_STAGE);
 #pragma unroll
                 for (int ks = 0; ks < KC / 16; ++ks)
-                    umma_f16(d_tmem, sw128_desc(ah + ks * 32, 16, 1024), sw128_desc(bl + ks * 32, 16, 1024), idesc, 1);
-                umma_commit(&ms.b_empty[st]);
+                    mma(d_tmem, sw128_desc(ah + ks * 32, 16, 1024), sw128_desc(bl + ks * 32, 16, 1024), 1);
+                commit(&ms.b_empty[st]);
                 ++bs;
             };
-            for (long long mt = blockIdx.x; mt < num_mt && ok; mt += gridDim.x, ++lt) {
+            for (long long mt = mt0; mt < num_mt && ok; mt += mt_step, ++lt) {
                 const int ab = lt % Cf::A_BUFS;
                 const uint32_t au = (uint32_t)(lt / Cf::A_BUFS);
                 if (!Cf::STREAM) {
@@ -300,19 +356,20 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                             tc_fence_after();
                             const uint32_t ah = smem_u32(smA + sa * Cf::A_TILE);
                             chunk(d_tmem, ah, ah + Cf::A_CHUNK, accum);
-                            if (ok) umma_commit(&ms.a_empty[sa]);
+                            if (ok) commit(&ms.a_empty[sa]);
                             ++as;
                         } else {
                             chunk(d_tmem, a_addr + (uint32_t)(kc * Cf::A_CHUNK),
                                   a_addr + (uint32_t)((nkc + kc) * Cf::A_CHUNK), accum);
                         }
                     }
-                    if (ok) umma_commit(&ms.t_full[tb]);
+                    if (ok) commit(&ms.t_full[tb]);
                 }
-                if (ok && !Cf::STREAM) umma_commit(&ms.a_empty[ab]);
+                if (ok && !Cf::STREAM) commit(&ms.a_empty[ab]);
             }
             /* every MMA issued by this thread has completed once fin flips */
-            umma_commit(&ms.fin);
+            if (PAIR) umma_commit_pair(peer_addr(&ms.fin, 0));
+            else umma_commit(&ms.fin);
             drain_wait(&ms.fin, 0);
         }
     } else {
@@ -334,7 +391,7 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
         /* The loop runs every tile even after a failed wait (ok == false, the
          * kernel is aborting): both halves must reach the same named barriers. */
         if (EMIT) {
-            for (long long mt = blockIdx.x; mt < num_mt; mt += gridDim.x) {
+            for (long long mt = mt0; mt < num_mt; mt += mt_step) {
                 const long long row = mt * BM + r_loc;
                 const bool live = row < n;
                 /* Every column the filter could admit, (D - v0) <= thr_of(T0, D, v0), has
@@ -392,7 +449,7 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                 if (ok && live) ccount[row * 2 + half] = cnt;
             }
         } else
-        for (long long mt = blockIdx.x; mt < num_mt; mt += gridDim.x) {
+        for (long long mt = mt0; mt < num_mt; mt += mt_step) {
             float a0[kClasses], a1[kClasses];
             int i0[kClasses];
 #pragma unroll
@@ -438,7 +495,13 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                     }
                 }
                 tc_fence_before();
-                mbar_arrive(&ms.t_empty[tb]);
+                if (PAIR) {
+                    /* one arrival per warp, on CTA 0's barrier */
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(peer_addr(&ms.t_empty[tb], 0));
+                } else {
+                    mbar_arrive(&ms.t_empty[tb]);
+                }
 #pragma unroll
                 for (int c = 0; c < kClasses; ++c)
                     if (pos[c] >= 0) i0[c] = nt * BN + pos[c];
@@ -461,7 +524,7 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
                 ms.xc[r_loc] = hj0;
             }
             named_bar(bar_id, 64);
-            const long long row = mt * BM + r_loc;
+            const long long row = (PAIR ? 2 * mt + rank : mt) * BM + r_loc;
             if (half == 0) {
                 const float ov0 = ms.xa[r_loc], ov1 = ms.xb[r_loc];
                 const int oj0 = ms.xc[r_loc];
@@ -526,43 +589,116 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
     }
 
     tc_fence_before();
-    __syncthreads();
+    /* PAIR: neither CTA leaves while the other may still signal its barriers or
+     * the pair's MMAs may read its shared memory */
+    if (PAIR) cluster_sync();
+    else __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, Cf::TMEM_COLS);
+        if (PAIR) tmem_dealloc_pair(tmem_base, Cf::TMEM_COLS);
+        else tmem_dealloc(tmem_base, Cf::TMEM_COLS);
     }
 }
 
-template <int BN, int NKC, bool EMIT>
+template <int BN, int NKC, bool EMIT, bool PAIR>
 cudaError_t launch_t(const AssignArgs& a, cudaStream_t s) {
-    using Cf = Cfg<BN, NKC>;
-    auto kern = k_assign_tc<BN, NKC, EMIT>;
+    using Cf = Cfg<BN, NKC, PAIR>;
+    auto kern = k_assign_tc<BN, NKC, EMIT, PAIR>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    const long long num_mt = (a.n + BM - 1) / BM;
-    const int grid = (int)(num_mt < a.num_sms ? num_mt : a.num_sms);
-    kern<<<grid, kThreads, Cf::SMEM_BYTES, s>>>(*a.tmX, *a.tmC, a.n, a.k, a.dp / KC, a.xnorm, a.cn, a.prm,
-                                                 a.labels, a.list, a.refine, a.bc, a.dbg,
-                                                 EMIT ? a.wide->went : nullptr, EMIT ? a.wide->cand : nullptr,
-                                                 EMIT ? a.wide->ccount : nullptr, EMIT ? a.wbase : 0,
-                                                 EMIT ? -1 : a.stall);
-    return cudaGetLastError();
+    const int* went = EMIT ? a.wide->went : nullptr;
+    int* cand = EMIT ? a.wide->cand : nullptr;
+    int* ccount = EMIT ? a.wide->ccount : nullptr;
+    const long long wbase = EMIT ? a.wbase : 0;
+    const int stall = EMIT ? -1 : a.stall;
+    if (!PAIR) {
+        const long long num_mt = (a.n + BM - 1) / BM;
+        const int grid = (int)(num_mt < a.num_sms ? num_mt : a.num_sms);
+        kern<<<grid, kThreads, Cf::SMEM_BYTES, s>>>(*a.tmX, *a.tmC, a.n, a.k, a.dp / KC, a.xnorm, a.cn, a.prm,
+                                                     a.labels, a.list, a.refine, a.bc, a.dbg, went, cand, ccount,
+                                                     wbase, stall);
+        return cudaGetLastError();
+    }
+    /* clusters of two CTAs, as many as can be resident at once, each running
+     * pairs of row tiles round robin */
+    const long long pairs = (a.n + 2 * BM - 1) / (2 * BM);
+    const int nclus = (int)(pairs < a.pair_clusters ? pairs : a.pair_clusters);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * nclus, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cf::SMEM_BYTES;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, *a.tmX, *a.tmCh, a.n, a.k, a.dp / KC, a.xnorm, a.cn, a.prm, a.labels,
+                           a.list, a.refine, a.bc, a.dbg, went, cand, ccount, wbase, stall);
+    return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+/* Clusters of two that can be resident at once for the pair kernel of this
+ * depth (0: it cannot run). */
+template <int NKC>
+int pair_clusters_t(int num_sms) {
+    using Cf = Cfg<256, NKC, true>;
+    auto kern = k_assign_tc<256, NKC, false, true>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM_BYTES) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cf::SMEM_BYTES;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int nc = 0;
+    if (cudaOccupancyMaxActiveClusters(&nc, kern, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return nc;
 }
 
 template <int BN, bool EMIT>
 cudaError_t launch_bn(const AssignArgs& a, cudaStream_t s) {
+    /* the pair kernel: 256-wide tiles, a resident point tile, no test hook; by default
+     * only at depth 256 (192 < d <= 256), where it measured faster (at d = 128 it
+     * was slower); a.pair == 2 takes it at every depth */
+    const bool pair = BN == 256 && !EMIT && a.pair_clusters > 0 && a.stall < 0 &&
+                      (a.pair == 2 || (a.pair == 1 && a.dp / KC == 4));
     switch (a.dp / KC) {
-        case 1: return launch_t<BN, 1, EMIT>(a, s);
-        case 2: return launch_t<BN, 2, EMIT>(a, s);
-        case 3: return launch_t<BN, 3, EMIT>(a, s);
-        case 4: return launch_t<BN, 4, EMIT>(a, s);
-        default: return launch_t<BN, 0, EMIT>(a, s);      /* d > 256: streaming point chunks */
+        case 1: return pair ? launch_t<256, 1, false, true>(a, s) : launch_t<BN, 1, EMIT, false>(a, s);
+        case 2: return pair ? launch_t<256, 2, false, true>(a, s) : launch_t<BN, 2, EMIT, false>(a, s);
+        case 3: return pair ? launch_t<256, 3, false, true>(a, s) : launch_t<BN, 3, EMIT, false>(a, s);
+        case 4: return pair ? launch_t<256, 4, false, true>(a, s) : launch_t<BN, 4, EMIT, false>(a, s);
+        default: return launch_t<BN, 0, EMIT, false>(a, s);      /* d > 256: streaming point chunks */
     }
 }
 
 }  /* namespace */
 
 int assign_bn_for(int k) { return k <= 64 ? 64 : (k <= 128 ? 128 : 256); }
+
+int assign_pair_clusters(int k, int dp, int num_sms) {
+    if (assign_bn_for(k) != 256) return 0;
+    switch (dp / KC) {
+        case 1: return pair_clusters_t<1>(num_sms);
+        case 2: return pair_clusters_t<2>(num_sms);
+        case 3: return pair_clusters_t<3>(num_sms);
+        case 4: return pair_clusters_t<4>(num_sms);
+        default: return 0;
+    }
+}
 int assign_supported(int d) { return d >= 1 && d <= kMaxDim; }
 
 cudaError_t launch_assign(const AssignArgs& a, cudaStream_t s) {

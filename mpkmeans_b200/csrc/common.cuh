@@ -230,6 +230,79 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int ab_fmt, int a
          | ((uint32_t)(M >> 4) << 24);
 }
 
+/* ------------------------------------------------------- CTA pairs ---- */
+/* A cluster of two CTAs on two SMs sharing one tcgen05.mma (cta_group::2): the
+ * even CTA issues every MMA, each CTA supplies its half of the operand tiles
+ * from its own shared memory and receives its half of the rows of D in its own
+ * TMEM.  Every tcgen05 instruction of such a kernel uses cta_group::2. */
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+/* Address, in the cluster's shared-memory window, of the variable at the
+ * same offset as `local` in the shared memory of CTA `rank`. */
+__device__ __forceinline__ uint32_t peer_addr(const void* local, uint32_t rank) {
+    uint32_t a;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(local)), "r"(rank));
+    return a;
+}
+
+/* Arrive (release at cluster scope) on an mbarrier of any CTA of the cluster. */
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" :: "r"(cluster_addr) : "memory");
+}
+
+/* Every thread of both CTAs: arrive with release, wait with acquire. */
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+/* 3D tiled load into this CTA's shared memory whose completion is counted on
+ * an mbarrier of either CTA of the pair (`bar` is a cluster address). */
+__device__ __forceinline__ void tma_load_3d_pair(const CUtensorMap* map, uint32_t bar, void* smem,
+                                                 int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];"
+        :: "r"(smem_u32(smem)), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar),
+           "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+/* Issued by one warp in each CTA of the pair, at the same shared offset. */
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :: "r"(smem_u32(slot)), "r"(ncols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" :: "r"(taddr), "r"(ncols) : "memory");
+}
+
+/* The pair's D (+)= A * B^T: M = 256 rows, 128 from each CTA's A tile, and N
+ * columns, the first N/2 from the even CTA's B tile, the rest from the odd
+ * CTA's; descriptors name the same shared offsets in both CTAs. */
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        :: "r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+/* Arrive on the mbarrier at cluster address `bar` (either CTA) once every
+ * pair MMA this thread issued so far completes. */
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :: "r"(bar) : "memory");
+}
+
 /* --------------------------------------------------------------- misc ---- */
 
 __device__ __forceinline__ float warp_max(float v) {

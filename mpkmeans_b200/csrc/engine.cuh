@@ -5,7 +5,8 @@
  *   Xs     2 x n x dp FP16: plane 0 = hi, plane 1 = lo of s*P, dp = d rounded
  *          up to 64 (zero padded); split once per fit
  *   xnorm  n FP32: ||p_i|| (only feeds the error bound)
- *   Cs     2 x k x dp FP16: hi/lo of s*C, re-split every iteration
+ *   Cs     2 x kpad x dp FP16: hi/lo of s*C, re-split every iteration; rows
+ *          past k are zero (kpad = k rounded up to 256)
  *   cn     kpad FP32: ||c_j||^2 in the reference's tree order; +inf past k
  *   list   refinement entries (row + up to 4 candidates), capacity n
  *   sums   k*d int64 fixed-point coordinate sums, then k int64 counts
@@ -95,6 +96,9 @@ void launch_prep_c(const float* C, int k, int kpad, int d, int dp, DevParams* pr
 struct AssignArgs {
     const CUtensorMap* tmX;   /* host copies, passed by value to the kernel */
     const CUtensorMap* tmC;
+    const CUtensorMap* tmCh;  /* centroid planes in 128-row boxes: the CTA-pair kernel */
+    int pair;                 /* CTA-pair kernel: 0 never, 1 where faster, 2 wherever it applies */
+    int pair_clusters;        /* resident clusters of two for it (0: not available) */
     long long n;
     int k, d, dp;
     const float* xnorm;
@@ -116,6 +120,7 @@ struct AssignArgs {
 };
 int  assign_bn_for(int k);                   /* N tile width chosen for k     */
 int  assign_supported(int d);                /* 1 when d fits the kernel      */
+int  assign_pair_clusters(int k, int dp, int num_sms);   /* 0: no CTA-pair kernel */
 cudaError_t launch_assign(const AssignArgs& a, cudaStream_t s);
 
 /* ---- refine / update (kernels.cu) ---- */

@@ -101,7 +101,11 @@ __global__ void k_prep_c(const float* __restrict__ C, int k, int d, int dp, DevP
     __shared__ float sh[256];
     const int j = blockIdx.x;
     const int t = threadIdx.x;
-    if (j >= k) {
+    if (j >= k) {                        /* padding rows: zero planes, infinite norm */
+        for (int f = t; f < dp; f += 256) {
+            planes[(size_t)j * dp + f] = __float2half_rn(0.f);
+            planes[(size_t)j * dp + plane_stride + f] = __float2half_rn(0.f);
+        }
         if (t == 0) cn[j] = INFINITY;
         return;
     }
@@ -752,7 +756,7 @@ void launch_split_rows(const float* src, long long rows, int d, int dp, const De
 
 void launch_prep_c(const float* C, int k, int kpad, int d, int dp, DevParams* prm, __half* planes, float* cn,
                    cudaStream_t s) {
-    k_prep_c<<<kpad, 256, 0, s>>>(C, k, d, dp, prm, planes, (long long)k * dp, cn);
+    k_prep_c<<<kpad, 256, 0, s>>>(C, k, d, dp, prm, planes, (long long)kpad * dp, cn);
 }
 
 void launch_wide_gather(const RefineEntry* list, const __half* Xs, long long n, int dp, const WideScratch& w,

@@ -183,11 +183,13 @@ struct mpkEngine_s {
     double* dInertia = nullptr;
     unsigned long long* hist = nullptr;   /* MPK_MAX_HIST slots */
     UpdateScratch us{nullptr, nullptr, nullptr, nullptr};
-    CUtensorMap tmX, tmC, tmXw;
+    CUtensorMap tmX, tmC, tmCh, tmXw;   /* tmCh: centroid planes in 128-row halves (CTA pairs) */
     WideScratch wide{nullptr, nullptr, nullptr, nullptr, nullptr, 0, 0, 0};
     BoundConsts bc;
     float4* dbg = nullptr;                /* test hook, set by mpkDebugSetAssignTrace */
     int stall = -1;                       /* test hook, set by mpkDebugInjectStall */
+    int pair = 1;                         /* CTA-pair assignment kernel (mpkDebugAssignPair) */
+    int pair_clusters = 0;                /* resident clusters of two for it */
     long long launches = 0;               /* kernels this engine has launched */
     bool prof = false;                    /* bench hook: events around the hot kernels */
     std::vector<cudaEvent_t> ev_assign, ev_accum;
@@ -290,7 +292,7 @@ static mpkStatus engine_create(mpkEngine* out, const float* dP, long long n, int
     if (need_assign) {
         ALLOC(e->Xs, (size_t)2 * (n > 0 ? n : 1) * e->dp * sizeof(__half));
         ALLOC(e->xnorm, (size_t)(n > 0 ? n : 1) * sizeof(float));
-        ALLOC(e->Cs, (size_t)2 * k * e->dp * sizeof(__half));
+        ALLOC(e->Cs, (size_t)2 * e->kpad * e->dp * sizeof(__half));
         ALLOC(e->cn, (size_t)e->kpad * sizeof(float));
         ALLOC(e->list, (size_t)(n > 0 ? n : 1) * sizeof(RefineEntry));
         /* the wide path: only when some row could need more than kWideRescan
@@ -332,12 +334,14 @@ static mpkStatus engine_create(mpkEngine* out, const float* dP, long long n, int
             return MPK_ERR_CUDA;
         }
         if ((n > 0 && !make_tmap_planes(&e->tmX, e->Xs, n, e->dp, 128)) ||
-            !make_tmap_planes(&e->tmC, e->Cs, k, e->dp, assign_bn_for(k)) ||
+            !make_tmap_planes(&e->tmC, e->Cs, e->kpad, e->dp, assign_bn_for(k)) ||
+            (assign_bn_for(k) == 256 && !make_tmap_planes(&e->tmCh, e->Cs, e->kpad, e->dp, 128)) ||
             (e->wide.cap > 0 && !make_tmap_planes(&e->tmXw, e->wide.Xw, e->wide.cap, e->dp, 128))) {
             fprintf(stderr, "mpkmeans_b200: tensor map encoding failed\n");
             engine_free(e);
             return MPK_ERR_CUDA;
         }
+        e->pair_clusters = assign_pair_clusters(k, e->dp, e->num_sms);
     }
     if (cudaGetLastError() != cudaSuccess) {
         engine_free(e);
@@ -371,6 +375,9 @@ static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int r
     AssignArgs a;
     a.tmX = &e->tmX;
     a.tmC = &e->tmC;
+    a.tmCh = &e->tmCh;
+    a.pair = e->pair;
+    a.pair_clusters = e->pair_clusters;
     a.n = e->n;
     a.k = e->k;
     a.d = e->d;
@@ -658,6 +665,14 @@ mpkStatus mpkDebugSetWaitLimit(mpkEngine e, unsigned long long ns) {
 mpkStatus mpkDebugInjectStall(mpkEngine e, int stage) {
     if (!e) return MPK_ERR_INVALID;
     e->stall = stage < 0 ? -1 : stage;
+    return MPK_OK;
+}
+
+mpkStatus mpkDebugAssignPair(mpkEngine e, int mode) {
+    if (!e) return MPK_ERR_INVALID;
+    if (mode < 0 || mode > 2) return MPK_ERR_INVALID;
+    e->pair = mode;
+    graphs_release(e);                    /* captured iterations name the old kernel */
     return MPK_OK;
 }
 

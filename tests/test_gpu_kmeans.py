@@ -74,6 +74,34 @@ def test_assign_equals_fp32_oracle(cuda, n, d, k):
     assert st.hp_baseline == n * k
 
 
+@pytest.mark.parametrize("n,d,k", [(1111, 64, 300), (1200, 128, 1024), (700, 256, 520), (385, 192, 257),
+                                   (4200, 128, 4096)])
+def test_assign_pair_kernel_equals_single(cuda, n, d, k):
+    """The CTA-pair assignment kernel (two SMs per MMA, 256 rows a pair) and the
+    one-CTA kernel give the oracle's labels and the same tensor-core values;
+    the shapes leave the last pair with no second tile (n = 1111, 385, 4200) or a
+    partial one, and k not a multiple of 256 (zero centroid rows past k)."""
+    P, C = make_problem(n, d, k, seed=n * 7 + k)
+    dP, dC = dev(P), dev(C)
+    labs, traces = [], []
+    for mode in (2, 0):
+        with M.Engine(dP, k, C0=dC) as e:
+            e.assign_pair(mode)
+            out4 = torch.zeros((n, 4), dtype=torch.float32, device="cuda")
+            lab = torch.full((n,), -7, dtype=torch.int32, device="cuda")
+            e.trace(out4)
+            e.assign(dC, lab, refine=True)
+            torch.cuda.synchronize()
+            e.trace(None)
+            assert e.counters()["status"] == 0
+        labs.append(lab.cpu().numpy())
+        traces.append(out4.cpu().numpy())
+    assert np.array_equal(labs[0], O.assign_fp32(P, C))
+    assert np.array_equal(labs[0], labs[1])
+    v_pair, v_one = traces[0][:, :2].astype(np.float64), traces[1][:, :2].astype(np.float64)
+    assert np.all(np.abs(v_pair - v_one) <= 1e-6 * (np.abs(v_one) + 1.0))
+
+
 def test_assign_tie_break_smaller_index(cuda):
     rng = np.random.default_rng(1)
     n, d, k = 640, 32, 48
