@@ -45,7 +45,7 @@ mpkStatus mpkDebugClearStatus(mpkEngine e);
 /* Assignment kernel choice.  The CTA-pair kernel processes row tiles in pairs
  * on two SMs that share each tensor-core MMA; it applies when k > 128 and
  * d <= 256.  mode 0: never; 1 (the default): where it is the faster kernel
- * (192 < d <= 256); 2: wherever it applies.  Every mode gives the same labels. */
+ * (128 < d <= 256); 2: wherever it applies.  Every mode gives the same labels. */
 mpkStatus mpkDebugAssignPair(mpkEngine e, int mode);
 
 /* Failure injection on the host: the nth device allocation the library makes
