@@ -21,6 +21,11 @@
  *               classes (column mod 8) the best value with its column and the
  *               runner-up value.
  *
+ * The pair variant (128 < d <= 256) runs the same roles on a cluster of two
+ * CTAs: CTA 0's MMA warp issues tcgen05.mma.cta_group::2 over 256 rows (128
+ * from each CTA's point tile) and 256 centroids (each CTA stages 128), every
+ * CTA's epilogue reads its own 128 rows of the accumulator from its own TMEM.
+ *
  * After the last centroid tile of a row tile the two halves exchange their
  * summaries through shared memory and every row writes its argmin (smaller
  * index on ties).  A row whose runner-up lies within the certified error
