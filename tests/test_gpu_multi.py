@@ -13,11 +13,12 @@ import mpkmeans_b200 as M  # noqa: E402
 pytestmark = pytest.mark.gpu
 
 
-def test_mg_two_gpus_equals_one(cuda):
+@pytest.mark.parametrize("d,k", [(64, 128), (256, 1024)])     # d = 256: the CTA-pair assignment
+def test_mg_two_gpus_equals_one(cuda, d, k):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    P = O.make_gmm(200_000, 64, 128, 9, 5.0, 0.5, 2.0, True)
-    C0 = P[np.sort(O.init_random_idx(200_000, 128, 9))].copy()
+    P = O.make_gmm(200_000, d, k, 9, 5.0, 0.5, 2.0, True)
+    C0 = P[np.sort(O.init_random_idx(200_000, k, 9))].copy()
     lab1 = torch.empty(200_000, dtype=torch.int32, device="cuda:0")
     dC1 = torch.from_numpy(C0).to("cuda:0")
     M.means_mixed(torch.from_numpy(P).to("cuda:0"), dC1, lab1, M.params_init(max_iter=6))
@@ -29,7 +30,7 @@ def test_mg_two_gpus_equals_one(cuda):
     st = M.mpkStats()
     p = M.params_init(max_iter=6)
     rc = M.lib().mpkMeansMixedMG(2, arr(ctypes.c_int, [0, 1]), arr(ctypes.c_void_p, [x.data_ptr() for x in dPs]),
-                                 arr(ctypes.c_int, [b - a for a, b in halves]), 64, 128,
+                                 arr(ctypes.c_int, [b - a for a, b in halves]), d, k,
                                  arr(ctypes.c_void_p, [x.data_ptr() for x in dCs]),
                                  arr(ctypes.c_void_p, [x.data_ptr() for x in dAs]), ctypes.byref(p), ctypes.byref(st))
     assert rc == M.MPK_OK
