@@ -44,8 +44,8 @@ mpkStatus mpkDebugClearStatus(mpkEngine e);
 
 /* Assignment kernel choice.  The CTA-pair kernel processes row tiles in pairs
  * on two SMs that share each tensor-core MMA; it applies when k > 128 and
- * d <= 256.  mode 0: never; 1 (the default): where it is the faster kernel
- * (128 < d <= 256); 2: wherever it applies.  Every mode gives the same labels. */
+ * d <= 256 and is the default there.  mode 0: one CTA per row tile instead;
+ * non-zero: the default.  Both give the same labels. */
 mpkStatus mpkDebugAssignPair(mpkEngine e, int mode);
 
 /* Failure injection on the host: the nth device allocation the library makes

@@ -361,7 +361,7 @@ class Engine:
         check("mpkDebugInjectStall", lib().mpkDebugInjectStall(self.h, stage))
 
     def assign_pair(self, mode: int) -> None:
-        """CTA-pair assignment kernel: 0 never, 1 where faster (default), 2 wherever it applies."""
+        """CTA-pair assignment kernel where it applies (the default); 0: one CTA per row tile."""
         check("mpkDebugAssignPair", lib().mpkDebugAssignPair(self.h, int(mode)))
 
     def clear_status(self) -> None:

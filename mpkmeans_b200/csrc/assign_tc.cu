@@ -21,7 +21,7 @@
  *               classes (column mod 8) the best value with its column and the
  *               runner-up value.
  *
- * The pair variant (128 < d <= 256) runs the same roles on a cluster of two
+ * The pair variant (k > 128, d <= 256) runs the same roles on a cluster of two
  * CTAs: CTA 0's MMA warp issues tcgen05.mma.cta_group::2 over 256 rows (128
  * from each CTA's point tile) and 256 centroids (each CTA stages 128), every
  * CTA's epilogue reads its own 128 rows of the accumulator from its own TMEM.
@@ -676,12 +676,8 @@ int pair_clusters_t(int num_sms) {
 
 template <int BN, bool EMIT>
 cudaError_t launch_bn(const AssignArgs& a, cudaStream_t s) {
-    /* the pair kernel: 256-wide tiles, a resident point tile, no test hook.  By default
-     * only for 128 < d <= 256, where it measured 2-5 % faster; at d = 64 and 128 it was
-     * 12 % and 3-5 % slower (the epilogue dominates there, and a pair's two SMs wait
-     * for each other's); a.pair == 2 takes it at every depth */
-    const bool pair = BN == 256 && !EMIT && a.pair_clusters > 0 && a.stall < 0 &&
-                      (a.pair == 2 || (a.pair == 1 && a.dp / KC >= 3));
+    /* the pair kernel: 256-wide tiles, a resident point tile (d <= 256), no test hook */
+    const bool pair = BN == 256 && !EMIT && a.pair != 0 && a.pair_clusters > 0 && a.stall < 0;
     switch (a.dp / KC) {
         case 1: return pair ? launch_t<256, 1, false, true>(a, s) : launch_t<BN, 1, EMIT, false>(a, s);
         case 2: return pair ? launch_t<256, 2, false, true>(a, s) : launch_t<BN, 2, EMIT, false>(a, s);

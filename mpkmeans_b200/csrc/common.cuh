@@ -250,9 +250,13 @@ __device__ __forceinline__ uint32_t peer_addr(const void* local, uint32_t rank) 
     return a;
 }
 
-/* Arrive (release at cluster scope) on an mbarrier of any CTA of the cluster. */
+/* Arrive on an mbarrier of any CTA of the cluster, with the instruction's
+ * default semantics (release at CTA scope): after tcgen05.wait::ld and
+ * tcgen05.fence::before_thread_sync this orders a warp's TMEM reads before the
+ * MMAs that the barrier's waiter issues next; a cluster-scope release would
+ * also wait for the warp's outstanding global stores. */
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" :: "r"(cluster_addr) : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" :: "r"(cluster_addr) : "memory");
 }
 
 /* Every thread of both CTAs: arrive with release, wait with acquire. */

@@ -97,7 +97,7 @@ struct AssignArgs {
     const CUtensorMap* tmX;   /* host copies, passed by value to the kernel */
     const CUtensorMap* tmC;
     const CUtensorMap* tmCh;  /* centroid planes in 128-row boxes: the CTA-pair kernel */
-    int pair;                 /* CTA-pair kernel: 0 never, 1 where faster, 2 wherever it applies */
+    int pair;                 /* CTA-pair kernel where it applies (0: one CTA per tile) */
     int pair_clusters;        /* resident clusters of two for it (0: not available) */
     long long n;
     int k, d, dp;

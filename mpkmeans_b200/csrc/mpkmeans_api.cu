@@ -670,8 +670,7 @@ mpkStatus mpkDebugInjectStall(mpkEngine e, int stage) {
 
 mpkStatus mpkDebugAssignPair(mpkEngine e, int mode) {
     if (!e) return MPK_ERR_INVALID;
-    if (mode < 0 || mode > 2) return MPK_ERR_INVALID;
-    e->pair = mode;
+    e->pair = mode != 0;
     graphs_release(e);                    /* captured iterations name the old kernel */
     return MPK_OK;
 }

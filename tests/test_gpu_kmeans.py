@@ -84,7 +84,7 @@ def test_assign_pair_kernel_equals_single(cuda, n, d, k):
     P, C = make_problem(n, d, k, seed=n * 7 + k)
     dP, dC = dev(P), dev(C)
     labs, traces = [], []
-    for mode in (2, 0):
+    for mode in (1, 0):
         with M.Engine(dP, k, C0=dC) as e:
             e.assign_pair(mode)
             out4 = torch.zeros((n, 4), dtype=torch.float32, device="cuda")
