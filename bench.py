@@ -723,7 +723,7 @@ def main():
         achieved = flops / (a_ms / 1e3) / 1e12
         # DRAM bytes of one assignment launch, from the committed ncu summary of this workload (recorded
         # for the N = 1 shard; traffic grows with the rows, so it is scaled to this rank's rows)
-        prof_ref = {"config3": ("assign_tc_config3.md", N_FULL), "config4": ("assign_tc_config4.md", 6_250_000)}
+        prof_ref = {"config3": ("assign_pair_config3.md", N_FULL), "config4": ("assign_tc_config4.md", 6_250_000)}
         traffic = None
         if args.workload in prof_ref:
             fig = profile_figure(prof_ref[args.workload][0], "dram_bytes_per_launch")
