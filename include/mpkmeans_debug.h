@@ -43,8 +43,8 @@ mpkStatus mpkDebugInjectStall(mpkEngine e, int stage);
 mpkStatus mpkDebugClearStatus(mpkEngine e);
 
 /* Assignment kernel choice.  The CTA-pair kernel processes row tiles in pairs
- * on two SMs that share each tensor-core MMA; it applies when k > 128 and
- * d <= 256 and is the default there.  mode 0: one CTA per row tile instead;
+ * on two SMs that share each tensor-core MMA; it applies when k > 128 and is
+ * the default there.  mode 0: one CTA per row tile instead;
  * non-zero: the default.  Both give the same labels. */
 mpkStatus mpkDebugAssignPair(mpkEngine e, int mode);
 

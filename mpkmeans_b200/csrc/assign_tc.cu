@@ -21,7 +21,7 @@
  *               classes (column mod 8) the best value with its column and the
  *               runner-up value.
  *
- * The pair variant (k > 128, d <= 256) runs the same roles on a cluster of two
+ * The pair variant (k > 128) runs the same roles on a cluster of two
  * CTAs: CTA 0's MMA warp issues tcgen05.mma.cta_group::2 over 256 rows (128
  * from each CTA's point tile) and 256 centroids (each CTA stages 128), every
  * CTA's epilogue reads its own 128 rows of the accumulator from its own TMEM.
@@ -78,7 +78,7 @@ struct Cfg {
     static_assert(SMEM_BYTES <= kSmemMax, "shared memory");
     static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512, "TMEM columns");
     static_assert(HALF % 32 == 0, "epilogue half must be whole 32-column chunks");
-    static_assert(!PAIR || (BN == 256 && !STREAM), "CTA pairs: 256-wide tiles, resident point tile");
+    static_assert(!PAIR || BN == 256, "CTA pairs: 256-wide tiles");
 };
 
 /* Shared-memory block after the tiles. */
@@ -236,16 +236,28 @@ k_assign_tc(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUt
             };
             for (long long mt = mt0; mt < num_mt && ok; mt += mt_step, ++lt) {
                 if (Cf::STREAM) {
+                    /* PAIR: as for the resident tile below, CTA 1 loads its chunks only when
+                     * the pair's second tile holds rows */
+                    const bool rows1 = (2 * mt + 1) * BM < n;
                     for (int nt = 0; nt < NT && ok; ++nt)
                         for (int kc = 0; kc < nkc && ok; ++kc, ++as) {
                             const int ab = (int)(as % Cf::A_BUFS);
                             const uint32_t au = as / Cf::A_BUFS;
                             if (!mbar_wait(&ms.a_empty[ab], (au & 1u) ^ 1u, abort_flag, status, lim)) { ok = false; break; }
-                            mbar_expect_tx(&ms.a_full[ab], Cf::A_TILE);
                             a_last[ab] = au;
-                            for (int p = 0; p < 2; ++p)
-                                tma_load_3d(&tmX, &ms.a_full[ab], smA + ab * Cf::A_TILE + p * Cf::A_CHUNK, kc * KC,
-                                            (int)(mt * BM), p);
+                            if (PAIR) {
+                                if (rank == 0) mbar_expect_tx(&ms.a_full[ab], (rows1 ? 2 : 1) * Cf::A_TILE);
+                                if (rank == 0 || rows1)
+                                    for (int p = 0; p < 2; ++p)
+                                        tma_load_3d_pair(&tmX, peer_addr(&ms.a_full[ab], 0),
+                                                         smA + ab * Cf::A_TILE + p * Cf::A_CHUNK, kc * KC,
+                                                         (int)((2 * mt + rank) * BM), p);
+                            } else {
+                                mbar_expect_tx(&ms.a_full[ab], Cf::A_TILE);
+                                for (int p = 0; p < 2; ++p)
+                                    tma_load_3d(&tmX, &ms.a_full[ab], smA + ab * Cf::A_TILE + p * Cf::A_CHUNK,
+                                                kc * KC, (int)(mt * BM), p);
+                            }
                             load_b(nt, kc);
                         }
                     continue;
@@ -676,14 +688,15 @@ int pair_clusters_t(int num_sms) {
 
 template <int BN, bool EMIT>
 cudaError_t launch_bn(const AssignArgs& a, cudaStream_t s) {
-    /* the pair kernel: 256-wide tiles, a resident point tile (d <= 256), no test hook */
+    /* the pair kernel: 256-wide tiles, no test hook */
     const bool pair = BN == 256 && !EMIT && a.pair != 0 && a.pair_clusters > 0 && a.stall < 0;
     switch (a.dp / KC) {
         case 1: return pair ? launch_t<256, 1, false, true>(a, s) : launch_t<BN, 1, EMIT, false>(a, s);
         case 2: return pair ? launch_t<256, 2, false, true>(a, s) : launch_t<BN, 2, EMIT, false>(a, s);
         case 3: return pair ? launch_t<256, 3, false, true>(a, s) : launch_t<BN, 3, EMIT, false>(a, s);
         case 4: return pair ? launch_t<256, 4, false, true>(a, s) : launch_t<BN, 4, EMIT, false>(a, s);
-        default: return launch_t<BN, 0, EMIT, false>(a, s);      /* d > 256: streaming point chunks */
+        default:                                                  /* d > 256: streaming point chunks */
+            return pair ? launch_t<256, 0, false, true>(a, s) : launch_t<BN, 0, EMIT, false>(a, s);
     }
 }
 
@@ -698,7 +711,7 @@ int assign_pair_clusters(int k, int dp, int num_sms) {
         case 2: return pair_clusters_t<2>(num_sms);
         case 3: return pair_clusters_t<3>(num_sms);
         case 4: return pair_clusters_t<4>(num_sms);
-        default: return 0;
+        default: return pair_clusters_t<0>(num_sms);
     }
 }
 int assign_supported(int d) { return d >= 1 && d <= kMaxDim; }

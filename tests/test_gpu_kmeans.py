@@ -75,7 +75,9 @@ def test_assign_equals_fp32_oracle(cuda, n, d, k):
 
 
 @pytest.mark.parametrize("n,d,k", [(1111, 64, 300), (1200, 128, 1024), (700, 256, 520), (385, 192, 257),
-                                   (4200, 128, 4096)])
+                                   (4200, 128, 4096),
+                                   # d > 256: point chunks stream through their own ring
+                                   (1000, 300, 300), (2100, 768, 600), (3000, 1000, 1024)])
 def test_assign_pair_kernel_equals_single(cuda, n, d, k):
     """The CTA-pair assignment kernel (two SMs per MMA, 256 rows a pair) and the
     one-CTA kernel give the oracle's labels and the same tensor-core values;
