@@ -43,6 +43,33 @@ def test_assign_wait_timeout_is_reported_and_recoverable(cuda):
     assert float(torch.ones(4, device="cuda").sum()) == 4.0     # the context is still usable
 
 
+@pytest.mark.parametrize("d", [128, 512])         # resident point tile; streaming point chunks
+def test_pair_kernel_wait_timeout_winds_down(cuda, d):
+    """The CTA-pair assignment kernel with every wait limited to 2 us: waits run
+    out in both CTAs of every pair, which then let their loads in flight land,
+    meet at the cluster barrier and return.  The timeout is reported, the
+    context stays usable, and the next assignment is exact."""
+    rng = np.random.default_rng(22)
+    n, k = 6000, 520
+    P = rng.standard_normal((n, d)).astype(np.float32)
+    C = P[rng.choice(n, size=k, replace=False)].copy()
+    dP, dC = torch.from_numpy(P).cuda(), torch.from_numpy(C).cuda()
+    lab = torch.full((n,), -1, dtype=torch.int32, device="cuda")
+    with M.Engine(dP, k, C0=dC) as e:
+        e.assign_pair(1)
+        e.set_wait_limit(2_000)
+        e.assign(dC, lab, refine=True)
+        torch.cuda.synchronize()               # the kernel returned: no hang, no fault
+        assert e.counters()["status"] & MPK_DEV_TIMEOUT
+        e.clear_status()
+        e.set_wait_limit(0)
+        e.assign(dC, lab, refine=True)
+        torch.cuda.synchronize()
+        assert e.counters()["status"] == 0
+    assert np.array_equal(lab.cpu().numpy(), O.assign_fp32(P, C))
+    assert float(torch.ones(4, device="cuda").sum()) == 4.0
+
+
 def test_allocation_failures_unwind(cuda):
     """Host-side injection: the n-th device allocation of a fit fails, for
     every n the fit makes.  Each call returns MPK_ERR_ALLOC with nothing left
