@@ -3,20 +3,31 @@
 
 Workload: n = 10,000,000 points, d = 128, k = 1024, FP32; a 1024-component
 Gaussian mixture (means U[-5,5]^d, sigma_j U[0.5,2], Dirichlet(1) weights),
-seeded synthetic data generated on the device; initial centroids are k
-distinct random points.  One step = one Lloyd iteration over all n points:
-centroid split, fused tensor-core assignment, near-tie refinement, the exact
-fixed-point update and (N > 1) one int64 NCCL allreduce of the sums.  With N
-GPUs the n rows are sharded (strong scaling: total work fixed).
+seeded synthetic data generated on the device in 2^16-row blocks, each block
+from its own counter-seeded generator, so a row's values do not depend on how
+the rows are split across GPUs; the initial centroids are k distinct rows
+chosen by a seeded draw over the global row indices.  One step = one Lloyd
+iteration over all n points: centroid split, fused tensor-core assignment,
+near-tie refinement, the exact fixed-point update and (N > 1) one int64 NCCL
+allreduce of the sums.  With N GPUs the n rows are sharded (strong scaling:
+total work fixed), and the centroids after the run are bit-identical for
+every N (integer sums); the line carries their hash.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   python bench.py --workload sgemm [--sgemm-n 8192]    # config 2 only
 
-At N = 1 the line also carries `emulated_sgemm_config2`: config 2 (C = A B,
-M = N = K = 8192, FP32 inputs U[-1,1] and u * 2^e, e in {-8..8}) through the
-mpemu C ABI -- BF16 3-word split with 3, 6 and 9 products and scaled FP16
-2-word split with 3 products -- with effective TFLOP/s and max error against
-FP64, beside native FP32 SGEMM.
+After the config-3 headline the line carries:
+  * `phases`: the timed steps split into the tensor-core assignment, the
+    refinement, the update, the allreduce and the rest (CUDA events on the
+    engine's stream inside the timed region);
+  * `label_check`: every rank's labels on a row sample of its shard against
+    the CPU oracle's FP32 argmin on the final centroids (test infrastructure
+    used as the checker, outside the timed region), and `centroid_sha`;
+  * `config5` (every N) and `config4` (N = 1 and 8): those configurations'
+    Lloyd iterations with one eighth of their rows per GPU (N = 8 is the whole
+    configuration), 10 timed iterations each, with the same checks;
+  * at N = 1, `emulated_sgemm_config2`: config 2 (C = A B, M = N = K = 8192,
+    FP32 inputs U[-1,1] and u * 2^e, e in {-8..8}) through the mpemu C ABI.
 
 `value` is device-timed (inputs resident in HBM, 5 GB of points > the 126 MB
 L2, so no flush is needed), max over ranks.  `e2e` runs the public C ABI
@@ -24,12 +35,14 @@ L2, so no flush is needed), max over ranks.  `e2e` runs the public C ABI
 `--impl reference` times the reference's own implementation of the path
 (oracle/_ref: CornellHPC/mpkmeans' mpkMeansFP32, compiled from its sources --
 the reference has no CPU k-means; its mixed driver overflows int32 indices at
-this size) on the same workload on rank 0's GPU.
+this size) on the same workload on rank 0's GPU, as whole 25-iteration fits,
+and its split-precision SGEMM (mpemu) on config 2.
 """
 from __future__ import annotations
 
 import argparse
 import ctypes
+import hashlib
 import json
 import os
 import re
@@ -93,6 +106,10 @@ def parse():
     ap.add_argument("--shift-nonneg", action="store_true",
                     help="P += max|P| before the fit, as the reference's driver does for its conditions "
                          "(mpkShiftNonNegative); a stress variant, not a BASELINE configuration")
+    ap.add_argument("--no-blocks", action="store_true",
+                    help="skip the config-4 / config-5 blocks that follow the config-3 headline")
+    ap.add_argument("--block-steps", type=int, default=10, help="timed iterations of each config-4/5 block")
+    ap.add_argument("--block-warmup", type=int, default=3)
     return ap.parse_args()
 
 
@@ -134,46 +151,69 @@ def component_params(seed, ncomp, d, box, sig_lo, sig_hi):
     return means.float(), sig.float(), cw
 
 
-def gen_shard(n_local, rank, device, wl="config3"):
-    """Seeded synthetic rows of a workload, generated on the device (rank-dependent stream)."""
+BLOCK = 1 << 16
+
+
+def _gen_block(wl, b, device, consts):
+    """Block b (rows [b * BLOCK, (b + 1) * BLOCK)) of the workload's dataset."""
     d, k = WORKLOADS[wl]["d"], WORKLOADS[wl]["k"]
-    g = torch.Generator(device=device).manual_seed(SEED * 1000003 + rank)
-    P = torch.empty((n_local, d), dtype=torch.float32, device=device)
-    chunk = 1 << 20
+    g = torch.Generator(device=device).manual_seed(SEED * 1000003 + b)
+    if wl == "config3":
+        means, sig, cw = consts
+        u = torch.rand(BLOCK, generator=g, device=device, dtype=torch.float64)
+        comp = torch.clamp(torch.searchsorted(cw, u), max=k - 1)
+        return means[comp] + sig[comp, None] * torch.randn((BLOCK, d), generator=g, device=device)
+    comp = torch.randint(0, k, (BLOCK,), generator=g, device=device)
+    x = consts[comp] + torch.randn((BLOCK, d), generator=g, device=device)
+    if wl == "config4":
+        x /= x.norm(dim=1, keepdim=True)
+    return x
+
+
+def gen_rows(wl, r0, r1, device):
+    """Rows [r0, r1) of a workload's seeded synthetic dataset, generated on the device.
+      config1: 64 components, means U[-10, 10]^d, sigma 1, equal weights (mpkMakeBlobs' distribution);
+      config3: 1024 components, means U[-5, 5]^d, sigma_j U[0.5, 2], Dirichlet(1) weights;
+      config4: N(0, I) draws around k random N(0, I) centres, each point scaled to unit norm;
+      config5: a shared offset of norm 1e3; means offset + N(0, 4I); points mean + N(0, I).
+    Every 2^16-row block has its own generator, so the rows do not depend on the split."""
+    d, k = WORKLOADS[wl]["d"], WORKLOADS[wl]["k"]
+    gc = torch.Generator().manual_seed(SEED + 17)
     if wl == "config3":
         means, sig, cw = component_params(SEED, k, d, 5.0, 0.5, 2.0)
-        means, sig, cw = means.to(device), sig.to(device), cw.to(device)
-        for r0 in range(0, n_local, chunk):
-            r1 = min(n_local, r0 + chunk)
-            u = torch.rand(r1 - r0, generator=g, device=device, dtype=torch.float64)
-            comp = torch.clamp(torch.searchsorted(cw, u), max=k - 1)
-            P[r0:r1] = means[comp] + sig[comp, None] * torch.randn((r1 - r0, d), generator=g, device=device)
-        return P
-    gc = torch.Generator().manual_seed(SEED + 17)
-    if wl == "config1":
-        # 64 components, means U[-10, 10]^d, sigma 1, equal weights (mpkMakeBlobs' distribution)
-        means = ((torch.rand((k, d), generator=gc) * 2 - 1) * 10.0).to(device)
-        comp = torch.randint(0, k, (n_local,), generator=g, device=device)
-        P.copy_(means[comp] + torch.randn((n_local, d), generator=g, device=device))
-        return P
-    if wl == "config4":
-        # N(0, I) draws around k random N(0, I) centres, each point scaled to unit norm
-        cen = torch.randn((k, d), generator=gc).to(device)
-        for r0 in range(0, n_local, chunk):
-            r1 = min(n_local, r0 + chunk)
-            comp = torch.randint(0, k, (r1 - r0,), generator=g, device=device)
-            x = cen[comp] + torch.randn((r1 - r0, d), generator=g, device=device)
-            P[r0:r1] = x / x.norm(dim=1, keepdim=True)
-        return P
-    # config5: a shared offset of norm 1e3; means offset + N(0, 4I); points mean + N(0, I)
-    o = torch.randn(d, generator=gc, dtype=torch.float64)
-    o = (o / o.norm() * 1e3).float()
-    means = (o + 2.0 * torch.randn((k, d), generator=gc)).to(device)
-    for r0 in range(0, n_local, chunk):
-        r1 = min(n_local, r0 + chunk)
-        comp = torch.randint(0, k, (r1 - r0,), generator=g, device=device)
-        P[r0:r1] = means[comp] + torch.randn((r1 - r0, d), generator=g, device=device)
+        consts = (means.to(device), sig.to(device), cw.to(device))
+    elif wl == "config1":
+        consts = ((torch.rand((k, d), generator=gc) * 2 - 1) * 10.0).to(device)
+    elif wl == "config4":
+        consts = torch.randn((k, d), generator=gc).to(device)
+    else:
+        o = torch.randn(d, generator=gc, dtype=torch.float64)
+        o = (o / o.norm() * 1e3).float()
+        consts = (o + 2.0 * torch.randn((k, d), generator=gc)).to(device)
+    P = torch.empty((max(0, r1 - r0), d), dtype=torch.float32, device=device)
+    for b in range(r0 // BLOCK, (r1 - 1) // BLOCK + 1 if r1 > r0 else r0 // BLOCK):
+        lo, hi = max(r0, b * BLOCK), min(r1, (b + 1) * BLOCK)
+        P[lo - r0:hi - r0] = _gen_block(wl, b, device, consts)[lo - b * BLOCK:hi - b * BLOCK]
     return P
+
+
+def start_rows(n_total, k, seed=SEED):
+    """k distinct global row indices, ascending: the initial centroids."""
+    return np.sort(np.random.default_rng(seed).choice(n_total, size=k, replace=False))
+
+
+def start_centroids(P, r0, n_total, k, world, device):
+    """The rows start_rows names, gathered from whichever rank holds them: each rank writes
+    its own rows and an integer all-reduce of the bit patterns assembles C0 on every rank."""
+    idx = start_rows(n_total, k)
+    C0 = torch.zeros((k, P.shape[1]), dtype=torch.float32, device=device)
+    mine = np.nonzero((idx >= r0) & (idx < r0 + P.shape[0]))[0]
+    if len(mine):
+        C0[torch.from_numpy(mine).to(device)] = P[torch.from_numpy(idx[mine] - r0).to(device)]
+    if world > 1:
+        bits = C0.view(torch.int32)
+        dist.all_reduce(bits)
+    return C0
 
 
 def shard_rows(n, world, rank):
@@ -229,44 +269,67 @@ class Clocks:
 
 # ----------------------------------------------------------- our engine -----
 
-def workload_rows(args, world, rank):
-    """(rows on this rank, rows over all ranks) for the chosen workload."""
-    w = WORKLOADS[args.workload]
-    n_conf = args.n if args.n is not None else w["n"]
+def workload_rows(wl, n_override, world, rank):
+    """(first global row, rows on this rank, rows over all ranks) of a workload.  Config 3
+    (and 1) split a fixed n over the ranks; configs 4 and 5 hold an eighth of their n per
+    GPU, so N GPUs run the first N eighths."""
+    w = WORKLOADS[wl]
+    n_conf = n_override if n_override is not None else w["n"]
     if w["shards"]:
         n_local = n_conf // w["shards"]
-        return n_local, n_local * world
-    return shard_rows(n_conf, world, rank), n_conf
+        return rank * n_local, n_local, n_local * world
+    base, rem = divmod(n_conf, world)
+    return rank * base + min(rank, rem), shard_rows(n_conf, world, rank), n_conf
 
 
-def run_ours(args, world, rank, local):
+def label_check(P, C, labels, seconds, threads):
+    """This rank's labels on a random row sample of its shard against the CPU oracle's FP32
+    argmin on the same centroids (the checker; outside every timed region).  The sample is
+    sized from a pilot for about `seconds` of oracle work on `threads` host threads."""
+    import oracle as O
+    O.lib().orc_set_threads(max(1, threads))
+    rng = np.random.default_rng(1234)
+    n = P.shape[0]
+    Cn = C.cpu().numpy()
+    pilot = np.sort(rng.choice(n, size=min(n, 256), replace=False))
+    t0 = time.perf_counter()
+    O.assign_fp32(P[torch.from_numpy(pilot).to(P.device)].cpu().numpy(), Cn)
+    per_row = (time.perf_counter() - t0) / len(pilot)
+    m = int(min(n, max(len(pilot), seconds / max(per_row, 1e-9))))
+    rows = np.sort(rng.choice(n, size=m, replace=False))
+    ridx = torch.from_numpy(rows).to(P.device)
+    want = O.assign_fp32(P[ridx].cpu().numpy(), Cn)
+    got = labels[ridx].cpu().numpy()
+    return {"rows": m, "match": int((got == want).sum())}
+
+
+def run_lloyd(wl, world, rank, local, steps, warmup, n_override=None, e2e=False, cpu=False,
+              shift_nonneg=False, check_s=3.0):
+    """One workload on this rank: generate its rows, time `steps` Lloyd iterations after
+    `warmup` untimed ones, then check and (optionally) measure e2e and the CPU baseline."""
     import mpkmeans_b200 as M
     dev = torch.device("cuda", local)
-    K, D = WORKLOADS[args.workload]["k"], WORKLOADS[args.workload]["d"]
-    n_local, n_total = workload_rows(args, world, rank)
-    P = gen_shard(n_local, rank, dev, args.workload)
-    if args.shift_nonneg:
+    K, D = WORKLOADS[wl]["k"], WORKLOADS[wl]["d"]
+    r0, n_local, n_total = workload_rows(wl, n_override, world, rank)
+    P = gen_rows(wl, r0, r0 + n_local, dev)
+    if shift_nonneg:
         m = P.abs().max().reshape(1)
         if world > 1:
             dist.all_reduce(m, op=dist.ReduceOp.MAX)
         P += m
-    # initial centroids from rank 0's shard, broadcast: k-means++ (config 1) or k distinct rows
-    if rank == 0 and args.workload == "config1":
-        C0 = M.kmeanspp(P, K, SEED)
-    elif rank == 0:
-        g = torch.Generator(device=dev).manual_seed(SEED)
-        idx = torch.sort(torch.randperm(n_local, generator=g, device=dev)[:K]).values
-        C0 = P[idx].clone()
+    # initial centroids: k-means++ (config 1, on rank 0's rows) or k distinct global rows
+    if wl == "config1":
+        C0 = M.kmeanspp(P, K, SEED) if rank == 0 else torch.empty((K, D), dtype=torch.float32, device=dev)
+        if world > 1:
+            dist.broadcast(C0, 0)
     else:
-        C0 = torch.empty((K, D), dtype=torch.float32, device=dev)
+        C0 = start_centroids(P, r0, n_total, K, world, dev)
     pmax = torch.maximum(P.abs().max(), C0.abs().max()).reshape(1)
     if world > 1:
-        dist.broadcast(C0, 0)
-        pmax = torch.maximum(P.abs().max(), C0.abs().max()).reshape(1)
         dist.all_reduce(pmax, op=dist.ReduceOp.MAX)
     torch.cuda.synchronize()
-    # one GPU: the engine runs on a side stream, where mpkEngineIterate can capture an iteration
-    # as CUDA graphs and replay it; with ranks, the allreduce sits between accumulate and finalize
+    # one GPU: the engine runs on a side stream, where mpkEngineIterate captures an iteration
+    # as CUDA graphs and replays it; with ranks, the allreduce sits between accumulate and finalize
     if world == 1:
         torch.cuda.set_stream(torch.cuda.Stream(dev))
     stream = torch.cuda.current_stream(dev).cuda_stream
@@ -275,16 +338,22 @@ def run_ours(args, world, rank, local):
     sums = torch.empty(eng.sums_length, dtype=torch.int64, device=dev)
     C = C0.clone()
 
-    def step():
+    def step(ar=None):
         if world == 1:
             eng.iterate(C, labels, sums, 1)
             return
         eng.assign(C, labels)
         eng.accumulate(labels, sums)
+        if ar is not None:
+            ar.append(torch.cuda.Event(enable_timing=True))
+            ar[-1].record()
         dist.all_reduce(sums)
+        if ar is not None:
+            ar.append(torch.cuda.Event(enable_timing=True))
+            ar[-1].record()
         eng.finalize(sums, C)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     if world > 1:
@@ -293,11 +362,12 @@ def run_ours(args, world, rank, local):
     time.sleep(0.3)
     eng.profile(True)
     launches0 = eng.launches()
+    ar = []
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     w0 = time.time()
     e0.record()
-    for _ in range(args.steps):
-        step()
+    for _ in range(steps):
+        step(ar)
     e1.record()
     launches = eng.launches() - launches0
     torch.cuda.synchronize()
@@ -306,29 +376,57 @@ def run_ours(args, world, rank, local):
         dist.barrier()
     clk = clocks.stop((w0, w1))
     prof = eng.profile_read()
-    t_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    t_local = e0.elapsed_time(e1)
+    ar_ms = sum(ar[i].elapsed_time(ar[i + 1]) for i in range(0, len(ar), 2))
+    # phases of one step on this rank, then the max over ranks of each (and of the step time)
+    ph = torch.tensor([t_local, prof["assign_ms"], prof["refine_ms"], prof["accum_ms"], ar_ms],
+                      dtype=torch.float64, device=dev) / steps
     if world > 1:
-        dist.all_reduce(t_ms, op=dist.ReduceOp.MAX)
-    t_ms = float(t_ms.item())
+        dist.all_reduce(ph, op=dist.ReduceOp.MAX)
+    ph = ph.tolist()
+    t_ms = ph[0] * steps
+    phases = {"assign_ms": ph[1], "refine_ms": ph[2], "update_ms": ph[3], "allreduce_ms": ph[4],
+              "other_ms": max(0.0, ph[0] - sum(ph[1:])),
+              "what": ("tensor-core assignment (centroid split + k_assign_tc), refinement (k_refine + wide and "
+                       "full-scan passes), update (sorted fixed-point update" +
+                       (" + finalize, one CUDA graph each" if world == 1 else "; finalize is in other_ms") +
+                       "), allreduce (int64 NCCL allreduce of the sums); max over ranks of each, per step")}
+    a_ms = prof["assign_ms"] / max(1, prof["assign_launches"])
+    u_ms = prof["accum_ms"] / max(1, prof["accum_launches"])
     cnt = eng.counters()
+    sha = hashlib.sha256(C.cpu().numpy().tobytes()).hexdigest()[:16]
 
-    # one more assignment on saved centroids, for the label check (untimed)
+    # one more assignment on the final centroids, for the label check (untimed)
     C_chk = C.clone()
     eng.assign(C_chk, labels)
     torch.cuda.synchronize()
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    chk = label_check(P, C_chk, labels, check_s, max(1, cores // world))
+    agg = torch.tensor([chk["rows"], chk["match"], chk["rows"] - chk["match"]], dtype=torch.int64, device=dev)
+    shas = [sha]
+    if world > 1:
+        dist.all_reduce(agg)
+        shas = [None] * world
+        dist.all_gather_object(shas, sha)
+    agg = agg.tolist()
 
-    res = {"t_ms": t_ms, "prof": prof, "clk": clk, "counters": cnt, "n_local": n_local, "launches": launches}
-    res["e2e"] = None if args.no_e2e else run_e2e(M, P, C0, world, rank, dev, n_total,
-                                                  iters=WORKLOADS[args.workload]["iters"])
-    res["n_total"] = n_total
-    res["cpu"] = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        res["cpu"] = cpu_baseline(P, C_chk, labels)
+    res = {"wl": wl, "t_ms": t_ms, "steps": steps, "warmup": warmup, "phases": phases, "a_ms": a_ms, "u_ms": u_ms,
+           "clk": clk, "counters": cnt, "n_local": n_local, "n_total": n_total, "launches": launches, "K": K, "D": D,
+           "label_check": {"rows": agg[0], "match_pct": 100.0 * agg[1] / max(1, agg[0]), "mismatches": agg[2],
+                           "what": "each rank's labels on a random row sample of its shard against the CPU "
+                                   "oracle's FP32 argmin on the final centroids, summed over ranks"},
+           "centroid_sha": sha, "centroid_sha_ranks_equal": len(set(shas)) == 1,
+           "iterations_before_hash": warmup + steps}
+    res["e2e"] = run_e2e(M, P, C0, world, rank, dev, n_total, iters=WORKLOADS[wl]["iters"]) if e2e else None
+    res["cpu"] = cpu_baseline(P, C_chk, labels) if (cpu and rank == 0 and world == 1) else None
     if cnt["status"] != 0:
         raise RuntimeError(f"engine device status {cnt['status']}")
     eng.close()
     torch.cuda.synchronize()
     torch.cuda.set_stream(torch.cuda.default_stream(dev))
+    del P, labels, sums, C, C0, C_chk
+    torch.cuda.empty_cache()
+    M.lib().mpkTrimMemoryPool(local)
     return res
 
 
@@ -397,6 +495,8 @@ def cpu_baseline(P, C_chk, labels):
     sample of the same workload, extrapolated to n.  Its labels on the sample
     also score the GPU labels against the same centroids (label match %)."""
     import oracle as O
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    O.lib().orc_set_threads(cores)
     threads = O.lib().orc_num_threads()
     rng = np.random.default_rng(0)
     n = P.shape[0]
@@ -421,6 +521,36 @@ def cpu_baseline(P, C_chk, labels):
             "label_match_pct": match, "label_match_rows": m}
 
 
+def lloyd_summary(r, hbm, bf16):
+    """The numbers of one run_lloyd result (rank 0), for the JSON line."""
+    K, D, n_local = r["K"], r["D"], r["n_local"]
+    value = r["steps"] / (r["t_ms"] / 1e3)
+    flops = 2.0 * n_local * K * D * 3
+    achieved = flops / (r["a_ms"] / 1e3) / 1e12
+    # the burst figure: cuBLAS bf16 timed alone at full clock.  (Scaling it by the sampled SM
+    # clock does not work: at config 5's 1.5-1.6 GHz under the power cap this kernel runs at
+    # 0.98 of the burst figure itself, so the cuBLAS number is not the tensor pipe's limit.)
+    peak = bf16
+    ubytes = n_local * D * 4 + n_local * 4
+    u_gbs = ubytes / (r["u_ms"] / 1e3) / 1e9
+    nit = max(1, r["warmup"] + r["steps"] + 1)
+    return value, {
+        "value": value, "unit": UNIT, "ms_per_step": r["t_ms"] / r["steps"], "steps": r["steps"], "warmup": r["warmup"],
+        "n": r["n_total"], "n_per_gpu": n_local, "d": D, "k": K,
+        "effective_tflops": 2.0 * r["n_total"] * K * D * value / 1e12,
+        "assign": {"achieved_tflops": achieved, "peak_tflops": peak, "frac": achieved / peak,
+                   "peak_source": "measured burst bf16 (MEASURED_PEAKS.json bf16_tflops)",
+                   "sm_mhz_median": r["clk"].get("sm_mhz"), "avg_launch_ms": r["a_ms"]},
+        "update": {"achieved_gbs": u_gbs, "peak_gbs": hbm, "frac": u_gbs / hbm, "avg_launch_ms": r["u_ms"]},
+        "phases": r["phases"], "label_check": r["label_check"], "centroid_sha": r["centroid_sha"],
+        "centroid_sha_ranks_equal": r["centroid_sha_ranks_equal"],
+        "iterations_before_hash": r["iterations_before_hash"],
+        "refined_rows_per_iter": r["counters"]["rows_refined"] / nit,
+        "refined_candidates_per_iter": r["counters"]["cand_refined"] / nit,
+        "class_rescan_rows_per_iter": r["counters"]["rows_full_scan"] / nit,
+        "gpu_launches": r["launches"], "clocks": r["clk"]}
+
+
 # ----------------------------------------------------------- reference ------
 
 def run_reference(args, world, rank, local):
@@ -437,21 +567,22 @@ def run_reference(args, world, rank, local):
     ref.mpkParamsInit.argtypes = [ctypes.POINTER(M.mpkParams)]
     dev = torch.device("cuda", local)
     K, D = WORKLOADS[args.workload]["k"], WORKLOADS[args.workload]["d"]
-    n, _ = workload_rows(args, 1, 0)
+    _, n, _ = workload_rows(args.workload, args.n, 1, 0)
     need = n * K * 4 + 2 * n * D * 4
     if need > 0.85 * torch.cuda.get_device_properties(dev).total_memory:
         return {"unavailable": f"the reference's mpkMeansFP32 materialises the n x k distance matrix "
                                f"({n * K * 4 / 1e9:.0f} GB at n={n}, k={K}): it does not fit one GPU"}
-    P = gen_shard(n, 0, dev, args.workload)
-    g = torch.Generator(device=dev).manual_seed(SEED)
+    P = gen_rows(args.workload, 0, n, dev)
     if args.workload == "config1":
         import mpkmeans_b200 as MB
         C0 = MB.kmeanspp(P, K, SEED)      # the same start as our arm (the reference has no k-means++)
     else:
-        C0 = P[torch.sort(torch.randperm(n, generator=g, device=dev)[:K]).values].clone()
+        C0 = start_centroids(P, 0, n, K, 1, dev)
     lab = torch.empty(n, dtype=torch.int32, device=dev)
     blas = torch.cuda.current_blas_handle()
-    iters = 2
+    # whole fits of the configuration's length, as the other arm's e2e fit: the reference
+    # allocates and frees its n x k matrix and other scratch once per call
+    iters = WORKLOADS[args.workload]["iters"]
     prm = M.mpkParams()
     ref.mpkParamsInit(ctypes.byref(prm))
     prm.max_iter = iters
@@ -463,6 +594,7 @@ def run_reference(args, world, rank, local):
                               ctypes.byref(st))
         if rc != 0:
             raise RuntimeError(f"reference mpkMeansFP32 returned {rc}")
+        return st
 
     for _ in range(max(1, args.warmup)):
         one()
@@ -470,12 +602,15 @@ def run_reference(args, world, rank, local):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        one()
+        st = one()
     e1.record()
     torch.cuda.synchronize()
     t = e0.elapsed_time(e1)
     value = iters * args.steps / (t / 1e3)
-    return {"value": value, "t_ms": t, "iters_per_step": iters}
+    out = {"value": value, "t_ms": t, "iters_per_step": iters, "ms_per_fit_own_timer": st.t_total_ms}
+    del P, lab, C0
+    torch.cuda.empty_cache()
+    return out
 
 
 # ------------------------------------------------- config 2: emulated SGEMM --
@@ -581,53 +716,96 @@ def run_sgemm(n=8192, reps=5):
 
 def run_sgemm_reference(n=8192, reps=5):
     """Config 2 through the reference's own mpemu (oracle/_ref: gemm-emulation compiled from its
-    sources; one cuBLAS BF16 GEMM per cross product accumulating through C), on the same
-    device-generated inputs as run_sgemm's case (a)."""
+    sources; one cuBLAS GEMM per cross product, accumulating through C), on the same
+    device-generated inputs as run_sgemm: BF16 3-word split with 3 and 6 products, scaled FP16
+    2-word split with 3 products; max error against FP64."""
     ref_path = ROOT / "oracle" / "_ref" / "libmpkref.so"
     if not ref_path.exists():
         return {"unavailable": "oracle/_ref/libmpkref.so was not built (needs the reference sources at build time)"}
     ref = ctypes.CDLL(str(ref_path))
-    VP, I64 = ctypes.c_void_p, ctypes.c_int64
+    VP, I64, F = ctypes.c_void_p, ctypes.c_int64, ctypes.c_float
     ref.mpemuSplitBF16.argtypes = [VP, I64, I64, I64, ctypes.c_int, VP, I64, I64, VP]
-    ref.mpemuGemmEmulated.argtypes = [VP, ctypes.c_int, ctypes.c_int, I64, I64, I64, ctypes.c_float, VP, I64, I64,
-                                      VP, I64, I64, ctypes.c_int, ctypes.c_int, ctypes.c_float, VP, I64]
+    ref.mpemuSplitFP16.argtypes = [VP, I64, I64, I64, ctypes.c_int, F, VP, I64, I64, VP]
+    ref.mpemuAutoScaleFP16.argtypes = [VP, I64, I64, I64, ctypes.POINTER(F), VP]
+    ref.mpemuGemmEmulated.argtypes = [VP, ctypes.c_int, ctypes.c_int, I64, I64, I64, F, VP, I64, I64,
+                                      VP, I64, I64, ctypes.c_int, ctypes.c_int, F, VP, I64]
+    ref.mpemuGemmMultiword.argtypes = [VP, ctypes.c_int, ctypes.c_int, I64, I64, I64, F, VP, I64, I64, F,
+                                       VP, I64, I64, F, ctypes.c_int, ctypes.c_int, F, VP, I64]
     dev = "cuda"
     h = torch.cuda.current_blas_handle()
-    g = torch.Generator(device=dev)
-    g.manual_seed(20)
-    A = torch.rand(n * n, device=dev, generator=g) * 2 - 1
-    B = torch.rand(n * n, device=dev, generator=g) * 2 - 1
     lds = (n + 7) // 8 * 8
     st = lds * n
-    SA = torch.empty(st * 3, dtype=torch.int16, device=dev)
-    SB = torch.empty_like(SA)
-    if (ref.mpemuSplitBF16(A.data_ptr(), n, n, n, 3, SA.data_ptr(), lds, st, None) != 0 or
-            ref.mpemuSplitBF16(B.data_ptr(), n, n, n, 3, SB.data_ptr(), lds, st, None) != 0):
-        return {"unavailable": "the reference's mpemuSplitBF16 failed"}
-    C64 = B.view(n, n).double() @ A.view(n, n).double()
-    C = torch.empty(n * n, device=dev)
-    out = {}
-    for name, macs in (("bf16x3", 3), ("bf16x6", 6)):
-        def f(macs=macs):
-            if ref.mpemuGemmEmulated(h, 0, 0, n, n, n, 1.0, SA.data_ptr(), lds, st, SB.data_ptr(), lds, st, 3, macs,
-                                     0.0, C.data_ptr(), n) != 0:
-                raise RuntimeError("reference mpemuGemmEmulated failed")
+    out = {"shape": [n, n, n], "unit": "TFLOP/s (effective FP32: 2*M*N*K / time)",
+           "what": "the reference's mpemuGemmEmulated / mpemuGemmMultiword (cuBLAS per cross product)"}
+
+    def timeit(fn):
         for _ in range(2):
-            f()
+            fn()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(reps):
-            f()
+            fn()
         e1.record()
         torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / reps
-        out[name] = {"ms": ms, "tflops": 2.0 * n ** 3 / ms / 1e9,
-                     "max_err": float((C.view(n, n).double() - C64).abs().max())}
+        return e0.elapsed_time(e1) / reps
+
+    for case, emax in (("a_uniform", 0), ("b_wide_exponent", 8)):
+        g = torch.Generator(device=dev)
+        g.manual_seed(20 + emax)
+        A = torch.rand(n * n, device=dev, generator=g) * 2 - 1
+        B = torch.rand(n * n, device=dev, generator=g) * 2 - 1
+        if emax:
+            A *= torch.exp2(torch.randint(-emax, emax + 1, (n * n,), device=dev, generator=g).float())
+            B *= torch.exp2(torch.randint(-emax, emax + 1, (n * n,), device=dev, generator=g).float())
+        SA = torch.empty(st * 3, dtype=torch.int16, device=dev)
+        SB = torch.empty_like(SA)
+        HA = torch.empty(st * 2, dtype=torch.int16, device=dev)
+        HB = torch.empty_like(HA)
+        sa, sb = F(), F()
+        if (ref.mpemuSplitBF16(A.data_ptr(), n, n, n, 3, SA.data_ptr(), lds, st, None) != 0 or
+                ref.mpemuSplitBF16(B.data_ptr(), n, n, n, 3, SB.data_ptr(), lds, st, None) != 0 or
+                ref.mpemuAutoScaleFP16(A.data_ptr(), n, n, n, ctypes.byref(sa), None) != 0 or
+                ref.mpemuAutoScaleFP16(B.data_ptr(), n, n, n, ctypes.byref(sb), None) != 0 or
+                ref.mpemuSplitFP16(A.data_ptr(), n, n, n, 2, sa, HA.data_ptr(), lds, st, None) != 0 or
+                ref.mpemuSplitFP16(B.data_ptr(), n, n, n, 2, sb, HB.data_ptr(), lds, st, None) != 0):
+            return {"unavailable": "the reference's mpemu splits failed"}
+        C64 = B.view(n, n).double() @ A.view(n, n).double()
+        C = torch.empty(n * n, device=dev)
+        res = {}
+        for name, macs in (("bf16x3", 3), ("bf16x6", 6)):
+            def f(macs=macs):
+                if ref.mpemuGemmEmulated(h, 0, 0, n, n, n, 1.0, SA.data_ptr(), lds, st, SB.data_ptr(), lds, st, 3,
+                                         macs, 0.0, C.data_ptr(), n) != 0:
+                    raise RuntimeError("reference mpemuGemmEmulated failed")
+            ms = timeit(f)
+            res[name] = {"ms": ms, "tflops": 2.0 * n ** 3 / ms / 1e9,
+                         "max_err": float((C.view(n, n).double() - C64).abs().max())}
+
+        def f16():
+            if ref.mpemuGemmMultiword(h, 0, 0, n, n, n, 1.0, HA.data_ptr(), lds, st, sa, HB.data_ptr(), lds, st, sb,
+                                      2, 3, 0.0, C.data_ptr(), n) != 0:
+                raise RuntimeError("reference mpemuGemmMultiword failed")
+        ms = timeit(f16)
+        res["fp16x3"] = {"ms": ms, "tflops": 2.0 * n ** 3 / ms / 1e9,
+                         "max_err": float((C.view(n, n).double() - C64).abs().max())}
+        out[case] = res
+        del A, B, SA, SB, HA, HB, C64, C
+        torch.cuda.empty_cache()
     return out
 
 
 # ------------------------------------------------------------------ main ----
+
+def traffic_per_launch(wl, n_local):
+    """DRAM bytes of one assignment launch, from the committed ncu summary of the workload
+    (recorded for one GPU's rows; traffic grows with the rows, so it is scaled to this rank's)."""
+    prof_ref = {"config3": ("assign_pair_config3.md", N_FULL), "config4": ("assign_tc_config4.md", 6_250_000)}
+    if wl not in prof_ref:
+        return None
+    fig = profile_figure(prof_ref[wl][0], "dram_bytes_per_launch")
+    return fig * n_local / prof_ref[wl][1] if fig else None
+
 
 def main():
     args = parse()
@@ -640,12 +818,14 @@ def main():
     if args.workload in ("config4", "config5"):
         args.no_e2e = args.no_e2e or world > 1
         args.no_sgemm = True
-    n_local0, n_all = workload_rows(args, world, 0) if args.workload != "sgemm" else (0, 0)
+    n_all = workload_rows(args.workload, args.n, world, 0)[2] if args.workload != "sgemm" else 0
     cfg = {"workload": wl["desc"], "n": n_all, "d": D, "k": K,
            "parallelism": f"rows sharded x{world}, int64 allreduce",
            "l2": "inputs (points) larger than L2; no flush"}
     if args.shift_nonneg:
         cfg["preprocessing"] = "P += max|P| (the reference driver's mpkShiftNonNegative): stress variant"
+    sgemm_metric = "effective emulated-FP32 TFLOP/s, config 2 (BF16x3, uniform case)"
+    sgemm_cfg = {"workload": f"config 2: C = A B, M = N = K = {args.sgemm_n}, FP32 inputs"}
     if args.workload == "sgemm" and args.impl == "reference":
         if rank == 0:
             torch.cuda.set_device(local)
@@ -653,13 +833,12 @@ def main():
             if "unavailable" in r:
                 print(json.dumps({"impl": "reference", "unavailable": r["unavailable"]}))
             else:
-                best = r["bf16x3"]
+                best = r["a_uniform"]["bf16x3"]
                 print(json.dumps({
-                    "impl": "reference", "metric": "effective emulated-FP32 TFLOP/s, config 2 (BF16x3, uniform case)",
+                    "impl": "reference", "metric": sgemm_metric,
                     "value": best["tflops"], "unit": "TFLOP/s", "n_gpus": 1, "steps": 5, "warmup": 2,
                     "ms_per_step": best["ms"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                    "dtype": "bf16x3->f32", "data": "synthetic (device-generated, seeded)",
-                    "config": {"workload": f"config 2: C = A B, M = N = K = {args.sgemm_n}, FP32 inputs"},
+                    "dtype": "bf16x3->f32", "data": "synthetic (device-generated, seeded)", "config": sgemm_cfg,
                     "cpu_baseline": {"kind": "reference", "cores": 1, "value": best["tflops"], "unit": "TFLOP/s",
                                      "sample": "the reference's mpemuGemmEmulated (one cuBLAS BF16 GEMM per cross "
                                                "product) on one B200; the reference has no CPU path"},
@@ -676,11 +855,10 @@ def main():
             r = run_sgemm(args.sgemm_n)
             best = r["a_uniform"]["bf16x3"]
             print(json.dumps({
-                "metric": "effective emulated-FP32 TFLOP/s, config 2 (BF16x3, uniform case)", "value": best["tflops"],
+                "metric": sgemm_metric, "value": best["tflops"],
                 "unit": "TFLOP/s", "n_gpus": 1, "steps": 5, "warmup": 2, "ms_per_step": best["ms"],
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16x3->f32",
-                "data": "synthetic (device-generated, seeded)",
-                "config": {"workload": f"config 2: C = A B, M = N = K = {args.sgemm_n}, FP32 inputs"},
+                "data": "synthetic (device-generated, seeded)", "config": sgemm_cfg,
                 "roofline": {"bound": "tensor", "achieved": best["tensor_tflops"], "peak": bf16, "unit": "TFLOP/s",
                              "frac": best["tensor_tflops"] / bf16, "traffic": None,
                              "kernel": "k_gemm_tc (3 BF16 products per call)", "peak_source": f"{peak_src} burst bf16"},
@@ -695,67 +873,83 @@ def main():
             if r is None or "unavailable" in r:
                 print(json.dumps({"impl": "reference", "unavailable": (r or {}).get("unavailable", "rank 0 only")}))
             else:
+                n_ref = workload_rows(args.workload, args.n, 1, 0)[1]
                 line = {"impl": "reference", "metric": wl["metric"], "value": r["value"], "unit": UNIT, "n_gpus": 1,
                         "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["t_ms"] / args.steps,
-                        "higher_is_better": True, "scaling": "weak" if wl["shards"] else "strong", "vs_baseline": None, "dtype": "f32",
+                        "higher_is_better": True, "scaling": "weak" if wl["shards"] else "strong",
+                        "vs_baseline": None, "dtype": "f32",
                         "data": "synthetic (device-generated, seeded)", "config": cfg,
                         "cpu_baseline": {"kind": "reference", "cores": 1, "value": r["value"], "unit": UNIT,
-                                         "sample": f"the full {args.workload} workload on one GPU "
-                                                   f"({workload_rows(args, 1, 0)[0]} rows), {r['iters_per_step']} "
-                                                   "iterations per step, through the reference's mpkMeansFP32 "
-                                                   "(cuBLAS SGEMM + its kernels) on one B200; the reference has no "
-                                                   "CPU k-means"},
-                        "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+                                         "sample": f"the full {args.workload} workload on one GPU ({n_ref} rows), "
+                                                   f"whole {r['iters_per_step']}-iteration fits per step, through "
+                                                   "the reference's mpkMeansFP32 (cuBLAS SGEMM + its kernels) on one "
+                                                   "B200; the reference has no CPU k-means"},
+                        "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                        "iters_per_step": r["iters_per_step"], "ms_per_fit_own_timer": r["ms_per_fit_own_timer"]}
+                if args.workload == "config3" and not args.no_sgemm:
+                    try:
+                        line["emulated_sgemm_config2"] = run_sgemm_reference(args.sgemm_n)
+                    except (RuntimeError, torch.cuda.OutOfMemoryError) as exc:
+                        line["emulated_sgemm_config2"] = {"error": str(exc)[:300]}
                 print(json.dumps(line))
         if world > 1:
             dist.destroy_process_group()
         return
 
-    r = run_ours(args, world, rank, local)
+    r = run_lloyd(args.workload, world, rank, local, args.steps, args.warmup, n_override=args.n,
+                  e2e=not args.no_e2e, cpu=not args.no_cpu, shift_nonneg=args.shift_nonneg)
+    # configs 5 (every N) and 4 (N = 1 and 8) after the config-3 headline, an eighth of their
+    # rows per GPU: at N = 8 each is the whole configuration
+    blocks = {}
+    if args.workload == "config3" and args.n is None and not args.no_blocks and not args.shift_nonneg:
+        for bw in ("config5", "config4"):
+            if bw == "config4" and world not in (1, 8):
+                continue
+            blocks[bw] = run_lloyd(bw, world, rank, local, args.block_steps, args.block_warmup)
     if rank == 0:
-        t_ms = r["t_ms"]
-        value = args.steps / (t_ms / 1e3)
-        prof = r["prof"]
-        n_local = r["n_local"]
-        a_ms = prof["assign_ms"] / max(1, prof["assign_launches"])
-        u_ms = prof["accum_ms"] / max(1, prof["accum_launches"])
-        flops = 2.0 * n_local * K * D * 3
-        achieved = flops / (a_ms / 1e3) / 1e12
-        # DRAM bytes of one assignment launch, from the committed ncu summary of this workload (recorded
-        # for the N = 1 shard; traffic grows with the rows, so it is scaled to this rank's rows)
-        prof_ref = {"config3": ("assign_pair_config3.md", N_FULL), "config4": ("assign_tc_config4.md", 6_250_000)}
-        traffic = None
-        if args.workload in prof_ref:
-            fig = profile_figure(prof_ref[args.workload][0], "dram_bytes_per_launch")
-            traffic = fig * n_local / prof_ref[args.workload][1] if fig else None
-        ubytes = n_local * D * 4 + n_local * 4
-        u_gbs = ubytes / (u_ms / 1e3) / 1e9
+        value, summ = lloyd_summary(r, hbm, bf16)
+        a, u = summ["assign"], summ["update"]
         line = {
             "metric": wl["metric"], "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": t_ms / args.steps, "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": summ["ms_per_step"], "higher_is_better": True,
             "scaling": "weak" if wl["shards"] else "strong",
             "vs_baseline": None, "dtype": "f16x3->f32", "data": "synthetic (device-generated, seeded)", "config": cfg,
-            "effective_tflops": 2.0 * r["n_total"] * K * D * value / 1e12,
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": bf16_sus, "unit": "TFLOP/s",
-                         "frac": achieved / bf16_sus, "traffic": traffic,
+            "effective_tflops": summ["effective_tflops"],
+            "roofline": {"bound": "tensor", "achieved": a["achieved_tflops"], "peak": a["peak_tflops"],
+                         "unit": "TFLOP/s", "frac": a["frac"], "traffic": traffic_per_launch(args.workload, r["n_local"]),
                          "kernel": "k_assign_tc (fused FP16x3 split GEMM + argmin)",
-                         "work": "2*n*k*d*3 tensor FLOP per launch", "peak_source": f"{peak_src} sustained bf16",
-                         "frac_of_burst": achieved / bf16, "avg_launch_ms": a_ms},
-            "roofline_update": {"bound": "hbm", "achieved": u_gbs, "peak": hbm, "unit": "GB/s", "frac": u_gbs / hbm,
-                                "kernel": "update: k_label_hist + k_bin_scan + k_label_scatter + k_segsum", "work": "n*d*4 + n*4 bytes per update",
-                                "avg_launch_ms": u_ms},
+                         "work": "2*n*k*d*3 tensor FLOP per launch", "peak_source": f"{peak_src} " + a["peak_source"],
+                         "sm_mhz_median": a["sm_mhz_median"], "avg_launch_ms": a["avg_launch_ms"],
+                         "timing": "CUDA events on the engine's stream around every tensor-core assignment in the "
+                                   "timed steps (with one GPU, the replayed graph of the centroid split and the kernel)"},
+            "roofline_update": {"bound": "hbm", "achieved": u["achieved_gbs"], "peak": hbm, "unit": "GB/s",
+                                "frac": u["frac"], "peak_source": f"{peak_src} copy bandwidth",
+                                "kernel": "update: k_label_hist + k_bin_scan + k_label_scatter + k_segsum" +
+                                          (" (+ memset and k_finalize_fixed: one graph)" if world == 1 else ""),
+                                "work": "n*d*4 + n*4 bytes per update", "avg_launch_ms": u["avg_launch_ms"]},
+            "phases": summ["phases"],
             "gpu_launches": r["launches"],
-            "refined_rows_per_iter": r["counters"]["rows_refined"] / max(1, args.warmup + args.steps + 1),
-            "refined_candidates_per_iter": r["counters"]["cand_refined"] / max(1, args.warmup + args.steps + 1),
-            "class_rescan_rows_per_iter": r["counters"]["rows_full_scan"] / max(1, args.warmup + args.steps + 1),
+            "label_check": summ["label_check"], "label_match_pct": summ["label_check"]["match_pct"],
+            "centroid_sha": summ["centroid_sha"], "centroid_sha_ranks_equal": summ["centroid_sha_ranks_equal"],
+            "iterations_before_hash": summ["iterations_before_hash"],
+            "refined_rows_per_iter": summ["refined_rows_per_iter"],
+            "refined_candidates_per_iter": summ["refined_candidates_per_iter"],
+            "class_rescan_rows_per_iter": summ["class_rescan_rows_per_iter"],
             "clocks": r["clk"],
         }
         if r["cpu"] is not None:
             line["cpu_baseline"] = {k_: r["cpu"][k_] for k_ in ("value", "unit", "cores", "kind", "sample")}
-            line["label_match_pct"] = r["cpu"]["label_match_pct"]
-            line["label_match_rows"] = r["cpu"]["label_match_rows"]
+            line["cpu_baseline_label_match_pct"] = r["cpu"]["label_match_pct"]
+            line["cpu_baseline_label_match_rows"] = r["cpu"]["label_match_rows"]
         if r["e2e"] is not None:
             line["e2e"] = r["e2e"]
+        for bw, br in blocks.items():
+            _, bs = lloyd_summary(br, hbm, bf16)
+            bs["metric"] = WORKLOADS[bw]["metric"]
+            bs["workload"] = WORKLOADS[bw]["desc"] + f"; the first {world} eighth(s) of the rows"
+            bs["scaling"] = "weak"
+            bs["assign"]["traffic"] = traffic_per_launch(bw, br["n_local"])
+            line[bw] = bs
         if world == 1 and not args.no_sgemm:
             try:
                 line["emulated_sgemm_config2"] = run_sgemm(args.sgemm_n)

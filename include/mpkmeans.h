@@ -238,7 +238,9 @@ mpkStatus mpkMeansMixedMG(int ngpu, const int* devices, const float* const* dPsh
  *   256) must not exceed 32 MiB -- e.g. n up to about 8.1 million rows at
  *   d = 128, k = 1024; larger sizes return MPK_ERR_INVALID (use mpkUpdate).
  * The first call on each device looks up the array's device address (make it
- * before any stream capture).  The array is shared by every call and keeps
+ * before any stream capture); with CUDA's lazy module loading it is also the
+ * call that places the 32 MiB on that device, so a caller whose footprint must
+ * stay fixed makes one call at start-up.  The array is shared by every call and keeps
  * the last call's contents (cleared where needed at each call): calls that
  * overlap on the GPU race.  Synchronises `stream` to report invalid labels.
  * Same result as mpkUpdate, bit for bit.  No counterpart in the reference. */

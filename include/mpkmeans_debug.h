@@ -72,13 +72,17 @@ int mpkDebugGemmStatus(int clear);
 mpkStatus mpkDebugWideRoundRows(mpkEngine e, long long rows);
 
 /* While enabled, the engine records a CUDA event pair on its stream around
- * every assignment kernel and every accumulation (update) kernel launch. */
+ * three steps of every iteration: the tensor-core assignment (the kernel
+ * alone when launched directly; the centroid split and the kernel when
+ * replayed by mpkEngineIterate), the refinement (k_refine and the wide and
+ * full-scan passes) and the accumulation (the sorted update; with
+ * mpkEngineIterate, also the finalisation). */
 mpkStatus mpkDebugProfile(mpkEngine e, int enable);
 
-/* Synchronises; summed device milliseconds and launch counts of the two
- * kernels since profiling was enabled; clears the record. */
-mpkStatus mpkDebugProfileRead(mpkEngine e, double* assign_ms, long long* assign_launches, double* accum_ms,
-                              long long* accum_launches);
+/* Synchronises; summed device milliseconds and event-pair counts of the three
+ * steps since profiling was enabled; clears the record. */
+mpkStatus mpkDebugProfileRead(mpkEngine e, double* assign_ms, long long* assign_launches, double* refine_ms,
+                              long long* refine_launches, double* accum_ms, long long* accum_launches);
 
 #ifdef __cplusplus
 }

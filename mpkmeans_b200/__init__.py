@@ -183,7 +183,7 @@ SIGNATURES = {
                                 ctypes.POINTER(_F), ctypes.POINTER(_F)]),
     "mpkDebugProfile": (_I, [_P, _I]),
     "mpkDebugProfileRead": (_I, [_P, ctypes.POINTER(_D), ctypes.POINTER(_LL), ctypes.POINTER(_D),
-                                 ctypes.POINTER(_LL)]),
+                                 ctypes.POINTER(_LL), ctypes.POINTER(_D), ctypes.POINTER(_LL)]),
     "mpkDebugWideCounters": (_I, [_P, ctypes.POINTER(_LL), ctypes.POINTER(_LL), ctypes.POINTER(_LL)]),
     "mpkDebugWideRoundRows": (_I, [_P, _LL]),
     "mpkDebugGemmStatus": (_I, [_I]),
@@ -381,11 +381,13 @@ class Engine:
         check("mpkDebugProfile", lib().mpkDebugProfile(self.h, int(bool(enable))))
 
     def profile_read(self) -> dict:
-        a, u = _D(), _D()
-        na, nu = _LL(), _LL()
+        a, r, u = _D(), _D(), _D()
+        na, nr, nu = _LL(), _LL(), _LL()
         check("mpkDebugProfileRead", lib().mpkDebugProfileRead(self.h, ctypes.byref(a), ctypes.byref(na),
+                                                               ctypes.byref(r), ctypes.byref(nr),
                                                                ctypes.byref(u), ctypes.byref(nu)))
-        return {"assign_ms": a.value, "assign_launches": na.value, "accum_ms": u.value, "accum_launches": nu.value}
+        return {"assign_ms": a.value, "assign_launches": na.value, "refine_ms": r.value, "refine_launches": nr.value,
+                "accum_ms": u.value, "accum_launches": nu.value}
 
     def trace(self, out4) -> None:
         check("mpkDebugSetAssignTrace", lib().mpkDebugSetAssignTrace(self.h, _ptr(out4)))

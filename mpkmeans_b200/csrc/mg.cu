@@ -31,6 +31,13 @@
 #include <thread>
 #include <vector>
 
+namespace mpk {
+/* mpkmeans_api.cu: excl_cond3 (or excl_cond6) of the reference's mpkStats from
+ * S->tested, the rows the bound left to the refinement and the FP32 candidates
+ * evaluated. */
+void fill_exclusions(mpkStats* S, const mpkParams& P, long long rows_refined, long long cands);
+}  /* namespace mpk */
+
 namespace {
 
 struct Nccl {
@@ -256,6 +263,7 @@ extern "C" mpkStatus mpkMeansMixedMG(int ngpu, const int* devices, const float* 
         cudaSetDevice(devices[0]);
         cudaEventElapsedTime(&ms, e0, e1);
         S->t_total_ms = ms;
+        long long rows_all = 0;
         for (int g = 0; g < ngpu; ++g) {
             cudaSetDevice(devices[g]);
             long long rows = 0, cands = 0, full = 0;
@@ -264,9 +272,11 @@ extern "C" mpkStatus mpkMeansMixedMG(int ngpu, const int* devices, const float* 
             mpkEngineCounters(eng[g], &rows, &cands, &full, &status);
             if (status) { rc = MPK_ERR_CUDA; goto done; }
             S->hp_update += cands;
+            rows_all += rows;
             if (nshard[g] > 0 && mpkEngineInertia(eng[g], dC[g], dAssign[g], &ine) != MPK_OK) { rc = MPK_ERR_CUDA; goto done; }
             S->inertia += ine;
         }
+        if (refine) mpk::fill_exclusions(S, P, rows_all, S->hp_update);
     }
 done:
     for (int g = 0; g < ngpu; ++g) {

@@ -192,24 +192,26 @@ struct mpkEngine_s {
     int pair_clusters = 0;                /* resident clusters of two for it */
     long long launches = 0;               /* kernels this engine has launched */
     bool prof = false;                    /* bench hook: events around the hot kernels */
-    std::vector<cudaEvent_t> ev_assign, ev_accum;
-    /* mpkEngineIterate: one iteration as two graphs (assignment; update),
-     * captured for these buffers and this refine flag */
+    std::vector<cudaEvent_t> ev_assign, ev_refine, ev_accum;
+    /* mpkEngineIterate: one iteration as three graphs (the tensor-core
+     * assignment; its refinement; the update), captured for these buffers and
+     * this refine flag */
     struct {
-        cudaGraphExec_t assign = nullptr, update = nullptr;
+        cudaGraphExec_t assign = nullptr, refine_g = nullptr, update = nullptr;
         const float* C = nullptr;
         const int* A = nullptr;
         const long long* S = nullptr;
         int refine = -1;
-        long long n_assign = 0, n_update = 0;   /* kernels per replay */
+        long long n_assign = 0, n_refine = 0, n_update = 0;   /* kernels per replay */
         bool failed = false;                    /* a capture failed: launch directly from then on */
     } g;
 };
 
 static void graphs_release(mpkEngine e) {
     if (e->g.assign) cudaGraphExecDestroy(e->g.assign);
+    if (e->g.refine_g) cudaGraphExecDestroy(e->g.refine_g);
     if (e->g.update) cudaGraphExecDestroy(e->g.update);
-    e->g.assign = e->g.update = nullptr;
+    e->g.assign = e->g.refine_g = e->g.update = nullptr;
     e->g.C = nullptr;
     e->g.A = nullptr;
     e->g.S = nullptr;
@@ -227,8 +229,10 @@ static void prof_mark(mpkEngine e, std::vector<cudaEvent_t>& v) {
 
 static void prof_clear(mpkEngine e) {
     for (auto x : e->ev_assign) cudaEventDestroy(x);
+    for (auto x : e->ev_refine) cudaEventDestroy(x);
     for (auto x : e->ev_accum) cudaEventDestroy(x);
     e->ev_assign.clear();
+    e->ev_refine.clear();
     e->ev_accum.clear();
 }
 
@@ -365,13 +369,10 @@ bool make_tmap_planes(CUtensorMap* map, const __half* base, long long rows, int 
 }
 }  /* namespace mpk */
 
-/* record_hist: the refinement writes its entry count to the next slot of the
- * engine's survivor history (prm->hist_next counts the slots used). */
-static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int refine, bool record_hist) {
-    if (!e->can_assign) return MPK_ERR_INVALID;
-    launch_prep_c(dC, e->k, e->kpad, e->d, e->dp, e->prm, e->Cs, e->cn, e->s);
-    ++e->launches;
-    if (e->n == 0) return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
+/* The assignment proper: the centroid split and the tensor-core pass, whose
+ * labels are final for every row it does not list for refinement. */
+/* Arguments of the engine's tensor-core pass over its own rows. */
+static AssignArgs assign_args(mpkEngine e, int* dAssign, int refine) {
     AssignArgs a;
     a.tmX = &e->tmX;
     a.tmC = &e->tmC;
@@ -396,6 +397,17 @@ static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int r
     a.wide = &e->wide;
     a.wbase = 0;
     a.stall = e->stall;
+    return a;
+}
+
+/* The assignment proper: the centroid split and the tensor-core pass, whose
+ * labels are final for every row it does not list for refinement. */
+static mpkStatus engine_assign_tc(mpkEngine e, const float* dC, int* dAssign, int refine) {
+    if (!e->can_assign) return MPK_ERR_INVALID;
+    launch_prep_c(dC, e->k, e->kpad, e->d, e->dp, e->prm, e->Cs, e->cn, e->s);
+    ++e->launches;
+    if (e->n == 0) return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
+    const AssignArgs a = assign_args(e, dAssign, refine);
     prof_mark(e, e->ev_assign);
     cudaError_t err = launch_assign(a, e->s);
     prof_mark(e, e->ev_assign);
@@ -404,42 +416,54 @@ static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int r
         fprintf(stderr, "mpkmeans_b200: assignment launch failed: %s\n", cudaGetErrorString(err));
         return MPK_ERR_CUDA;
     }
-    if (refine) {
-        launch_refine(e->P, dC, e->cn, e->d, e->k, assign_bn_for(e->k), e->list, e->prm, dAssign, e->n,
-                      record_hist ? e->hist : nullptr, MPK_MAX_HIST, e->Xs, e->n, e->dp,
-                      e->wide, e->num_sms, e->s);
-        ++e->launches;
-        /* rows the refinement queued: per round, a tensor-core pass that lists their
-         * candidates, then the FP32 evaluation of just those (every launch sizes itself from
-         * prm->nwide; rounds past the queue exit at once) */
-        for (int r = 0; r < e->wide.rounds; ++r) {
-            const long long base = (long long)r * e->wide.per_round;
-            if (r > 0) {
-                launch_wide_gather(e->list, e->Xs, e->n, e->dp, e->wide, base, e->prm, e->num_sms, e->s);
-                ++e->launches;
-            }
-            AssignArgs w = a;
-            w.tmX = &e->tmXw;
-            w.n = e->wide.per_round;
-            w.labels = nullptr;
-            w.dbg = nullptr;
-            w.emit = true;
-            w.wbase = base;
-            err = launch_assign(w, e->s);
-            if (err != cudaSuccess) {
-                fprintf(stderr, "mpkmeans_b200: wide assignment launch failed: %s\n", cudaGetErrorString(err));
-                return MPK_ERR_CUDA;
-            }
-            launch_refine_wide(e->P, dC, e->cn, e->d, e->k, e->list, e->wide, base, e->prm, dAssign, e->num_sms,
-                               e->s);
-            e->launches += 2;                 /* the emit pass and the FP32 evaluation */
-        }
-        if (e->wide.scan) {                   /* rows whose lists overflowed: all k, tiled */
-            launch_full_scan(e->P, dC, e->cn, e->d, e->k, e->wide.scan, e->prm, dAssign, e->num_sms, e->s);
+    return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
+}
+
+/* The FP32 refinement of the rows the last engine_assign_tc listed.
+ * record_hist: the refinement writes its entry count to the next slot of the
+ * engine's survivor history (prm->hist_next counts the slots used). */
+static mpkStatus engine_refine(mpkEngine e, const float* dC, int* dAssign, bool record_hist) {
+    if (e->n == 0) return MPK_OK;
+    prof_mark(e, e->ev_refine);
+    launch_refine(e->P, dC, e->cn, e->d, e->k, assign_bn_for(e->k), e->list, e->prm, dAssign, e->n,
+                  record_hist ? e->hist : nullptr, MPK_MAX_HIST, e->Xs, e->n, e->dp,
+                  e->wide, e->num_sms, e->s);
+    ++e->launches;
+    /* rows the refinement queued: per round, a tensor-core pass that lists their
+     * candidates, then the FP32 evaluation of just those (every launch sizes itself from
+     * prm->nwide; rounds past the queue exit at once) */
+    for (int r = 0; r < e->wide.rounds; ++r) {
+        const long long base = (long long)r * e->wide.per_round;
+        if (r > 0) {
+            launch_wide_gather(e->list, e->Xs, e->n, e->dp, e->wide, base, e->prm, e->num_sms, e->s);
             ++e->launches;
         }
+        AssignArgs w = assign_args(e, nullptr, 1);
+        w.tmX = &e->tmXw;
+        w.n = e->wide.per_round;
+        w.dbg = nullptr;
+        w.emit = true;
+        w.wbase = base;
+        const cudaError_t err = launch_assign(w, e->s);
+        if (err != cudaSuccess) {
+            fprintf(stderr, "mpkmeans_b200: wide assignment launch failed: %s\n", cudaGetErrorString(err));
+            return MPK_ERR_CUDA;
+        }
+        launch_refine_wide(e->P, dC, e->cn, e->d, e->k, e->list, e->wide, base, e->prm, dAssign, e->num_sms, e->s);
+        e->launches += 2;                 /* the emit pass and the FP32 evaluation */
     }
+    if (e->wide.scan) {                   /* rows whose lists overflowed: all k, tiled */
+        launch_full_scan(e->P, dC, e->cn, e->d, e->k, e->wide.scan, e->prm, dAssign, e->num_sms, e->s);
+        ++e->launches;
+    }
+    prof_mark(e, e->ev_refine);
     return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
+}
+
+static mpkStatus engine_assign(mpkEngine e, const float* dC, int* dAssign, int refine, bool record_hist) {
+    const mpkStatus st = engine_assign_tc(e, dC, dAssign, refine);
+    if (st != MPK_OK || !refine) return st;
+    return engine_refine(e, dC, dAssign, record_hist);
 }
 
 /* Capture body() on gs (a non-default stream) into an executable graph.
@@ -481,6 +505,27 @@ static mpkStatus engine_finalize(mpkEngine e, const long long* dSums, float* dC,
     return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
 }
 
+namespace mpk {
+/* The exclusion attribution of the reference's mpkStats (mpkmeans.h:147-156,
+ * filled at mpkmeans.cu:655-676), from S->tested and the engine's counters.
+ * This engine has one exclusion test: the certified bound on the tensor-core
+ * distances, formed from those values and the norms alone -- the role of the
+ * reference's condition (3).  It computes no exact reference entry per row
+ * before excluding, so condition (6) and hp_reference have no counterpart and
+ * stay 0, as in the reference's own (3)-only scheme.  Every row the bound does
+ * not settle has its incumbent evaluated in FP32 together with its candidates
+ * (all counted in hp_update), so the pairs the bound excluded are the tested
+ * pairs less the non-incumbent candidates evaluated:
+ *     excl = tested - (hp_update - rows refined).
+ * The count goes to excl_cond3, or to excl_cond6 when the caller enabled only
+ * condition (6); excl_both stays 0. */
+void fill_exclusions(mpkStats* S, const mpkParams& P, long long rows_refined, long long cands) {
+    const long long excl = S->tested - (cands - rows_refined);
+    if (P.use_cond3 || !P.use_cond6) S->excl_cond3 = excl;
+    else S->excl_cond6 = excl;
+}
+}  /* namespace mpk */
+
 extern "C" {
 
 mpkStatus mpkEngineCreate(mpkEngine* out, const float* dP, long long n, int d, int k, const float* dC0,
@@ -512,7 +557,8 @@ mpkStatus mpkEngineFinalize(mpkEngine e, const long long* dSums, float* dC, floa
 
 mpkStatus mpkEngineIterate(mpkEngine e, float* dC, int* dAssign, long long* dSums, int iters, int refine) {
     if (!e || !dC || !dAssign || !dSums || iters < 0 || !e->can_assign) return MPK_ERR_INVALID;
-    auto assign = [&] { return engine_assign(e, dC, dAssign, refine, false); };
+    auto assign = [&] { return engine_assign_tc(e, dC, dAssign, refine); };
+    auto refine_step = [&] { return engine_refine(e, dC, dAssign, false); };
     auto update = [&] {
         const mpkStatus a = engine_accumulate(e, dAssign, dSums);
         return a != MPK_OK ? a : engine_finalize(e, dSums, dC, nullptr);
@@ -526,10 +572,14 @@ mpkStatus mpkEngineIterate(mpkEngine e, float* dC, int* dAssign, long long* dSum
         const bool prof = e->prof;
         const long long l0 = e->launches;
         e->prof = false;
+        /* three graphs rather than one so that the profiling hook can time the
+         * tensor-core pass, the refinement and the update apart */
         bool ok = capture_graph(e->s, assign, &e->g.assign);
         const long long l1 = e->launches;
-        ok = ok && capture_graph(e->s, update, &e->g.update);
+        ok = ok && (!refine || capture_graph(e->s, refine_step, &e->g.refine_g));
         const long long l2 = e->launches;
+        ok = ok && capture_graph(e->s, update, &e->g.update);
+        const long long l3 = e->launches;
         e->prof = prof;
         e->launches = l0;                         /* captured, not yet run */
         if (ok) {
@@ -538,7 +588,8 @@ mpkStatus mpkEngineIterate(mpkEngine e, float* dC, int* dAssign, long long* dSum
             e->g.S = dSums;
             e->g.refine = refine;
             e->g.n_assign = l1 - l0;
-            e->g.n_update = l2 - l1;
+            e->g.n_refine = l2 - l1;
+            e->g.n_update = l3 - l2;
             have = true;
         } else {
             graphs_release(e);
@@ -550,12 +601,18 @@ mpkStatus mpkEngineIterate(mpkEngine e, float* dC, int* dAssign, long long* dSum
             prof_mark(e, e->ev_assign);
             if (cudaGraphLaunch(e->g.assign, e->s) != cudaSuccess) return MPK_ERR_CUDA;
             prof_mark(e, e->ev_assign);
+            if (e->g.refine_g) {
+                prof_mark(e, e->ev_refine);
+                if (cudaGraphLaunch(e->g.refine_g, e->s) != cudaSuccess) return MPK_ERR_CUDA;
+                prof_mark(e, e->ev_refine);
+            }
             prof_mark(e, e->ev_accum);
             if (cudaGraphLaunch(e->g.update, e->s) != cudaSuccess) return MPK_ERR_CUDA;
             prof_mark(e, e->ev_accum);
-            e->launches += e->g.n_assign + e->g.n_update;
+            e->launches += e->g.n_assign + e->g.n_refine + e->g.n_update;
         } else {
             mpkStatus st = assign();
+            if (st == MPK_OK && refine) st = refine_step();
             if (st == MPK_OK) st = update();
             if (st != MPK_OK) return st;
         }
@@ -605,7 +662,8 @@ mpkStatus mpkDebugSetAssignTrace(mpkEngine e, float* dOut4) {
 }
 
 /* Bench hook: while enabled, the engine records a CUDA event pair on its
- * stream around every assignment kernel and every accumulation kernel. */
+ * stream around every tensor-core assignment, refinement and accumulation
+ * step (include/mpkmeans_debug.h says what each pair covers). */
 mpkStatus mpkDebugProfile(mpkEngine e, int enable) {
     if (!e) return MPK_ERR_INVALID;
     cudaStreamSynchronize(e->s);
@@ -614,26 +672,26 @@ mpkStatus mpkDebugProfile(mpkEngine e, int enable) {
     return MPK_OK;
 }
 
-/* Synchronises, returns the summed device time and launch counts of the two
- * kernels since mpkDebugProfile(e, 1), and clears the record. */
-mpkStatus mpkDebugProfileRead(mpkEngine e, double* assign_ms, long long* assign_launches, double* accum_ms,
-                              long long* accum_launches) {
+/* Synchronises, returns the summed device time and launch counts of the
+ * three profiled steps since mpkDebugProfile(e, 1), and clears the record. */
+mpkStatus mpkDebugProfileRead(mpkEngine e, double* assign_ms, long long* assign_launches, double* refine_ms,
+                              long long* refine_launches, double* accum_ms, long long* accum_launches) {
     if (!e) return MPK_ERR_INVALID;
     MPK_TRY(cudaStreamSynchronize(e->s));
-    double a = 0.0, u = 0.0;
-    for (size_t i = 0; i + 1 < e->ev_assign.size(); i += 2) {
-        float ms = 0.f;
-        cudaEventElapsedTime(&ms, e->ev_assign[i], e->ev_assign[i + 1]);
-        a += ms;
-    }
-    for (size_t i = 0; i + 1 < e->ev_accum.size(); i += 2) {
-        float ms = 0.f;
-        cudaEventElapsedTime(&ms, e->ev_accum[i], e->ev_accum[i + 1]);
-        u += ms;
-    }
-    if (assign_ms) *assign_ms = a;
+    auto total = [](const std::vector<cudaEvent_t>& v) {
+        double t = 0.0;
+        for (size_t i = 0; i + 1 < v.size(); i += 2) {
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, v[i], v[i + 1]);
+            t += ms;
+        }
+        return t;
+    };
+    if (assign_ms) *assign_ms = total(e->ev_assign);
     if (assign_launches) *assign_launches = (long long)(e->ev_assign.size() / 2);
-    if (accum_ms) *accum_ms = u;
+    if (refine_ms) *refine_ms = total(e->ev_refine);
+    if (refine_launches) *refine_launches = (long long)(e->ev_refine.size() / 2);
+    if (accum_ms) *accum_ms = total(e->ev_accum);
     if (accum_launches) *accum_launches = (long long)(e->ev_accum.size() / 2);
     prof_clear(e);
     return MPK_OK;
@@ -772,8 +830,10 @@ mpkStatus mpkShiftCentroids(float* dC, int k, int d, float delta) {
 /* ------------------------------------------------------------ drivers --- */
 
 
+
 static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k, float* dC, int* dAssign,
-                       const mpkParams* params, mpkStats* stats, bool force_refine, const char* tag) {
+                       const mpkParams* params, mpkStats* stats, bool force_refine, bool exclusion_stats,
+                       const char* tag) {
     if (n <= 0 || d <= 0 || k <= 0 || k > n || !dP || !dC || !dAssign) return MPK_ERR_INVALID;
     mpkParams P;
     if (params) P = *params; else mpkParamsInit(&P);
@@ -873,7 +933,7 @@ static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k
         }
         cudaEventRecord(ev[4 * it + 2], gs);
         S->hp_baseline += (long long)n * k;
-        S->tested += (long long)n * (k - 1);
+        if (exclusion_stats) S->tested += (long long)n * (k - 1);
         if (P.tol > 0.f || P.verbose) {
             unsigned long long hv[2] = {0, 0};   /* changed labels, rows refined this iteration */
             cudaMemcpyAsync(h_moved.data(), moved2, (size_t)k * sizeof(float), cudaMemcpyDeviceToHost, gs);
@@ -916,6 +976,7 @@ static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k
         int status = 0;
         mpkEngineCounters(e, &rows, &cands, &full, &status);
         S->hp_update = cands;
+        if (exclusion_stats && refine) fill_exclusions(S, P, rows, cands);
         S->n_hist = it < MPK_MAX_HIST ? it : MPK_MAX_HIST;
         cudaMemcpy(S->hist_survivors, e->hist, sizeof(long long) * S->n_hist, cudaMemcpyDeviceToHost);
         if (verify) {
@@ -962,12 +1023,12 @@ done:
 
 mpkStatus mpkMeansMixed(cublasHandle_t blas, const float* dP, int n, int d, int k, float* dC, int* dAssign,
                         const mpkParams* params, mpkStats* stats) {
-    return lloyd(blas, dP, n, d, k, dC, dAssign, params, stats, false, "mixed");
+    return lloyd(blas, dP, n, d, k, dC, dAssign, params, stats, false, true, "mixed");
 }
 
 mpkStatus mpkMeansFP32(cublasHandle_t blas, const float* dP, int n, int d, int k, float* dC, int* dAssign,
                        const mpkParams* params, mpkStats* stats) {
-    return lloyd(blas, dP, n, d, k, dC, dAssign, params, stats, true, "fp32");
+    return lloyd(blas, dP, n, d, k, dC, dAssign, params, stats, true, false, "fp32");
 }
 
 /* The reference's double-fp16 driver (kmeans/src/multiword.cu:245-645) refuses
@@ -983,7 +1044,7 @@ mpkStatus mpkMeansMultiword(cublasHandle_t blas, const float* dP, int n, int d, 
         fprintf(stderr, "mpkMeansMultiword: at least one condition must be on\n");
         return MPK_ERR_INVALID;
     }
-    mpkStatus st = lloyd(blas, dP, n, d, k, dC, dAssign, params, S, true, "mw");
+    mpkStatus st = lloyd(blas, dP, n, d, k, dC, dAssign, params, S, true, true, "mw");
     if (st == MPK_OK) {
         S->mw_products = 3LL * S->iters;
         S->mw_refine_rows = 0;
@@ -1023,6 +1084,7 @@ mpkStatus mpkAssign(cublasHandle_t blas, const float* dP, int n, int d, int k, c
         stats->hp_baseline = (long long)n * k;
         stats->tested = (long long)n * (k - 1);
         stats->hp_update = cands;
+        if (refine) fill_exclusions(stats, P, rows, cands);
         stats->n_hist = 1;
         stats->hist_survivors[0] = rows;
         if (status) st = MPK_ERR_CUDA;

@@ -9,16 +9,25 @@
  * part of the library image: every GPU that loads the library holds these
  * kNoAllocScratchBytes (32 MiB) until the process exits.
  *
+ * With CUDA's lazy module loading (the default) the array is only placed on a
+ * device when the library's code is first loaded there, which the first call
+ * does: that call grows the device footprint by the 32 MiB, so a caller whose
+ * footprint must stay fixed makes one call at start-up.
+ *
  * Host code cannot use the array's name as a device address, so the first
  * call on each device resolves it with cudaGetSymbolAddress (with that device
- * current) and caches it; that first call should therefore come before any
- * stream capture.  The array keeps the contents of the last call: everything
- * that must start from zero is cleared at the start of every call, and two
- * calls that overlap on the GPU (on different streams, or from several host
- * threads) would race on it.
+ * current) and caches it together with the device's current context; a new
+ * context on that device (after cudaDeviceReset, say) makes the next call
+ * resolve it again.  That first call should come before any stream capture.
+ * The array keeps the contents of the last call: everything that must start
+ * from zero is cleared at the start of every call, and two calls that overlap
+ * on the GPU (on different streams, or from several host threads) would race
+ * on it.
  */
 #include "engine.cuh"
 #include "mpkmeans.h"
+
+#include <cudaTypedefs.h>
 
 #include <cstdio>
 #include <mutex>
@@ -32,22 +41,44 @@ static __device__ __align__(256) unsigned char g_update_scratch[kNoAllocScratchB
 
 std::mutex g_addr_mutex;
 void* g_addr[kMaxDevices] = {};
+CUcontext g_ctx[kMaxDevices] = {};
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-/* Device address of g_update_scratch on the current device (resolved once). */
+/* The calling thread's current context (the driver's cuCtxGetCurrent, looked up
+ * through the runtime so the library does not link the driver library). */
+CUcontext current_context() {
+    static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 4000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(f);
+    });
+    CUcontext c = nullptr;
+    if (fn && fn(&c) != CUDA_SUCCESS) c = nullptr;
+    return c;
+}
+
+/* Device address of g_update_scratch on the current device: resolved on the
+ * first call in each of the device's contexts, cached after that. */
 void* scratch_address(int dev) {
     if (dev < 0 || dev >= kMaxDevices) return nullptr;
+    const CUcontext ctx = current_context();
     std::lock_guard<std::mutex> lock(g_addr_mutex);
-    if (!g_addr[dev]) {
+    if (!g_addr[dev] || !ctx || g_ctx[dev] != ctx) {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_update_scratch);
         if (e != cudaSuccess) {
             fprintf(stderr, "mpkUpdateNoAlloc: cudaGetSymbolAddress failed on device %d: %s\n", dev,
                     cudaGetErrorString(e));
+            g_addr[dev] = nullptr;
             return nullptr;
         }
         g_addr[dev] = p;
+        g_ctx[dev] = ctx;
     }
     return g_addr[dev];
 }

@@ -7,12 +7,12 @@
  *   k_label_hist     labels -> per-cluster counts (shared-memory histogram)
  *   k_bin_scan       counts -> bin starts; counts written to the sums buffer
  *   k_label_scatter  row indices grouped by label (perm)
- *   k_segsum         each warp walks a contiguous run of perm, reading whole
- *                    point rows (coalesced, 16 B per lane), quantising every
- *                    coordinate once to q = rint(x * 2^frac) and adding into
- *                    int64 registers; at a label boundary (and at the end of
- *                    its run) the warp adds its registers into the global
- *                    int64 sums.
+ *   k_segsum         each warp walks a contiguous run of perm over one
+ *                    128-feature slice of the rows (coalesced, 16 B per lane),
+ *                    quantising every coordinate once to q = rint(x * 2^frac)
+ *                    and adding into int64 registers; at a label boundary (and
+ *                    at the end of its run) the warp adds its registers into
+ *                    the global int64 sums.
  *
  * Integer sums are exact, so the result does not depend on the order of the
  * rows within a cluster, on the split of the work, or on the number of GPUs
@@ -24,6 +24,7 @@ namespace mpk {
 namespace {
 
 constexpr int kSmemHistMax = 48 * 1024;   /* labels per shared-memory histogram */
+constexpr unsigned FULL = 0xffffffffu;
 
 template <bool SMEM>
 __global__ void k_label_hist(const int* __restrict__ labels, long long n, int k, int* __restrict__ hist,
@@ -113,17 +114,26 @@ __device__ __forceinline__ long long quantise(float x, float sc) {
     return __float2ll_rn(x * sc);
 }
 
-/* Segmented sum over the label-sorted rows.  VEC = 4: lane l owns features
- * 4l..4l+3 of every 128-feature group (float4 loads); VEC = 1: lane l owns
- * features l, l+32, ...  NG groups per lane cover d.  U rows are loaded at
- * once; a narrow row (d <= 64: half the lanes or fewer hold a feature) takes
- * U = 8, since each load then moves little. */
-template <int VEC, int NG, int U = (NG <= 2 ? 4 : (NG <= 4 ? 2 : 1))>
-__global__ void __launch_bounds__(256)
-k_segsum(const float* __restrict__ P, int d, int f0, const int* __restrict__ perm, const int* __restrict__ bin_start,
+/* Segmented sum over the label-sorted rows, one feature slice per warp: slice
+ * blockIdx.y covers features [y * SPAN, (y + 1) * SPAN), SPAN = 32 * VEC.
+ * VEC = 4: lane l owns features 4l..4l+3 of the slice (float4 loads); VEC = 1:
+ * lane l owns feature l.  Wide rows are thus read by several warps at once,
+ * each a 512-byte (or 128-byte) piece, rather than by one warp with fewer
+ * rows in flight.
+ *
+ * A warp walks its contiguous run of perm 32 entries at a time: lane l loads
+ * entry e + l (one coalesced load, issued a chunk ahead), and the row indices
+ * reach the loads by shuffle, so no row load waits on a perm load; U = 8 rows
+ * are loaded at once. */
+template <int VEC, int U = 8>
+__global__ void __launch_bounds__(256, 4)
+k_segsum(const float* __restrict__ P, int d, const int* __restrict__ perm, const int* __restrict__ bin_start,
          int k, const DevParams* __restrict__ prm, long long* __restrict__ sums) {
-    constexpr int SPAN = 32 * VEC;                 /* features per group */
+    static_assert(32 % U == 0, "row batches tile a chunk of 32 entries");
+    constexpr int SPAN = 32 * VEC;                 /* features per slice */
     const int lane = threadIdx.x & 31;
+    const int f = blockIdx.y * SPAN + (VEC == 4 ? 4 * lane : lane);   /* this lane's first feature */
+    const bool has = f < d;
     const long long total = bin_start[k];
     const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
     const long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -141,94 +151,57 @@ k_segsum(const float* __restrict__ P, int d, int f0, const int* __restrict__ per
     long long next = bin_start[bin + 1];
     while (next <= e0) { ++bin; next = bin_start[bin + 1]; }
 
-    long long acc[NG][VEC];
+    long long acc[VEC];
 #pragma unroll
-    for (int g = 0; g < NG; ++g)
-#pragma unroll
-        for (int v = 0; v < VEC; ++v) acc[g][v] = 0;
+    for (int v = 0; v < VEC; ++v) acc[v] = 0;
 
     auto flush = [&](int b) {
 #pragma unroll
-        for (int g = 0; g < NG; ++g)
-#pragma unroll
-            for (int v = 0; v < VEC; ++v) {
-                const int f = f0 + g * SPAN + (VEC == 4 ? 4 * lane + v : lane);
-                if (f < d && acc[g][v])
-                    atomicAdd(reinterpret_cast<unsigned long long*>(&sums[(size_t)b * d + f]),
-                              (unsigned long long)acc[g][v]);
-                acc[g][v] = 0;
-            }
+        for (int v = 0; v < VEC; ++v) {
+            if (has && acc[v])
+                atomicAdd(reinterpret_cast<unsigned long long*>(&sums[(size_t)b * d + f + v]),
+                          (unsigned long long)acc[v]);
+            acc[v] = 0;
+        }
     };
 
-    for (long long e = e0; e < e1; e += U) {
-        float x[U][NG][VEC];
+    int idx = e0 + lane < e1 ? perm[e0 + lane] : 0;
+    for (long long e = e0; e < e1; e += 32) {
+        const int cnt = (int)min(32LL, e1 - e);
+        const int cur = idx;
+        idx = e + 32 + lane < e1 ? perm[e + 32 + lane] : 0;      /* the next chunk's entries */
+#pragma unroll 1
+        for (int u0 = 0; u0 < cnt; u0 += U) {
+            float x[U][VEC];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const bool live = e + u < e1;
-            const int row = live ? perm[e + u] : 0;
-            const float* p = P + (size_t)row * d;
-#pragma unroll
-            for (int g = 0; g < NG; ++g) {
-                if (VEC == 4) {
-                    const int f = f0 + g * SPAN + 4 * lane;
+            for (int u = 0; u < U; ++u) {
+                const bool live = has && u0 + u < cnt;
+                const float* p = P + (size_t)__shfl_sync(FULL, cur, (u0 + u) & 31) * d + f;
+                if constexpr (VEC == 4) {
                     float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (live && f < d) t = __ldg(reinterpret_cast<const float4*>(p + f));
-                    x[u][g][0] = t.x; x[u][g][1] = t.y; x[u][g][2] = t.z; x[u][g][3] = t.w;
+                    if (live) t = __ldg(reinterpret_cast<const float4*>(p));
+                    x[u][0] = t.x; x[u][1] = t.y; x[u][2] = t.z; x[u][3] = t.w;
                 } else {
-                    const int f = f0 + g * SPAN + lane;
-                    x[u][g][0] = (live && f < d) ? __ldg(p + f) : 0.f;
+                    x[u][0] = live ? __ldg(p) : 0.f;
                 }
             }
-        }
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            if (e + u >= e1) break;
-            while (e + u >= next) {       /* warp-uniform: every lane holds the same e */
-                flush(bin);
-                ++bin;
-                next = bin_start[bin + 1];
+            for (int u = 0; u < U; ++u) {
+                if (u0 + u >= cnt) break;
+                while (e + u0 + u >= next) {   /* warp-uniform: every lane holds the same entry */
+                    flush(bin);
+                    ++bin;
+                    next = bin_start[bin + 1];
+                }
+#pragma unroll
+                for (int v = 0; v < VEC; ++v) acc[v] += quantise(x[u][v], sc);
             }
-#pragma unroll
-            for (int g = 0; g < NG; ++g)
-#pragma unroll
-                for (int v = 0; v < VEC; ++v) acc[g][v] += quantise(x[u][g][v], sc);
         }
     }
     flush(bin);
 }
 
 int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
-
-template <int VEC>
-void launch_segsum_window(const float* P, int d, int f0, int ng, const int* perm, const int* bin_start, int k,
-                          const DevParams* prm, long long* sums, int blocks, cudaStream_t s) {
-    switch (ng) {
-        case 1:
-            if (d <= 64) k_segsum<VEC, 1, 8><<<blocks, 256, 0, s>>>(P, d, f0, perm, bin_start, k, prm, sums);
-            else k_segsum<VEC, 1><<<blocks, 256, 0, s>>>(P, d, f0, perm, bin_start, k, prm, sums);
-            break;
-        case 2: k_segsum<VEC, 2><<<blocks, 256, 0, s>>>(P, d, f0, perm, bin_start, k, prm, sums); break;
-        case 3: k_segsum<VEC, 3><<<blocks, 256, 0, s>>>(P, d, f0, perm, bin_start, k, prm, sums); break;
-        case 4: k_segsum<VEC, 4><<<blocks, 256, 0, s>>>(P, d, f0, perm, bin_start, k, prm, sums); break;
-        case 5: k_segsum<VEC, 5><<<blocks, 256, 0, s>>>(P, d, f0, perm, bin_start, k, prm, sums); break;
-        case 6: k_segsum<VEC, 6><<<blocks, 256, 0, s>>>(P, d, f0, perm, bin_start, k, prm, sums); break;
-        case 7: k_segsum<VEC, 7><<<blocks, 256, 0, s>>>(P, d, f0, perm, bin_start, k, prm, sums); break;
-        default: k_segsum<VEC, 8><<<blocks, 256, 0, s>>>(P, d, f0, perm, bin_start, k, prm, sums); break;
-    }
-}
-
-/* One launch per window of up to 8 groups of features. */
-template <int VEC>
-int launch_segsum(const float* P, int d, const int* perm, const int* bin_start, int k, const DevParams* prm,
-                  long long* sums, int blocks, cudaStream_t s) {
-    constexpr int WIN = 8 * 32 * VEC;
-    int launches = 0;
-    for (int f0 = 0; f0 < d; f0 += WIN, ++launches) {
-        const int ng = ceil_div(min(WIN, d - f0), 32 * VEC);
-        launch_segsum_window<VEC>(P, d, f0, ng, perm, bin_start, k, prm, sums, blocks, s);
-    }
-    return launches;
-}
 
 }  /* namespace */
 
@@ -252,11 +225,15 @@ int launch_update_sorted(const float* P, long long n, int d, const int* labels, 
     if (smem) k_label_scatter<true><<<blocks, 512, hb, s>>>(labels, n, k, sc.cursor, sc.perm, rpb);
     else k_label_scatter<false><<<blocks, 512, 0, s>>>(labels, n, k, sc.cursor, sc.perm, rpb);
     const bool vec = (d % 4 == 0) && ((reinterpret_cast<uintptr_t>(P) & 15) == 0);
-    /* eight warps a block; at least 32 rows a warp, so that a small problem does not pay
-     * a bin search and a flush of atomics for every handful of rows */
-    const int sblocks = (int)std::max<long long>(1, std::min<long long>((long long)num_sms * 8, (n + 255) / 256));
-    const int seg = vec ? launch_segsum<4>(P, d, sc.perm, sc.bin_start, k, prm, sums, sblocks, s)
-                        : launch_segsum<1>(P, d, sc.perm, sc.bin_start, k, prm, sums, sblocks, s);
+    /* eight warps a block, about eight blocks per SM over all feature slices; at least 32
+     * rows a warp, so that a small problem does not pay a bin search and a flush of atomics
+     * for every handful of rows */
+    const int ny = ceil_div(d, vec ? 128 : 32);
+    const long long want = std::max<long long>(1, ((long long)num_sms * 8 + ny - 1) / ny);
+    const dim3 grid((unsigned)std::max<long long>(1, std::min<long long>(want, (n + 255) / 256)), (unsigned)ny);
+    if (vec) k_segsum<4><<<grid, 256, 0, s>>>(P, d, sc.perm, sc.bin_start, k, prm, sums);
+    else k_segsum<1><<<grid, 256, 0, s>>>(P, d, sc.perm, sc.bin_start, k, prm, sums);
+    const int seg = 1;
     return 3 + seg;                       /* hist, scan, scatter, segmented sums */
 }
 

@@ -11,7 +11,11 @@
 # (mpkmeans.cu:555-582) is available.  The output is git-ignored; it travels to
 # the GPU box with the working tree.  Usage: oracle/build_ref.sh [REF_ROOT]
 set -euo pipefail
-REF="${1:-${MPK_REFERENCE_ROOT:-/root/reference}}"
+REF="${1:-${MPK_REFERENCE_ROOT:-}}"
+if [ -z "$REF" ]; then
+  echo "$(basename "$0"): give the reference checkout as the first argument or in MPK_REFERENCE_ROOT" >&2
+  exit 2
+fi
 HERE="$(cd "$(dirname "$0")" && pwd)"
 OUT="$HERE/_ref"
 if [ ! -d "$REF/kmeans/src" ]; then

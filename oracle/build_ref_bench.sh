@@ -12,10 +12,14 @@
 # The _b200 binaries are the drop-in check: the reference's programs run on
 # this library through the C ABI alone.  All travel with the working tree
 # (git-ignored).
-# Usage: oracle/build_ref_bench.sh [REF_ROOT]   (needs libmpkref.so and
+# Usage: oracle/build_ref_bench.sh REF_ROOT (or MPK_REFERENCE_ROOT)   (needs libmpkref.so and
 # libmpkmeans_b200.so built first)
 set -euo pipefail
-REF="${1:-${MPK_REFERENCE_ROOT:-/root/reference}}"
+REF="${1:-${MPK_REFERENCE_ROOT:-}}"
+if [ -z "$REF" ]; then
+  echo "$(basename "$0"): give the reference checkout as the first argument or in MPK_REFERENCE_ROOT" >&2
+  exit 2
+fi
 HERE="$(cd "$(dirname "$0")" && pwd)"
 ROOT="$(cd "$HERE/.." && pwd)"
 OUT="$HERE/_ref"

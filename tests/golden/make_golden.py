@@ -8,7 +8,7 @@ files (tolerance pins where the reference's arithmetic is cuBLAS's, exact pins
 where it is its own code).
 
 Usage (GPU machine, from the repository root):
-    python tests/golden/make_golden.py [outdir] [--only kmeans|mpemu|large]
+    python tests/golden/make_golden.py [outdir] [--only kmeans|mpemu|large|floor]
 
 The ``large`` cases (configs 4 and 5 shapes on row samples) also run this
 repository's engine (mpkmeans_b200) for two Lloyd iterations and then let the
@@ -254,6 +254,76 @@ def large_cases():
         print(name, "done")
 
 
+def _colperm_run(P, C0, iters, q):
+    """The reference on P and C0 with their coordinates permuted by q (the same points and
+    centroids; only the order of every FP32 dot product changes), mapped back."""
+    lab, C, st = run("mpkMeansFP32", np.ascontiguousarray(P[:, q]), np.ascontiguousarray(C0[:, q]), iters)
+    return lab, np.ascontiguousarray(C[:, np.argsort(q)]), st.inertia
+
+
+def floor_cases():
+    """The reference against itself: how far two of its own FP32 runs on the same
+    problem drift apart.  Each variant changes nothing a k-means answer depends on:
+    `rerun` repeats the call (its FP64-atomic update sums in arrival order), `rowperm`
+    permutes the rows (labels mapped back), `colperm*` permutes the coordinates of the
+    points and start centroids alike (every FP32 dot is summed in another order; the
+    centroids are mapped back).  The agreement between these runs is the noise floor
+    that end-of-run label and centroid agreement with any other FP32 implementation
+    is read against."""
+    rng = np.random.default_rng(2024)
+    out = {}
+
+    def store(prefix, lab, C, ine, dt):
+        out[f"{prefix}_labels"] = lab.astype(dt)
+        if C is not None:
+            out[f"{prefix}_C"] = C
+        if ine is not None:
+            out[f"{prefix}_inertia"] = np.float64(ine)
+
+    # BASELINE config 1: n = 1e5, d = 32, k = 64, k-means++ from seed 1, 20 iterations (and 100)
+    P = O.make_config1(100_000, 32, seed=1)
+    C0 = O.kmeanspp(P, 64, seed=1)
+    n, d = P.shape
+    out["c1_C0"] = C0
+    for iters in (20, 100):
+        lab, C, st = run("mpkMeansFP32", P, C0, iters)
+        store(f"c1_{iters}_base", lab, C, st.inertia, np.int8)
+        lab, C, st = run("mpkMeansFP32", P, C0, iters)
+        store(f"c1_{iters}_rerun", lab, C, st.inertia, np.int8)
+        perm = rng.permutation(n)
+        inv = np.empty(n, np.int64)
+        inv[perm] = np.arange(n)
+        lab, C, st = run("mpkMeansFP32", np.ascontiguousarray(P[perm]), C0, iters)
+        store(f"c1_{iters}_rowperm", lab[inv], C, st.inertia, np.int8)
+        for s in range(3):
+            lab, C, ine = _colperm_run(P, C0, iters, rng.permutation(d))
+            store(f"c1_{iters}_colperm{s}", lab, C, ine, np.int8)
+        print("floor config1", iters, "done")
+
+    # config-3 shape sample (n = 2e5, d = 128, k = 1024), 3 iterations
+    P = O.make_gmm(200_000, 128, 1024, 3, 5.0, 0.5, 2.0, True)
+    C0 = P[np.sort(O.init_random_idx(200_000, 1024, 3))].copy()
+    lab, C, st = run("mpkMeansFP32", P, C0, 3)
+    store("c3s_base", lab, C, st.inertia, np.int16)
+    for s in range(2):
+        lab, C, ine = _colperm_run(P, C0, 3, rng.permutation(128))
+        store(f"c3s_colperm{s}", lab, C, ine, np.int16)
+
+    # configs 4 and 5 geometries on the row samples of large_cases: iteration 0 (one assignment)
+    for tag, P, k, seed in (("c4s", O.make_sphere(30_000, 768, 4096, 41), 4096, 41),
+                            ("c5s", O.make_offset(40_000, 256, 16384, 51, 1e3), 16384, 51)):
+        n, d = P.shape
+        C0 = P[np.sort(O.init_random_idx(n, k, seed))].copy()
+        lab, _, _ = run("mpkMeansFP32", P, C0, 1)
+        store(f"{tag}_base", lab, None, None, np.int16)
+        for s in range(2):
+            lab, _, _ = _colperm_run(P, C0, 1, rng.permutation(d))
+            store(f"{tag}_colperm{s}", lab, None, None, np.int16)
+        print("floor", tag, "done")
+    np.savez_compressed(OUT / "ref_floor.npz", **out)
+    print("ref_floor done")
+
+
 if __name__ == "__main__":
     OUT.mkdir(parents=True, exist_ok=True)
     if ONLY in (None, "kmeans"):
@@ -262,3 +332,5 @@ if __name__ == "__main__":
         mpemu_cases()
     if ONLY in (None, "large"):
         large_cases()
+    if ONLY in (None, "floor"):
+        floor_cases()

@@ -41,3 +41,36 @@ def summary(P, C, la, lr):
     idx, g32, g64 = gaps(P, C, la, lr)
     return {"n": int(len(la)), "mismatches": int(len(idx)), "agree": float(1.0 - len(idx) / max(1, len(la))),
             "max_gap32": float(g32.max()) if len(idx) else 0.0, "max_gap64": float(g64.max()) if len(idx) else 0.0}
+
+
+# ------------------------------------------------------------- noise floor --
+
+def end_of_run(P, base, run):
+    """Agreement of one end-of-run result `run` = (labels, C, inertia) with the reference's
+    `base` run: label agreement, relative Frobenius distance of the centroids and relative
+    inertia difference.  (The centroids differ between runs, so a mismatch is not a
+    near-tie on one set of centroids; these three numbers are what end-of-run parity
+    can be read from.)"""
+    lb, Cb, ib = base
+    la, Ca, ia = run
+    Cb64 = np.asarray(Cb, np.float64)
+    return {"agree": float((np.asarray(la) == np.asarray(lb)).mean()),
+            "C_rel": float(np.linalg.norm(np.asarray(Ca, np.float64) - Cb64) / np.linalg.norm(Cb64)),
+            "inertia_rel": abs(float(ia) - float(ib)) / abs(float(ib))}
+
+
+def within_floor(ours, floors, slack=1.25):
+    """True when `ours` (an end_of_run dict against the reference) meets the north-star bar --
+    labels >= 99.99 %, centroids and inertia within 1e-5 relative -- or, where the reference
+    does not meet it against itself (`floors`: end_of_run dicts of the reference's own
+    variant runs against its base run), is no further from the reference than those runs
+    are, up to `slack` times their largest distance.  Returns (ok, bar) with the bar used."""
+    worst = {"disagree": max(1.0 - f["agree"] for f in floors),
+             "C_rel": max(f["C_rel"] for f in floors),
+             "inertia_rel": max(f["inertia_rel"] for f in floors)}
+    bar = {"disagree": max(1e-4, slack * worst["disagree"]),
+           "C_rel": max(1e-5, slack * worst["C_rel"]),
+           "inertia_rel": max(1e-5, slack * worst["inertia_rel"])}
+    ok = (1.0 - ours["agree"] <= bar["disagree"] and ours["C_rel"] <= bar["C_rel"]
+          and ours["inertia_rel"] <= bar["inertia_rel"])
+    return ok, bar

@@ -72,3 +72,32 @@ def test_two_gloo_ranks_match_single_process():
     _, C_single, _, _ = O.lloyd(P, C0, 3, update_mode=1, frac=frac)
     for C in res:
         assert np.array_equal(C.view(np.uint32), C_single.view(np.uint32))
+
+
+def _start_worker(rank, world, port, out):
+    import bench
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        n = 150_000
+        r0, n_local, n_total = bench.workload_rows("config3", n, world, rank)
+        P = bench.gen_rows("config3", r0, r0 + n_local, "cpu")
+        out[rank] = bench.start_centroids(P, r0, n_total, 1024, world, "cpu").numpy()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_bench_start_centroids_are_the_same_for_any_rank_count():
+    """bench.py's shards: each of two gloo ranks generates only its own rows, and the start
+    centroids assembled across them equal the single-process ones bit for bit."""
+    import bench
+    world = 2
+    port = _free_port()
+    with mp.Manager() as m:
+        out = m.dict()
+        mp.start_processes(_start_worker, args=(world, port, out), nprocs=world, start_method="spawn", join=True)
+        res = [out[r] for r in range(world)]
+    P = bench.gen_rows("config3", 0, 150_000, "cpu")
+    want = bench.start_centroids(P, 0, 150_000, 1024, 1, "cpu").numpy()
+    for C in res:
+        assert np.array_equal(C.view(np.uint32), want.view(np.uint32))

@@ -86,7 +86,32 @@ def compare(args):
 
 
 def test_blobs_default_shape(binaries):
-    compare(["-n", "200000", "-d", "64", "-k", "32", "-i", "20", "-e", "3"])
+    ours, ref = compare(["-n", "200000", "-d", "64", "-k", "32", "-i", "20", "-e", "3"])
+    check_exclusion_columns(ours, ref)
+
+
+def check_exclusion_columns(ours, ref):
+    """The exclusion attribution columns (main.cu:557-580) from this library: its one
+    exclusion test, the certified bound on the tensor-core distances, is reported as
+    condition (3) (it needs no exact reference entry, as (3) does not), so pct_cond3 is
+    filled and equal to pct_cond3_only, condition (6)'s columns and pct_reference are 0,
+    and the pairs left to the FP32 refinement (pct_update) plus those excluded cover the
+    tested pairs.  The reference's own (3) row excludes pairs too; both are reported."""
+    for cond in SCHEMES:
+        r, q = ours[cond], ref[cond]
+        c3, c3o = float(r["pct_cond3"]), float(r["pct_cond3_only"])
+        print(cond, "ours pct_cond3", c3, "pct_update", r["pct_update"], "ref pct_cond3", q["pct_cond3"],
+              "pct_cond6", q["pct_cond6"], "pct_update", q["pct_update"])
+        assert 50.0 < c3 <= 100.0 and c3 == c3o, (cond, r)
+        assert float(r["pct_cond6"]) == 0.0 and float(r["pct_cond6_only"]) == 0.0, (cond, r)
+        assert float(r["pct_reference"]) == 0.0 and int(r["hp_reference"]) == 0, (cond, r)
+        # excluded + non-incumbent FP32 evaluations = tested; hp_update counts the incumbents
+        # too (at most one per row and iteration), so pct_update (of n*k) brackets the rest
+        iters, n, k = int(r["iters"]), int(r["n"]), int(r["k"])
+        tested = n * (k - 1) * iters
+        excluded = c3 / 100.0 * tested
+        evaluated = float(r["pct_update"]) / 100.0 * n * k * iters
+        assert tested - evaluated - 1e-4 * tested <= excluded <= tested - evaluated + n * iters + 1e-4 * tested, (cond, r)
 
 
 def test_blobs_overlapping_zscore_fp16_accum(binaries):

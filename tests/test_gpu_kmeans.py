@@ -4,9 +4,15 @@ Bit-exact bars (integer / index work and the FP32 arithmetic the engine pins):
   * labels == the oracle's FP32 argmin of fmaf(-2, dot_warp, ||c||^2), the
     reference's refinement order, smaller index on ties;
   * centroids == the oracle's fixed-point update, bit for bit;
-Tolerance bars against the reference's own outputs (golden fixtures):
-  * label mismatches only on near-ties, FP64 relative gap < 1e-5;
-  * centroids within 1e-5 relative (per-centroid norm), inertia within 1e-5.
+Tolerance bars against the reference's own outputs (golden fixtures, and the
+reference library itself at config 3's full size):
+  * per iteration, on the reference's own centroids: labels agree on >= 99.99 %
+    and every mismatch is an FP32 near-tie (gap32 < 1e-5);
+  * end of run: labels >= 99.99 %, centroids and inertia within 1e-5 relative --
+    or, where the reference misses that bar against itself (the same problem
+    with its coordinates permuted, which changes only the FP32 summation order:
+    tests/golden/ref_floor.npz, and live at config 3), no further from the
+    reference than its own runs are (parity.within_floor).
 """
 import ctypes
 
@@ -338,12 +344,22 @@ def test_lloyd_config1_vs_reference_golden(cuda):
             s = parity.summary(P, C, lab, g["traj_labels"][t].astype(np.int32))
             assert s["max_gap32"] < 1e-5 and s["agree"] >= 0.9999, (t, s)
             C = g["traj_C"][t]
-    dC = dev(g["C0"])
-    lab = torch.empty(P.shape[0], dtype=torch.int32, device="cuda")
-    st = M.means_mixed(dP, dC, lab, M.params_init(max_iter=20))
-    lab = lab.cpu().numpy()
-    assert (lab == g["labels"].astype(np.int32)).mean() >= 0.999
-    assert abs(st.inertia - float(g["inertia"])) / float(g["inertia"]) < 1e-5
+    f = golden("ref_floor.npz")
+    for iters in (20, 100):
+        dC = dev(g["C0"])
+        lab = torch.empty(P.shape[0], dtype=torch.int32, device="cuda")
+        st = M.means_mixed(dP, dC, lab, M.params_init(max_iter=iters))
+        pre = f"c1_{iters}"
+        base = (f[f"{pre}_base_labels"].astype(np.int32), f[f"{pre}_base_C"], float(f[f"{pre}_base_inertia"]))
+        if iters == 20:
+            assert np.array_equal(base[0], g["labels"].astype(np.int32))
+        floors = [parity.end_of_run(P, base, (f[f"{pre}_{v}_labels"].astype(np.int32), f[f"{pre}_{v}_C"],
+                                              float(f[f"{pre}_{v}_inertia"])))
+                  for v in ("colperm0", "colperm1", "colperm2")]
+        ours = parity.end_of_run(P, base, (lab.cpu().numpy(), dC.cpu().numpy(), st.inertia))
+        ok, bar = parity.within_floor(ours, floors)
+        assert ok, (iters, ours, bar, floors)
+        assert ours["inertia_rel"] < 1e-5
 
 
 def test_lloyd_tol_and_fp32_driver(cuda):
@@ -655,6 +671,102 @@ def test_config3_full_size_properties(cuda):
     assert int(counts.sum()) == n
 
 
+def test_exclusion_statistics(cuda):
+    """mpkStats' exclusion attribution (the reference fills it at mpkmeans.cu:655-676):
+    the engine's one test, the certified bound, is reported under condition (3) -- or (6)
+    when only (6) is enabled -- as excluded = tested - (hp_update - rows refined), where
+    hp_update counts every FP32 candidate evaluated (each refined row's incumbent included)
+    and the rows refined per iteration are hist_survivors.  No exact reference entry is
+    computed before excluding, so hp_reference and excl_both stay 0; the FP32 driver and the
+    unrefined scheme test nothing."""
+    n, d, k, iters = 60_000, 32, 40, 5
+    P = O.make_gmm(n, d, k, 5, 2.0, 0.5, 2.0, True)
+    C0 = P[np.sort(O.init_random_idx(n, k, 5))].copy()
+    dP = dev(P)
+    lab = torch.empty(n, dtype=torch.int32, device="cuda")
+    for use3, use6, field, other in ((1, 1, "excl_cond3", "excl_cond6"), (1, 0, "excl_cond3", "excl_cond6"),
+                                     (0, 1, "excl_cond6", "excl_cond3")):
+        st = M.means_mixed(dP, dev(C0), lab, M.params_init(max_iter=iters, use_cond3=use3, use_cond6=use6))
+        rows = sum(st.hist_survivors[:st.n_hist])
+        assert st.n_hist == iters and rows > 0 and st.hp_update >= rows
+        assert st.tested == n * (k - 1) * iters and st.hp_baseline == n * k * iters
+        assert getattr(st, field) == st.tested - (st.hp_update - rows), (use3, use6)
+        assert 0 < getattr(st, field) <= st.tested
+        assert getattr(st, other) == 0 and st.excl_both == 0 and st.hp_reference == 0
+    st = M.means_mixed(dP, dev(C0), lab, M.params_init(max_iter=iters, use_cond3=0, use_cond6=0))
+    assert st.excl_cond3 == st.excl_cond6 == 0 and st.hp_update == 0
+    st = M.means_fp32(dP, dev(C0), lab, M.params_init(max_iter=iters))
+    assert st.tested == 0 and st.excl_cond3 == 0 and st.hp_baseline == n * k * iters
+    st = M.assign(dP, dev(C0), lab)
+    assert st.excl_cond3 == st.tested - (st.hp_update - st.hist_survivors[0])
+
+
+def _ref_fp32():
+    """The reference's own mpkMeansFP32 (oracle/_ref, compiled from its sources), as a
+    callable (P, C0, iters) -> (labels, C, inertia) on numpy arrays."""
+    if not O.REF_LIB_PATH.exists():
+        pytest.skip("oracle/_ref/libmpkref.so not built")
+    r = ctypes.CDLL(str(O.REF_LIB_PATH))
+    VP = ctypes.c_void_p
+    r.mpkMeansFP32.argtypes = [VP, VP, ctypes.c_int, ctypes.c_int, ctypes.c_int, VP, VP,
+                               ctypes.POINTER(M.mpkParams), ctypes.POINTER(M.mpkStats)]
+    r.mpkParamsInit.argtypes = [ctypes.POINTER(M.mpkParams)]
+    blas = torch.cuda.current_blas_handle()
+
+    def run(P, C0, iters):
+        n, d = P.shape
+        k = C0.shape[0]
+        prm = M.mpkParams()
+        r.mpkParamsInit(ctypes.byref(prm))
+        prm.max_iter = iters
+        dP, dC = dev(P), dev(C0)
+        lab = torch.empty(n, dtype=torch.int32, device="cuda")
+        st = M.mpkStats()
+        rc = r.mpkMeansFP32(blas, dP.data_ptr(), n, d, k, dC.data_ptr(), lab.data_ptr(), ctypes.byref(prm),
+                            ctypes.byref(st))
+        torch.cuda.synchronize()
+        assert rc == 0, rc
+        return lab.cpu().numpy(), dC.cpu().numpy(), st.inertia
+    return run
+
+
+def test_config3_vs_reference_library_full_size(cuda):
+    """BASELINE config 3 at full size (n = 1e7, d = 128, k = 1024, 25 iterations)
+    against the reference's own mpkMeansFP32 on the same points and start.
+    (a) Per iteration: on the reference's final centroids the engine's labels agree
+        with the reference's on >= 99.99 % of the rows, every mismatch an FP32
+        near-tie (gap32 < 1e-5) -- the north-star bar.
+    (b) End of run: the reference misses the end-of-run bar against itself -- the same
+        problem with its coordinates permuted (only the FP32 summation order changes)
+        ends 25 iterations later with ~98.8 % of labels and centroids ~4e-3 apart, the
+        run being far from converged -- and the engine is no further from the reference
+        than that (parity.within_floor)."""
+    ref = _ref_fp32()
+    n, d, k, iters = 10_000_000, 128, 1024, 25
+    P = O.make_gmm(n, d, k, 3, 5.0, 0.5, 2.0, True)          # Dirichlet(1) weights, as config 3
+    C0 = P[np.sort(O.init_random_idx(n, k, 3))].copy()
+    base = ref(P, C0, iters)
+    rng = np.random.default_rng(11)
+    floors = []
+    for _ in range(2):
+        q = rng.permutation(d)
+        lab, C, ine = ref(np.ascontiguousarray(P[:, q]), np.ascontiguousarray(C0[:, q]), iters)
+        floors.append(parity.end_of_run(P, base, (lab, np.ascontiguousarray(C[:, np.argsort(q)]), ine)))
+    dP, dC = dev(P), dev(C0)
+    lab = torch.empty(n, dtype=torch.int32, device="cuda")
+    st = M.means_mixed(dP, dC, lab, M.params_init(max_iter=iters))
+    ours = parity.end_of_run(P, base, (lab.cpu().numpy(), dC.cpu().numpy(), st.inertia))
+    ok, bar = parity.within_floor(ours, floors)
+    print("config 3 end of run:", ours, "reference floor:", floors)
+    assert ok, (ours, bar, floors)
+    # (a) one assignment on the reference's final centroids, both sides
+    lab_ref, _, _ = ref(P, base[1], 1)
+    lab_ours, _ = gpu_assign(P, base[1])
+    s = parity.summary(P, base[1], lab_ours, lab_ref)
+    print("config 3 per iteration:", s)
+    assert s["agree"] >= 0.9999 and s["max_gap32"] < 1e-5, s
+
+
 @pytest.mark.parametrize("name", ["ref_config4_sample", "ref_config5_sample"])
 def test_config4_config5_samples_vs_reference(cuda, name):
     """Configs 4 (unit sphere, d = 768, k = 4096) and 5 (offset 1e3, d = 256,
@@ -664,10 +776,16 @@ def test_config4_config5_samples_vs_reference(cuda, name):
     per-iteration check fed the engine's centroids.  Every mismatch must be an
     FP32 near-tie (gap32 < 1e-5); on the cancellation set, where the expanded
     FP32 formula's own error is ~1e-6 of the distances, such ties are common
-    early on (agreement >= 99.5 %, as for the small offset fixture)."""
+    early on: the reference itself agrees with a copy of its own run on permuted
+    coordinates on 99.815 % of this sample at the start, so the bar is that floor."""
     import hashlib
     g = golden(f"{name}.npz")
-    agree = 0.999 if "config4" in name else 0.995
+    # the bar, or the reference's own floor on this sample (its agreement with itself
+    # under permuted coordinates: 100 % on the unit sphere, 99.815 % under the offset)
+    f = golden("ref_floor.npz")
+    tag = "c4s" if "config4" in name else "c5s"
+    floor = min(float((f[f"{tag}_{v}_labels"] == f[f"{tag}_base_labels"]).mean()) for v in ("colperm0", "colperm1"))
+    agree = 1.0 - max(1e-4, 1.25 * (1.0 - floor))
     n, d, k, seed = (int(g[x]) for x in ("n", "d", "k", "seed"))
     P = O.make_sphere(n, d, k, seed) if d == 768 else O.make_offset(n, d, k, seed, 1e3)
     C0 = P[np.sort(O.init_random_idx(n, k, seed))].copy()

@@ -200,6 +200,77 @@ def test_golden_config1():
     assert abs(ine - float(g["inertia"])) / float(g["inertia"]) < 1e-5
 
 
+def _floor_runs(f, prefix, variants):
+    base = (f[f"{prefix}_base_labels"].astype(np.int32), f[f"{prefix}_base_C"], float(f[f"{prefix}_base_inertia"]))
+    runs = {v: (f[f"{prefix}_{v}_labels"].astype(np.int32), f[f"{prefix}_{v}_C"], float(f[f"{prefix}_{v}_inertia"]))
+            for v in variants}
+    return base, runs
+
+
+@pytest.mark.parametrize("iters", [20, 100])
+def test_reference_noise_floor_config1(iters):
+    """The reference against itself (tests/golden/ref_floor.npz, made by its own
+    mpkMeansFP32 on a B200): a repeated call and a row-permuted copy end bit-identical,
+    but permuting the coordinates -- the same points, only every FP32 dot summed in
+    another order -- moves the end of a 20- or 100-iteration run: labels agree on
+    99.7-99.98 %, centroids differ by 3e-4 to 2e-3 (relative Frobenius).  The oracle's
+    run (the engine's arithmetic: its labels and centroids are bit-exact to it on the
+    GPU) lies inside that spread: the north-star end-of-run bar (99.99 %, 1e-5) is
+    below the reference's own noise floor here."""
+    f = golden("ref_floor.npz")
+    P = O.make_config1(100_000, 32, seed=1)
+    C0 = f["c1_C0"]
+    assert np.array_equal(C0, O.kmeanspp(P, 64, seed=1))
+    base, runs = _floor_runs(f, f"c1_{iters}", ("rerun", "rowperm", "colperm0", "colperm1", "colperm2"))
+    for v in ("rerun", "rowperm"):
+        e = parity.end_of_run(P, base, runs[v])
+        assert e["agree"] == 1.0 and e["C_rel"] == 0.0, (v, e)
+    floors = [parity.end_of_run(P, base, runs[v]) for v in ("colperm0", "colperm1", "colperm2")]
+    assert min(fl["agree"] for fl in floors) < 0.9999       # the reference misses the bar against itself
+    lab, C, ine, _ = O.lloyd(P, C0, iters, update_mode=1, frac=O.fixed_frac(float(np.abs(P).max()), len(P)))
+    ours = parity.end_of_run(P, base, (lab, C, ine))
+    ok, bar = parity.within_floor(ours, floors)
+    assert ok, (ours, bar, floors)
+
+
+def test_reference_noise_floor_config3_sample():
+    """Config-3 shape (n = 2e5, d = 128, k = 1024), 3 iterations: the reference with
+    permuted coordinates agrees with itself on 99.965-99.976 % of labels; the oracle
+    (the engine's arithmetic) agrees with the reference inside that spread."""
+    f = golden("ref_floor.npz")
+    P = O.make_gmm(200_000, 128, 1024, 3, 5.0, 0.5, 2.0, True)
+    C0 = P[np.sort(O.init_random_idx(200_000, 1024, 3))].copy()
+    base, runs = _floor_runs(f, "c3s", ("colperm0", "colperm1"))
+    floors = [parity.end_of_run(P, base, runs[v]) for v in runs]
+    lab, C, ine, _ = O.lloyd(P, C0, 3, update_mode=1, frac=O.fixed_frac(float(np.abs(P).max()), len(P)))
+    ours = parity.end_of_run(P, base, (lab, C, ine))
+    ok, bar = parity.within_floor(ours, floors)
+    assert ok, (ours, bar, floors)
+
+
+@pytest.mark.parametrize("tag,maker,k,seed", [
+    ("c4s", lambda: O.make_sphere(30_000, 768, 4096, 41), 4096, 41),
+    ("c5s", lambda: O.make_offset(40_000, 256, 16384, 51, 1e3), 16384, 51)])
+def test_reference_noise_floor_iteration0_configs4_5(tag, maker, k, seed):
+    """One assignment from the random start on the config-4 and config-5 row samples.
+    Unit-sphere rows: the reference agrees with itself under permuted coordinates on every
+    row, and so does the oracle (the bar holds).  Offset-1e3 rows (cancellation stress):
+    the reference agrees with itself on 99.815 % only, every mismatch an FP32 near-tie
+    (gap32 < 1e-5); the oracle agrees with it on 99.855 %, every mismatch a near-tie too."""
+    f = golden("ref_floor.npz")
+    P = maker()
+    C0 = P[np.sort(O.init_random_idx(P.shape[0], k, seed))].copy()
+    base = f[f"{tag}_base_labels"].astype(np.int32)
+    floor_agree = []
+    for v in ("colperm0", "colperm1"):
+        s = parity.summary(P, C0, f[f"{tag}_{v}_labels"].astype(np.int32), base)
+        assert s["max_gap32"] < 1e-5, (v, s)
+        floor_agree.append(s["agree"])
+    s = parity.summary(P, C0, O.assign_fp32(P, C0), base)
+    assert s["max_gap32"] < 1e-5, s
+    assert 1.0 - s["agree"] <= max(1e-4, 1.25 * (1.0 - min(floor_agree))), (s, floor_agree)
+
+
 @pytest.mark.parametrize("name", ["ref_config3_sample.npz", "ref_offset.npz", "ref_sphere.npz"])
 def test_golden_assignment_on_identical_centroids(name):
     g = golden(name)

@@ -52,6 +52,28 @@ def test_no_alloc_update_matches_update_twice(cuda):
         assert torch.equal(C_na[k - 1], C[k - 1])
 
 
+def test_no_alloc_update_allocates_nothing(cuda):
+    """After a first call (which may place the library's fixed array on the device),
+    further calls leave the device's free memory exactly where it was."""
+    n, d, k = 200_000, 64, 256
+    P, C, lab = _problem(n, d, k, 3)
+    lib = M.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    moved = torch.empty(k, dtype=torch.float32, device="cuda")
+
+    def call():
+        assert lib.mpkUpdateNoAlloc(stream, P.data_ptr(), n, d, k, lab.data_ptr(), C.data_ptr(),
+                                    moved.data_ptr()) == M.MPK_OK
+
+    call()
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
+
+
 def test_no_alloc_update_rejects_what_does_not_fit(cuda):
     lib = M.lib()
     P = torch.zeros((16, 8), dtype=torch.float32, device="cuda")
