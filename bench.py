@@ -106,6 +106,8 @@ def parse():
     ap.add_argument("--shift-nonneg", action="store_true",
                     help="P += max|P| before the fit, as the reference's driver does for its conditions "
                          "(mpkShiftNonNegative); a stress variant, not a BASELINE configuration")
+    ap.add_argument("--api", choices=["engine", "mg"], default="engine",
+                    help="mg: one process drives --gpus devices through mpkMeansMixedMG (config 3; not a driver line)")
     ap.add_argument("--no-blocks", action="store_true",
                     help="skip the config-4 / config-5 blocks that follow the config-3 headline")
     ap.add_argument("--block-steps", type=int, default=10, help="timed iterations of each config-4/5 block")
@@ -328,10 +330,10 @@ def run_lloyd(wl, world, rank, local, steps, warmup, n_override=None, e2e=False,
     if world > 1:
         dist.all_reduce(pmax, op=dist.ReduceOp.MAX)
     torch.cuda.synchronize()
-    # one GPU: the engine runs on a side stream, where mpkEngineIterate captures an iteration
-    # as CUDA graphs and replays it; with ranks, the allreduce sits between accumulate and finalize
-    if world == 1:
-        torch.cuda.set_stream(torch.cuda.Stream(dev))
+    # the engine runs on a side stream, where an iteration is captured as CUDA graphs and
+    # replayed: one GPU, mpkEngineIterate; with ranks, mpkEngineStep (assign, refine,
+    # accumulate), then the allreduce of the sums and the finalisation
+    torch.cuda.set_stream(torch.cuda.Stream(dev))
     stream = torch.cuda.current_stream(dev).cuda_stream
     eng = M.Engine(P, K, pmax_global=float(pmax.item()), n_global=n_total, stream=stream)
     labels = torch.empty(n_local, dtype=torch.int32, device=dev)
@@ -342,8 +344,7 @@ def run_lloyd(wl, world, rank, local, steps, warmup, n_override=None, e2e=False,
         if world == 1:
             eng.iterate(C, labels, sums, 1)
             return
-        eng.assign(C, labels)
-        eng.accumulate(labels, sums)
+        eng.step(C, labels, sums)             # assign + refine + accumulate, replayed from CUDA graphs
         if ar is not None:
             ar.append(torch.cuda.Event(enable_timing=True))
             ar[-1].record()
@@ -807,8 +808,77 @@ def traffic_per_launch(wl, n_local):
     return fig * n_local / prof_ref[wl][1] if fig else None
 
 
+def run_mg(args):
+    """mpkMeansMixedMG (the single-process multi-GPU entry point) on config 3: the rows split
+    over --gpus devices of this process, the library's own NCCL communicators.  Two fits
+    from the same start, of W and W + K iterations; the iterations' time is the difference
+    of their t_total_ms (CUDA events around the library's iteration loop on device 0, which
+    the per-iteration allreduce keeps in step with the others) -- engine set-up excluded."""
+    import mpkmeans_b200 as M
+    ng = args.gpus
+    wl = WORKLOADS["config3"]
+    K, D = wl["k"], wl["d"]
+    n_total = args.n if args.n is not None else wl["n"]
+    Ps, labs = [], []
+    r0 = 0
+    for g in range(ng):
+        dev = torch.device("cuda", g)
+        nl = shard_rows(n_total, ng, g)
+        Ps.append(gen_rows("config3", r0, r0 + nl, dev))
+        labs.append(torch.empty(nl, dtype=torch.int32, device=dev))
+        r0 += nl
+    # start centroids: the global rows start_rows names, gathered on the host
+    idx = start_rows(n_total, K)
+    C0 = torch.empty((K, D), dtype=torch.float32)
+    r0 = 0
+    for g in range(ng):
+        nl = Ps[g].shape[0]
+        mine = np.nonzero((idx >= r0) & (idx < r0 + nl))[0]
+        if len(mine):
+            C0[torch.from_numpy(mine)] = Ps[g][torch.from_numpy(idx[mine] - r0).to(Ps[g].device)].cpu()
+        r0 += nl
+    for g in range(ng):
+        torch.cuda.synchronize(g)
+
+    def arr(t, v):
+        return (t * len(v))(*v)
+
+    def fit(iters):
+        Cs = [C0.to(torch.device("cuda", g)) for g in range(ng)]
+        st = M.mpkStats()
+        par = M.params_init(max_iter=iters)
+        rc = M.lib().mpkMeansMixedMG(ng, arr(ctypes.c_int, list(range(ng))),
+                                     arr(ctypes.c_void_p, [x.data_ptr() for x in Ps]),
+                                     arr(ctypes.c_int, [x.shape[0] for x in Ps]), D, K,
+                                     arr(ctypes.c_void_p, [x.data_ptr() for x in Cs]),
+                                     arr(ctypes.c_void_p, [x.data_ptr() for x in labs]),
+                                     ctypes.byref(par), ctypes.byref(st))
+        if rc != 0:
+            raise RuntimeError(f"mpkMeansMixedMG returned {rc}")
+        return st, Cs[0]
+
+    fit(args.warmup)
+    st_a, _ = fit(args.warmup)
+    t0 = time.perf_counter()
+    st_b, Cb = fit(args.warmup + args.steps)
+    wall = time.perf_counter() - t0
+    ms = (st_b.t_total_ms - st_a.t_total_ms) / args.steps
+    sha = hashlib.sha256(Cb.cpu().numpy().tobytes()).hexdigest()[:16]
+    print(json.dumps({
+        "api": "mpkMeansMixedMG", "metric": "Lloyd iterations/s, config 3 (n=1e7, d=128, k=1024, FP32)",
+        "value": 1e3 / ms, "unit": UNIT, "n_gpus": ng, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "fit_ms_total": {"W": st_a.t_total_ms, "W+K": st_b.t_total_ms}, "wall_s_W+K": wall,
+        "centroid_sha": sha, "iterations_before_hash": args.warmup + args.steps,
+        "what": "one process, one host thread over --gpus devices, the library's NCCL allreduce; iterations "
+                "timed as the difference of two fits' event-timed iteration loops (set-up excluded)"}))
+
+
 def main():
     args = parse()
+    if args.api == "mg":
+        run_mg(args)
+        return
     world, rank, local = dist_setup()
     if world != args.gpus and rank == 0:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)

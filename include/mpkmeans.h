@@ -277,10 +277,15 @@ mpkStatus mpkEngineFinalize(mpkEngine e, const long long* dSums, float* dC, floa
 /* iters whole Lloyd iterations of this engine alone -- assign, accumulate,
  * finalize in turn, no collective between -- with exactly their result.  The
  * first call for a given (dC, dAssign, dSums, refine) captures one iteration
- * as two CUDA graphs (assignment; update) and later calls replay them, so
+ * as three CUDA graphs (assignment; refinement; update) and later calls
+ * replay them, so
  * small problems are not held to the host's launch rate.  On the legacy
  * default stream (not capturable) it launches the kernels directly. */
 mpkStatus mpkEngineIterate(mpkEngine e, float* dC, int* dAssign, long long* dSums, int iters, int refine);
+/* One multi-GPU step without the finalisation: Assign (refine as given)
+ * then Accumulate into dSums, replayed from CUDA graphs like Iterate (the
+ * caller then allreduces dSums and calls Finalize).  dC is only read. */
+mpkStatus mpkEngineStep(mpkEngine e, const float* dC, int* dAssign, long long* dSums, int refine);
 /* FP64 inertia of this shard, returned to the host (synchronises) */
 mpkStatus mpkEngineInertia(mpkEngine e, const float* dC, const int* dAssign, double* out);
 int mpkEngineFracBits(mpkEngine e);          /* synchronises once */

@@ -120,6 +120,7 @@ SIGNATURES = {
     "mpkEngineAccumulate": (_I, [_P, _P, _P]),
     "mpkEngineFinalize": (_I, [_P, _P, _P, _P]),
     "mpkEngineIterate": (_I, [_P, _P, _P, _P, _I, _I]),
+    "mpkEngineStep": (_I, [_P, _P, _P, _P, _I]),
     "mpkDebugFailAlloc": (_I, [_I]),
     "mpkDebugMGFailNextWait": (_I, []),
     "mpkEngineInertia": (_I, [_P, _P, _P, ctypes.POINTER(_D)]),
@@ -329,6 +330,11 @@ class Engine:
         finalize), replayed from CUDA graphs after the first call."""
         check("mpkEngineIterate", lib().mpkEngineIterate(self.h, _ptr(C), _ptr(labels), _ptr(sums), int(iters),
                                                          int(bool(refine))))
+
+    def step(self, C, labels, sums, refine: bool = True) -> None:
+        """One multi-GPU step of this shard: assign then accumulate into ``sums`` (no
+        finalisation; allreduce ``sums`` and call finalize), replayed from CUDA graphs."""
+        check("mpkEngineStep", lib().mpkEngineStep(self.h, _ptr(C), _ptr(labels), _ptr(sums), int(bool(refine))))
 
     def inertia(self, C, labels) -> float:
         out = ctypes.c_double()

@@ -224,8 +224,8 @@ extern "C" mpkStatus mpkMeansMixedMG(int ngpu, const int* devices, const float* 
     for (it = 0; it < P.max_iter; ++it) {
         for (int g = 0; g < ngpu; ++g) {
             cudaSetDevice(devices[g]);
-            if ((rc = mpkEngineAssign(eng[g], dC[g], dAssign[g], refine)) != MPK_OK) goto done;
-            if ((rc = mpkEngineAccumulate(eng[g], dAssign[g], sums[g])) != MPK_OK) goto done;
+            /* assign, refine, accumulate: three CUDA graphs replayed per device */
+            if ((rc = mpkEngineStep(eng[g], dC[g], dAssign[g], sums[g], refine)) != MPK_OK) goto done;
         }
         N.groupStart();
         for (int g = 0; g < ngpu; ++g)

@@ -193,15 +193,17 @@ struct mpkEngine_s {
     long long launches = 0;               /* kernels this engine has launched */
     bool prof = false;                    /* bench hook: events around the hot kernels */
     std::vector<cudaEvent_t> ev_assign, ev_refine, ev_accum;
-    /* mpkEngineIterate: one iteration as three graphs (the tensor-core
-     * assignment; its refinement; the update), captured for these buffers and
-     * this refine flag */
+    /* mpkEngineIterate / mpkEngineStep: one iteration as three graphs (the
+     * tensor-core assignment; its refinement; the update -- with the
+     * finalisation for Iterate, without it for Step), captured for these
+     * buffers, this refine flag and that choice */
     struct {
         cudaGraphExec_t assign = nullptr, refine_g = nullptr, update = nullptr;
         const float* C = nullptr;
         const int* A = nullptr;
         const long long* S = nullptr;
         int refine = -1;
+        int finalize = -1;
         long long n_assign = 0, n_refine = 0, n_update = 0;   /* kernels per replay */
         bool failed = false;                    /* a capture failed: launch directly from then on */
     } g;
@@ -216,6 +218,7 @@ static void graphs_release(mpkEngine e) {
     e->g.A = nullptr;
     e->g.S = nullptr;
     e->g.refine = -1;
+    e->g.finalize = -1;
 }
 
 static void prof_mark(mpkEngine e, std::vector<cudaEvent_t>& v) {
@@ -555,18 +558,23 @@ mpkStatus mpkEngineFinalize(mpkEngine e, const long long* dSums, float* dC, floa
     return engine_finalize(e, dSums, dC, dMoved2);
 }
 
-mpkStatus mpkEngineIterate(mpkEngine e, float* dC, int* dAssign, long long* dSums, int iters, int refine) {
-    if (!e || !dC || !dAssign || !dSums || iters < 0 || !e->can_assign) return MPK_ERR_INVALID;
+}  /* extern "C" */
+
+/* iters iterations (finalize) or one step without the finalisation, replayed
+ * from the engine's three graphs where the stream allows */
+static mpkStatus engine_replay(mpkEngine e, float* dC, int* dAssign, long long* dSums, int iters, int refine,
+                               bool finalize) {
     auto assign = [&] { return engine_assign_tc(e, dC, dAssign, refine); };
     auto refine_step = [&] { return engine_refine(e, dC, dAssign, false); };
     auto update = [&] {
         const mpkStatus a = engine_accumulate(e, dAssign, dSums);
-        return a != MPK_OK ? a : engine_finalize(e, dSums, dC, nullptr);
+        return (a != MPK_OK || !finalize) ? a : engine_finalize(e, dSums, dC, nullptr);
     };
     /* graphs need a capturable stream, and no test hook that a replay would freeze */
     const bool graphable = e->s != nullptr && e->s != cudaStreamLegacy && e->s != cudaStreamPerThread &&
                            e->dbg == nullptr && e->stall < 0 && !e->g.failed;
-    bool have = e->g.assign && e->g.C == dC && e->g.A == dAssign && e->g.S == dSums && e->g.refine == refine;
+    bool have = e->g.assign && e->g.C == dC && e->g.A == dAssign && e->g.S == dSums && e->g.refine == refine &&
+                e->g.finalize == (int)finalize;
     if (graphable && !have && iters > 0) {
         graphs_release(e);
         const bool prof = e->prof;
@@ -587,6 +595,7 @@ mpkStatus mpkEngineIterate(mpkEngine e, float* dC, int* dAssign, long long* dSum
             e->g.A = dAssign;
             e->g.S = dSums;
             e->g.refine = refine;
+            e->g.finalize = (int)finalize;
             e->g.n_assign = l1 - l0;
             e->g.n_refine = l2 - l1;
             e->g.n_update = l3 - l2;
@@ -618,6 +627,18 @@ mpkStatus mpkEngineIterate(mpkEngine e, float* dC, int* dAssign, long long* dSum
         }
     }
     return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
+}
+
+extern "C" {
+
+mpkStatus mpkEngineIterate(mpkEngine e, float* dC, int* dAssign, long long* dSums, int iters, int refine) {
+    if (!e || !dC || !dAssign || !dSums || iters < 0 || !e->can_assign) return MPK_ERR_INVALID;
+    return engine_replay(e, dC, dAssign, dSums, iters, refine, true);
+}
+
+mpkStatus mpkEngineStep(mpkEngine e, const float* dC, int* dAssign, long long* dSums, int refine) {
+    if (!e || !dC || (e->n > 0 && !dAssign) || !dSums || !e->can_assign) return MPK_ERR_INVALID;
+    return engine_replay(e, const_cast<float*>(dC), dAssign, dSums, 1, refine, false);
 }
 
 mpkStatus mpkEngineInertia(mpkEngine e, const float* dC, const int* dAssign, double* out) {

@@ -229,7 +229,7 @@ int launch_update_sorted(const float* P, long long n, int d, const int* labels, 
      * rows a warp, so that a small problem does not pay a bin search and a flush of atomics
      * for every handful of rows */
     const int ny = ceil_div(d, vec ? 128 : 32);
-    const long long want = std::max<long long>(1, ((long long)num_sms * 8 + ny - 1) / ny);
+    const long long want = std::max<long long>(1, (long long)num_sms * 8 / ny);   /* whole waves */
     const dim3 grid((unsigned)std::max<long long>(1, std::min<long long>(want, (n + 255) / 256)), (unsigned)ny);
     if (vec) k_segsum<4><<<grid, 256, 0, s>>>(P, d, sc.perm, sc.bin_start, k, prm, sums);
     else k_segsum<1><<<grid, 256, 0, s>>>(P, d, sc.perm, sc.bin_start, k, prm, sums);

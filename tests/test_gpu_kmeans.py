@@ -476,6 +476,40 @@ def test_engine_iterate_graphs_equal_steps(cuda):
     assert torch.equal(C_d, C_a) and torch.equal(lab_d, lab_a)
 
 
+def test_engine_step_graphs_equal_calls(cuda):
+    """mpkEngineStep (the multi-GPU step: assignment, refinement and update
+    replayed from CUDA graphs, no finalisation) followed by Finalize equals
+    Assign + Accumulate + Finalize called in turn, bit for bit, over six
+    iterations on a capturable stream, k = 512 (the wide path is in the graphs);
+    its replays launch the same kernels as the calls."""
+    P, C = make_problem(40000, 48, 512, seed=14)
+    dP = dev(P)
+    pmax = float(max(np.abs(P).max(), np.abs(C).max()))
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        with M.Engine(dP, 512, pmax_global=pmax, stream=side.cuda_stream) as e:
+            lab_a = torch.empty(40000, dtype=torch.int32, device="cuda")
+            sums_a = torch.empty(e.sums_length, dtype=torch.int64, device="cuda")
+            C_a = dev(C)
+            l0 = e.launches()
+            for _ in range(6):
+                e.assign(C_a, lab_a)
+                e.accumulate(lab_a, sums_a)
+                e.finalize(sums_a, C_a)
+            calls = e.launches() - l0
+            lab_b = torch.empty_like(lab_a)
+            sums_b = torch.empty_like(sums_a)
+            C_b = dev(C)
+            l1 = e.launches()
+            for _ in range(6):
+                e.step(C_b, lab_b, sums_b)
+                e.finalize(sums_b, C_b)
+            assert e.launches() - l1 == calls
+            side.synchronize()
+            assert e.counters()["status"] == 0
+    assert torch.equal(C_b, C_a) and torch.equal(lab_b, lab_a) and torch.equal(sums_b, sums_a)
+
+
 def test_tiled_full_scan_bit_exact_shifted_offset(cuda):
     """Cancellation stress with the reference driver's non-negativity shift
     (P += max|P|) and few points per cluster: most wide rows overflow their
