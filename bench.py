@@ -388,10 +388,13 @@ def run_lloyd(wl, world, rank, local, steps, warmup, n_override=None, e2e=False,
     t_ms = ph[0] * steps
     phases = {"assign_ms": ph[1], "refine_ms": ph[2], "update_ms": ph[3], "allreduce_ms": ph[4],
               "other_ms": max(0.0, ph[0] - sum(ph[1:])),
-              "what": ("tensor-core assignment (centroid split + k_assign_tc), refinement (k_refine + wide and "
-                       "full-scan passes), update (sorted fixed-point update" +
-                       (" + finalize, one CUDA graph each" if world == 1 else "; finalize is in other_ms") +
-                       "), allreduce (int64 NCCL allreduce of the sums); max over ranks of each, per step")}
+              "what": ("tensor-core assignment (centroid split + k_assign_tc, one CUDA graph); update (the "
+                       "sorted fixed-point update with the FP32 refinement -- k_refine and the wide and full-scan "
+                       "passes -- on a second stream beside its segmented sum, then the moves of the refined rows" +
+                       (" and the finalisation; one CUDA graph)" if world == 1 else "; one CUDA graph; the "
+                        "finalisation is in other_ms)") +
+                       "; refine_ms is 0 because the refinement is inside update_ms; allreduce (int64 NCCL "
+                       "allreduce of the sums); max over ranks of each, per step")}
     a_ms = prof["assign_ms"] / max(1, prof["assign_launches"])
     u_ms = prof["accum_ms"] / max(1, prof["accum_launches"])
     cnt = eng.counters()
@@ -994,7 +997,8 @@ def main():
                                    "timed steps (with one GPU, the replayed graph of the centroid split and the kernel)"},
             "roofline_update": {"bound": "hbm", "achieved": u["achieved_gbs"], "peak": hbm, "unit": "GB/s",
                                 "frac": u["frac"], "peak_source": f"{peak_src} copy bandwidth",
-                                "kernel": "update: k_label_hist + k_bin_scan + k_label_scatter + k_segsum" +
+                                "kernel": "update: k_label_hist + k_bin_scan + k_label_scatter + k_segsum, with the "
+                                          "refinement beside k_segsum" +
                                           (" (+ memset and k_finalize_fixed: one graph)" if world == 1 else ""),
                                 "work": "n*d*4 + n*4 bytes per update", "avg_launch_ms": u["avg_launch_ms"]},
             "phases": summ["phases"],

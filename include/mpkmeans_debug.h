@@ -48,6 +48,13 @@ mpkStatus mpkDebugClearStatus(mpkEngine e);
  * non-zero: the default.  Both give the same labels. */
 mpkStatus mpkDebugAssignPair(mpkEngine e, int mode);
 
+/* Refinement order.  By default mpkEngineIterate, mpkEngineStep and the Lloyd
+ * drivers (without verify or verbose) run the FP32 refinement on a second
+ * stream beside the update's segmented sum, which sums the assignment's
+ * labels and then moves the refined rows between clusters; mode 0 refines
+ * first and updates after.  Both give the same labels and sums, bit for bit. */
+mpkStatus mpkDebugOverlapRefine(mpkEngine e, int mode);
+
 /* Failure injection on the host: the nth device allocation the library makes
  * from now on (engine scratch, driver buffers) fails once, as if the device
  * were out of memory; 0 disables.  Every entry point must then return

@@ -192,6 +192,7 @@ SIGNATURES = {
     "mpkDebugSetWaitLimit": (_I, [_P, ctypes.c_ulonglong]),
     "mpkDebugInjectStall": (_I, [_P, _I]),
     "mpkDebugAssignPair": (_I, [_P, _I]),
+    "mpkDebugOverlapRefine": (_I, [_P, _I]),
     "mpkDebugClearStatus": (_I, [_P]),
 }
 
@@ -369,6 +370,10 @@ class Engine:
     def assign_pair(self, mode: int) -> None:
         """CTA-pair assignment kernel where it applies (the default); 0: one CTA per row tile."""
         check("mpkDebugAssignPair", lib().mpkDebugAssignPair(self.h, int(mode)))
+
+    def overlap_refine(self, mode: int) -> None:
+        """Refinement beside the update's segmented sum (the default); 0: refine, then update."""
+        check("mpkDebugOverlapRefine", lib().mpkDebugOverlapRefine(self.h, int(mode)))
 
     def clear_status(self) -> None:
         check("mpkDebugClearStatus", lib().mpkDebugClearStatus(self.h))

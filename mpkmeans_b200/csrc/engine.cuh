@@ -144,6 +144,22 @@ struct UpdateScratch {
  * Returns the number of kernels launched. */
 int launch_update_sorted(const float* P, long long n, int d, const int* labels, int k, DevParams* prm,
                           long long* sums, long long* counts, UpdateScratch sc, int num_sms, cudaStream_t s);
+/* The update in two halves: the counting sort of the rows by label (reads
+ * labels; writes perm, bin starts and the counts) and the segmented sum
+ * (reads only the points, perm and bin starts).  Same contract as
+ * launch_update_sorted, which is the two in turn. */
+int launch_update_sort(long long n, const int* labels, int k, DevParams* prm, long long* counts, UpdateScratch sc,
+                       int num_sms, cudaStream_t s);
+int launch_update_sum(const float* P, long long n, int d, int k, DevParams* prm, long long* sums, UpdateScratch sc,
+                      int num_sms, cudaStream_t s);
+/* Overlapping the refinement with the segmented sum: snapshot the listed
+ * rows' labels before the refinement (old, capacity cap entries); after it,
+ * move every row whose label changed between the clusters' sums and counts
+ * (sums: k*d + k int64, the counts after the sums). */
+int launch_refine_snapshot(const RefineEntry* list, const DevParams* prm, const int* labels, int* old, long long cap,
+                           int num_sms, cudaStream_t s);
+int launch_refine_correct(const float* P, int d, const RefineEntry* list, const DevParams* prm, const int* labels,
+                          const int* old, long long cap, int k, long long* sums, int num_sms, cudaStream_t s);
 void launch_finalize_fixed(const long long* sums, const long long* counts, int k, int d,
                            const DevParams* prm, float* C, float* moved2, cudaStream_t s);
 /* FP32 argmin over all k in the refinement's order, checked against labels

@@ -217,6 +217,24 @@ extern "C" mpkStatus mpkMeansMixedMG(int ngpu, const int* devices, const float* 
             goto done;
         }
     }
+    /* NCCL connects its peers at a communicator's first collective: one
+     * allreduce here, waited for, keeps that out of the timed iterations */
+    for (int g = 0; g < ngpu; ++g) {
+        cudaSetDevice(devices[g]);
+        cudaMemsetAsync(sums[g], 0, (size_t)len * sizeof(long long), st[g]);
+    }
+    N.groupStart();
+    for (int g = 0; g < ngpu; ++g)
+        N.allReduce(sums[g], sums[g], (size_t)len, ncclInt64, ncclSum, comm[g], st[g]);
+    {
+        const ncclResult_t r = N.groupEnd();
+        if (r != ncclSuccess) {
+            fprintf(stderr, "mpkMeansMixedMG: ncclAllReduce: %s\n", N.errStr(r));
+            rc = MPK_ERR_CUDA;
+            goto done;
+        }
+    }
+    if ((rc = mg_wait(ngpu, devices, st, comm, N)) != MPK_OK) goto done;
     cudaSetDevice(devices[0]);
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);

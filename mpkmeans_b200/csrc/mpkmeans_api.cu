@@ -189,6 +189,13 @@ struct mpkEngine_s {
     float4* dbg = nullptr;                /* test hook, set by mpkDebugSetAssignTrace */
     int stall = -1;                       /* test hook, set by mpkDebugInjectStall */
     int pair = 1;                         /* CTA-pair assignment kernel (mpkDebugAssignPair) */
+    /* the refinement beside the segmented sum (mpkDebugOverlapRefine): it runs on
+     * s2 between a fork and a join event, with the listed rows' labels before it
+     * in old_lab (n ints) */
+    int overlap = 1;
+    cudaStream_t s2 = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join2 = nullptr;
+    int* old_lab = nullptr;
     int pair_clusters = 0;                /* resident clusters of two for it */
     long long launches = 0;               /* kernels this engine has launched */
     bool prof = false;                    /* bench hook: events around the hot kernels */
@@ -204,6 +211,7 @@ struct mpkEngine_s {
         const long long* S = nullptr;
         int refine = -1;
         int finalize = -1;
+        int overlap = -1;
         long long n_assign = 0, n_refine = 0, n_update = 0;   /* kernels per replay */
         bool failed = false;                    /* a capture failed: launch directly from then on */
     } g;
@@ -219,16 +227,19 @@ static void graphs_release(mpkEngine e) {
     e->g.S = nullptr;
     e->g.refine = -1;
     e->g.finalize = -1;
+    e->g.overlap = -1;
 }
 
-static void prof_mark(mpkEngine e, std::vector<cudaEvent_t>& v) {
+static void prof_mark(mpkEngine e, std::vector<cudaEvent_t>& v, cudaStream_t s) {
     if (!e->prof) return;
     cudaEvent_t ev = nullptr;
     if (cudaEventCreate(&ev) == cudaSuccess) {
-        cudaEventRecord(ev, e->s);
+        cudaEventRecord(ev, s);
         v.push_back(ev);
     }
 }
+
+static void prof_mark(mpkEngine e, std::vector<cudaEvent_t>& v) { prof_mark(e, v, e->s); }
 
 static void prof_clear(mpkEngine e) {
     for (auto x : e->ev_assign) cudaEventDestroy(x);
@@ -244,9 +255,15 @@ static void engine_free(mpkEngine e) {
     prof_clear(e);
     graphs_release(e);
     void* bufs[] = {e->Xs, e->xnorm, e->Cs, e->cn, e->list, e->prm, e->dInertia, e->hist,
-                    e->us.perm, e->us.bin_start, e->us.cursor, e->us.hist,
+                    e->us.perm, e->us.bin_start, e->us.cursor, e->us.hist, e->old_lab,
                     e->wide.Xw, e->wide.went, e->wide.cand, e->wide.ccount, e->wide.scan};
     for (void* b : bufs) dev_free(b, e->s);
+    if (e->ev_fork) cudaEventDestroy(e->ev_fork);
+    if (e->ev_join2) cudaEventDestroy(e->ev_join2);
+    if (e->s2) {
+        cudaStreamSynchronize(e->s2);
+        cudaStreamDestroy(e->s2);
+    }
     delete e;
 }
 
@@ -302,6 +319,7 @@ static mpkStatus engine_create(mpkEngine* out, const float* dP, long long n, int
         ALLOC(e->Cs, (size_t)2 * e->kpad * e->dp * sizeof(__half));
         ALLOC(e->cn, (size_t)e->kpad * sizeof(float));
         ALLOC(e->list, (size_t)(n > 0 ? n : 1) * sizeof(RefineEntry));
+        ALLOC(e->old_lab, (size_t)(n > 0 ? n : 1) * sizeof(int));
         /* the wide path: only when some row could need more than kWideRescan
          * class-rescan columns (16 classes of k/16) */
         if (k > kWideRescan && n > 0) {
@@ -319,6 +337,17 @@ static mpkStatus engine_create(mpkEngine* out, const float* dP, long long n, int
         }
     }
 #undef ALLOC
+    /* the refinement's stream at the highest priority: as the update's blocks
+     * retire, the block scheduler places the latency-bound refinement first */
+    int prio_lo = 0, prio_hi = 0;
+    cudaDeviceGetStreamPriorityRange(&prio_lo, &prio_hi);
+    if (need_assign && (cudaStreamCreateWithPriority(&e->s2, cudaStreamNonBlocking, prio_hi) != cudaSuccess ||
+                        cudaEventCreateWithFlags(&e->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+                        cudaEventCreateWithFlags(&e->ev_join2, cudaEventDisableTiming) != cudaSuccess)) {
+        fprintf(stderr, "mpkmeans_b200: cannot create the engine's second stream\n");
+        engine_free(e);
+        return MPK_ERR_CUDA;
+    }
     cudaMemsetAsync(e->prm, 0, sizeof(DevParams), s);
     cudaMemsetAsync(e->hist, 0, sizeof(unsigned long long) * MPK_MAX_HIST, s);
     if (pmax_global > 0.f) {
@@ -425,12 +454,14 @@ static mpkStatus engine_assign_tc(mpkEngine e, const float* dC, int* dAssign, in
 /* The FP32 refinement of the rows the last engine_assign_tc listed.
  * record_hist: the refinement writes its entry count to the next slot of the
  * engine's survivor history (prm->hist_next counts the slots used). */
-static mpkStatus engine_refine(mpkEngine e, const float* dC, int* dAssign, bool record_hist) {
+static mpkStatus engine_refine(mpkEngine e, const float* dC, int* dAssign, bool record_hist,
+                               cudaStream_t rs = nullptr) {
     if (e->n == 0) return MPK_OK;
-    prof_mark(e, e->ev_refine);
+    if (!rs) rs = e->s;
+    prof_mark(e, e->ev_refine, rs);
     launch_refine(e->P, dC, e->cn, e->d, e->k, assign_bn_for(e->k), e->list, e->prm, dAssign, e->n,
                   record_hist ? e->hist : nullptr, MPK_MAX_HIST, e->Xs, e->n, e->dp,
-                  e->wide, e->num_sms, e->s);
+                  e->wide, e->num_sms, rs);
     ++e->launches;
     /* rows the refinement queued: per round, a tensor-core pass that lists their
      * candidates, then the FP32 evaluation of just those (every launch sizes itself from
@@ -438,7 +469,7 @@ static mpkStatus engine_refine(mpkEngine e, const float* dC, int* dAssign, bool 
     for (int r = 0; r < e->wide.rounds; ++r) {
         const long long base = (long long)r * e->wide.per_round;
         if (r > 0) {
-            launch_wide_gather(e->list, e->Xs, e->n, e->dp, e->wide, base, e->prm, e->num_sms, e->s);
+            launch_wide_gather(e->list, e->Xs, e->n, e->dp, e->wide, base, e->prm, e->num_sms, rs);
             ++e->launches;
         }
         AssignArgs w = assign_args(e, nullptr, 1);
@@ -447,19 +478,19 @@ static mpkStatus engine_refine(mpkEngine e, const float* dC, int* dAssign, bool 
         w.dbg = nullptr;
         w.emit = true;
         w.wbase = base;
-        const cudaError_t err = launch_assign(w, e->s);
+        const cudaError_t err = launch_assign(w, rs);
         if (err != cudaSuccess) {
             fprintf(stderr, "mpkmeans_b200: wide assignment launch failed: %s\n", cudaGetErrorString(err));
             return MPK_ERR_CUDA;
         }
-        launch_refine_wide(e->P, dC, e->cn, e->d, e->k, e->list, e->wide, base, e->prm, dAssign, e->num_sms, e->s);
+        launch_refine_wide(e->P, dC, e->cn, e->d, e->k, e->list, e->wide, base, e->prm, dAssign, e->num_sms, rs);
         e->launches += 2;                 /* the emit pass and the FP32 evaluation */
     }
     if (e->wide.scan) {                   /* rows whose lists overflowed: all k, tiled */
-        launch_full_scan(e->P, dC, e->cn, e->d, e->k, e->wide.scan, e->prm, dAssign, e->num_sms, e->s);
+        launch_full_scan(e->P, dC, e->cn, e->d, e->k, e->wide.scan, e->prm, dAssign, e->num_sms, rs);
         ++e->launches;
     }
-    prof_mark(e, e->ev_refine);
+    prof_mark(e, e->ev_refine, rs);
     return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
 }
 
@@ -482,7 +513,7 @@ static bool capture_graph(cudaStream_t gs, F&& body, cudaGraphExec_t* exec) {
     const mpkStatus st = body();
     const cudaError_t ec = cudaStreamEndCapture(gs, &g);
     const bool ok = st == MPK_OK && ec == cudaSuccess && g != nullptr &&
-                    cudaGraphInstantiate(exec, g, 0) == cudaSuccess;
+                    cudaGraphInstantiate(exec, g, cudaGraphInstantiateFlagUseNodePriority) == cudaSuccess;
     if (g) cudaGraphDestroy(g);
     if (!ok) {
         if (*exec) cudaGraphExecDestroy(*exec);
@@ -505,6 +536,35 @@ static mpkStatus engine_accumulate(mpkEngine e, const int* dAssign, long long* d
 static mpkStatus engine_finalize(mpkEngine e, const long long* dSums, float* dC, float* dMoved2) {
     launch_finalize_fixed(dSums, dSums + (long long)e->k * e->d, e->k, e->d, e->prm, dC, dMoved2, e->s);
     ++e->launches;
+    return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
+}
+
+/* The refinement of the rows the last engine_assign_tc listed and the update,
+ * overlapped (finalize: then the finalisation too, into dMoved2 if given).
+ * The counting sort reads the assignment's labels; then the latency-bound
+ * refinement runs on the second stream beside the bandwidth-bound segmented
+ * sum of those labels: it snapshots the listed rows' labels, refines them,
+ * and moves every row whose label changed from its old cluster's sums and
+ * count to the new one's.  The integer sums come out exactly as an update
+ * of the refined labels would give them. */
+static mpkStatus engine_refine_update(mpkEngine e, float* dC, int* dAssign, long long* dSums, bool record_hist,
+                                      bool finalize, float* dMoved2) {
+    const long long kd = (long long)e->k * e->d;
+    cudaMemsetAsync(dSums, 0, (size_t)(kd + e->k) * sizeof(long long), e->s);
+    prof_mark(e, e->ev_accum);
+    e->launches += launch_update_sort(e->n, dAssign, e->k, e->prm, dSums + kd, e->us, e->num_sms, e->s);
+    cudaEventRecord(e->ev_fork, e->s);
+    cudaStreamWaitEvent(e->s2, e->ev_fork, 0);
+    e->launches += launch_refine_snapshot(e->list, e->prm, dAssign, e->old_lab, e->n, e->num_sms, e->s2);
+    mpkStatus st = engine_refine(e, dC, dAssign, record_hist, e->s2);
+    e->launches += launch_refine_correct(e->P, e->d, e->list, e->prm, dAssign, e->old_lab, e->n, e->k, dSums,
+                                         e->num_sms, e->s2);
+    e->launches += launch_update_sum(e->P, e->n, e->d, e->k, e->prm, dSums, e->us, e->num_sms, e->s);
+    cudaEventRecord(e->ev_join2, e->s2);
+    cudaStreamWaitEvent(e->s, e->ev_join2, 0);       /* always joined, so a capture can end */
+    prof_mark(e, e->ev_accum);
+    if (st == MPK_OK && finalize) st = engine_finalize(e, dSums, dC, dMoved2);
+    if (st != MPK_OK) return st;
     return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
 }
 
@@ -570,11 +630,14 @@ static mpkStatus engine_replay(mpkEngine e, float* dC, int* dAssign, long long* 
         const mpkStatus a = engine_accumulate(e, dAssign, dSums);
         return (a != MPK_OK || !finalize) ? a : engine_finalize(e, dSums, dC, nullptr);
     };
+    /* the refinement beside the update's segmented sum (one graph for both) */
+    const bool ov = e->overlap && refine && e->n > 0;
+    auto refine_update = [&] { return engine_refine_update(e, dC, dAssign, dSums, false, finalize, nullptr); };
     /* graphs need a capturable stream, and no test hook that a replay would freeze */
     const bool graphable = e->s != nullptr && e->s != cudaStreamLegacy && e->s != cudaStreamPerThread &&
                            e->dbg == nullptr && e->stall < 0 && !e->g.failed;
     bool have = e->g.assign && e->g.C == dC && e->g.A == dAssign && e->g.S == dSums && e->g.refine == refine &&
-                e->g.finalize == (int)finalize;
+                e->g.finalize == (int)finalize && e->g.overlap == (int)ov;
     if (graphable && !have && iters > 0) {
         graphs_release(e);
         const bool prof = e->prof;
@@ -584,9 +647,9 @@ static mpkStatus engine_replay(mpkEngine e, float* dC, int* dAssign, long long* 
          * tensor-core pass, the refinement and the update apart */
         bool ok = capture_graph(e->s, assign, &e->g.assign);
         const long long l1 = e->launches;
-        ok = ok && (!refine || capture_graph(e->s, refine_step, &e->g.refine_g));
+        ok = ok && (!refine || ov || capture_graph(e->s, refine_step, &e->g.refine_g));
         const long long l2 = e->launches;
-        ok = ok && capture_graph(e->s, update, &e->g.update);
+        ok = ok && (ov ? capture_graph(e->s, refine_update, &e->g.update) : capture_graph(e->s, update, &e->g.update));
         const long long l3 = e->launches;
         e->prof = prof;
         e->launches = l0;                         /* captured, not yet run */
@@ -596,6 +659,7 @@ static mpkStatus engine_replay(mpkEngine e, float* dC, int* dAssign, long long* 
             e->g.S = dSums;
             e->g.refine = refine;
             e->g.finalize = (int)finalize;
+            e->g.overlap = (int)ov;
             e->g.n_assign = l1 - l0;
             e->g.n_refine = l2 - l1;
             e->g.n_update = l3 - l2;
@@ -621,8 +685,12 @@ static mpkStatus engine_replay(mpkEngine e, float* dC, int* dAssign, long long* 
             e->launches += e->g.n_assign + e->g.n_refine + e->g.n_update;
         } else {
             mpkStatus st = assign();
-            if (st == MPK_OK && refine) st = refine_step();
-            if (st == MPK_OK) st = update();
+            if (st == MPK_OK && ov) {
+                st = refine_update();
+            } else {
+                if (st == MPK_OK && refine) st = refine_step();
+                if (st == MPK_OK) st = update();
+            }
             if (st != MPK_OK) return st;
         }
     }
@@ -751,6 +819,13 @@ mpkStatus mpkDebugAssignPair(mpkEngine e, int mode) {
     if (!e) return MPK_ERR_INVALID;
     e->pair = mode != 0;
     graphs_release(e);                    /* captured iterations name the old kernel */
+    return MPK_OK;
+}
+
+mpkStatus mpkDebugOverlapRefine(mpkEngine e, int mode) {
+    if (!e) return MPK_ERR_INVALID;
+    e->overlap = mode != 0;
+    graphs_release(e);                    /* captured iterations hold the old order */
     return MPK_OK;
 }
 
@@ -894,6 +969,18 @@ static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k
      * per-iteration line the reference prints (mpkmeans.cu:598-603) */
     int* prev_lab = nullptr;
     unsigned long long* dchanged = nullptr;
+    /* Without the per-iteration label checks (verify, verbose), the refinement
+     * runs beside the update's segmented sum (engine_refine_update): the
+     * "assignment" below is then the tensor-core pass alone, and the update
+     * holds the refinement. */
+    const bool ov = refine && e->overlap && !verify && !P.verbose;
+    auto assign_step = [&] { return ov ? engine_assign_tc(e, dC, dAssign, refine)
+                                       : engine_assign(e, dC, dAssign, refine, true); };
+    auto update_step = [&] {
+        if (ov) return engine_refine_update(e, dC, dAssign, sums, true, true, moved2);
+        const mpkStatus a = engine_accumulate(e, dAssign, sums);
+        return a != MPK_OK ? a : engine_finalize(e, sums, dC, moved2);
+    };
     if (dev_alloc((void**)&sums, ((size_t)k * d + k) * sizeof(long long), s) != cudaSuccess ||
         dev_alloc((void**)&moved2, (size_t)k * sizeof(float), s) != cudaSuccess ||
         (verify && dev_alloc((void**)&vbuf, 2 * sizeof(unsigned long long), s) != cudaSuccess) ||
@@ -922,17 +1009,12 @@ static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k
     e->s = gs;
     for (it = 0; it < iters_cap; ++it) {
         cudaEventRecord(ev[4 * it + 0], gs);
-        if (it == 1 && try_graphs) {
-            try_graphs = capture_graph(gs, [&] { return engine_assign(e, dC, dAssign, refine, true); }, &g_assign) &&
-                         capture_graph(gs, [&] {
-                             const mpkStatus a = engine_accumulate(e, dAssign, sums);
-                             return a != MPK_OK ? a : engine_finalize(e, sums, dC, moved2);
-                         }, &g_update);
-        }
+        if (it == 1 && try_graphs)
+            try_graphs = capture_graph(gs, assign_step, &g_assign) && capture_graph(gs, update_step, &g_update);
         const bool replay = it >= 1 && try_graphs;
         if (replay) {
             if (cudaGraphLaunch(g_assign, gs) != cudaSuccess) { st = MPK_ERR_CUDA; goto done; }
-        } else if ((st = engine_assign(e, dC, dAssign, refine, true)) != MPK_OK) {
+        } else if ((st = assign_step()) != MPK_OK) {
             goto done;
         }
         cudaEventRecord(ev[4 * it + 1], gs);
@@ -948,9 +1030,8 @@ static mpkStatus lloyd(cublasHandle_t blas, const float* dP, int n, int d, int k
         }
         if (replay) {
             if (cudaGraphLaunch(g_update, gs) != cudaSuccess) { st = MPK_ERR_CUDA; goto done; }
-        } else {
-            if ((st = engine_accumulate(e, dAssign, sums)) != MPK_OK) goto done;
-            if ((st = engine_finalize(e, sums, dC, moved2)) != MPK_OK) goto done;
+        } else if ((st = update_step()) != MPK_OK) {
+            goto done;
         }
         cudaEventRecord(ev[4 * it + 2], gs);
         S->hp_baseline += (long long)n * k;

@@ -108,6 +108,80 @@ __global__ void k_label_scatter(const int* __restrict__ labels, long long n, int
     }
 }
 
+/* The scatter with coalesced writes (k <= kLocalSortMaxK): each block sorts
+ * its rows by label in chunks of kChunkRows in shared memory (a counting sort:
+ * local histogram, local starts, one global reservation per label and chunk
+ * from the cursors, placement), then writes each label's run of row indices
+ * to its reserved slots in order, so consecutive threads write consecutive
+ * perm entries.  (Scattering row by row writes one isolated 4-byte word per
+ * row.)  Shared memory: 2k ints + kChunkRows (int + short). */
+constexpr int kLocalSortMaxK = 4096;
+constexpr int kChunkRows = 8192;
+constexpr int kScatterThreads = 512;
+
+__global__ void __launch_bounds__(kScatterThreads)
+k_label_scatter_local(const int* __restrict__ labels, long long n, int k, int* __restrict__ cursor,
+                      int* __restrict__ perm, long long rows_per_block) {
+    extern __shared__ int sm[];
+    int* cnt = sm;                                   /* k: counts, then run starts, then run ends */
+    int* gb = sm + k;                                /* k: global slot of each run's first row */
+    int* idx = gb + k;                               /* kChunkRows row indices, sorted by label */
+    unsigned short* lab = reinterpret_cast<unsigned short*>(idx + kChunkRows);
+    __shared__ int part[kScatterThreads / 32];
+    const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+    const long long r0 = min(n, (long long)blockIdx.x * rows_per_block);
+    const long long r1 = min(n, r0 + rows_per_block);
+    const int per = (k + kScatterThreads - 1) / kScatterThreads;
+    const int j0 = min(k, t * per), j1 = min(k, j0 + per);
+    for (long long c0 = r0; c0 < r1; c0 += kChunkRows) {
+        const int m = (int)min((long long)kChunkRows, r1 - c0);
+        for (int j = t; j < k; j += kScatterThreads) cnt[j] = 0;
+        __syncthreads();
+        for (int i = t; i < m; i += kScatterThreads) {
+            const int a = labels[c0 + i];
+            if ((unsigned)a < (unsigned)k) atomicAdd(&cnt[a], 1);
+        }
+        __syncthreads();
+        /* exclusive scan of the counts (thread t owns labels [j0, j1)), and the reservations */
+        int sum = 0;
+        for (int j = j0; j < j1; ++j) sum += cnt[j];
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(FULL, incl, o);
+            if (lane >= o) incl += v;
+        }
+        if (lane == 31) part[w] = incl;
+        __syncthreads();
+        int run = incl - sum;
+        for (int q = 0; q < w; ++q) run += part[q];
+        for (int j = j0; j < j1; ++j) {
+            const int c = cnt[j];
+            cnt[j] = run;
+            gb[j] = c ? atomicAdd(&cursor[j], c) : 0;
+            run += c;
+        }
+        __syncthreads();
+        for (int i = t; i < m; i += kScatterThreads) {
+            const int a = labels[c0 + i];
+            if ((unsigned)a < (unsigned)k) {
+                const int q = atomicAdd(&cnt[a], 1);
+                idx[q] = (int)(c0 + i);
+                lab[q] = (unsigned short)a;
+            }
+        }
+        __syncthreads();
+        /* cnt[j] is now the end of run j, the start of run j + 1 */
+        const int total = cnt[k - 1];
+        for (int q = t; q < total; q += kScatterThreads) {
+            const int a = lab[q];
+            const int st = a ? cnt[a - 1] : 0;
+            perm[gb[a] + (q - st)] = idx[q];
+        }
+        __syncthreads();
+    }
+}
+
 __device__ __forceinline__ long long quantise(float x, float sc) {
     /* x * 2^frac is exact in FP32 (a power-of-two scale that cannot overflow
      * by the choice of frac); the conversion rounds to nearest, ties even. */
@@ -201,12 +275,53 @@ k_segsum(const float* __restrict__ P, int d, const int* __restrict__ perm, const
     flush(bin);
 }
 
+/* The listed rows' labels as the assignment left them (before the refinement
+ * may change them): old[e] = labels[list[e].row], e < nflag. */
+__global__ void k_refine_snapshot(const RefineEntry* __restrict__ list, const DevParams* __restrict__ prm,
+                                  const int* __restrict__ labels, int* __restrict__ old, long long cap) {
+    const long long nf = min((long long)prm->nflag, cap);
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < nf; e += (long long)gridDim.x * blockDim.x)
+        old[e] = labels[list[e].row];
+}
+
+/* After the refinement: every listed row whose label it changed from a to b
+ * moves its fixed-point coordinates from cluster a's sums to b's and one count
+ * with them (one warp per entry).  Integer adds commute, so this may run
+ * beside the segmented sum of the same update, and the result equals an
+ * update from the refined labels exactly. */
+__global__ void k_refine_correct(const float* __restrict__ P, int d, const RefineEntry* __restrict__ list,
+                                 const DevParams* __restrict__ prm, const int* __restrict__ labels,
+                                 const int* __restrict__ old, long long cap, int k, long long* __restrict__ sums) {
+    const long long nf = min((long long)prm->nflag, cap);
+    const int lane = threadIdx.x & 31;
+    const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
+    const float sc = ldexpf(1.0f, prm->frac);
+    long long* counts = sums + (size_t)k * d;
+    for (long long e = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); e < nf; e += nw) {
+        const int row = list[e].row;
+        const int a = old[e], b = labels[row];
+        if (a == b || (unsigned)a >= (unsigned)k || (unsigned)b >= (unsigned)k) continue;   /* warp-uniform */
+        const float* p = P + (size_t)row * d;
+        for (int f = lane; f < d; f += 32) {
+            const long long q = quantise(p[f], sc);
+            if (q) {
+                atomicAdd(reinterpret_cast<unsigned long long*>(&sums[(size_t)b * d + f]), (unsigned long long)q);
+                atomicAdd(reinterpret_cast<unsigned long long*>(&sums[(size_t)a * d + f]), (unsigned long long)(-q));
+            }
+        }
+        if (lane == 0) {
+            atomicAdd(reinterpret_cast<unsigned long long*>(&counts[b]), 1ull);
+            atomicAdd(reinterpret_cast<unsigned long long*>(&counts[a]), ~0ull);   /* -1 */
+        }
+    }
+}
+
 int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
 
 }  /* namespace */
 
-int launch_update_sorted(const float* P, long long n, int d, const int* labels, int k, DevParams* prm,
-                         long long* sums, long long* counts, UpdateScratch sc, int num_sms, cudaStream_t s) {
+int launch_update_sort(long long n, const int* labels, int k, DevParams* prm, long long* counts, UpdateScratch sc,
+                       int num_sms, cudaStream_t s) {
     cudaMemsetAsync(sc.hist, 0, sizeof(int) * (size_t)k, s);
     const bool smem = k <= kSmemHistMax;
     const size_t hb = smem ? sizeof(int) * (size_t)k : 0;
@@ -221,9 +336,23 @@ int launch_update_sorted(const float* P, long long n, int d, const int* labels, 
     }
     k_bin_scan<<<1, 1024, 0, s>>>(sc.hist, k, sc.bin_start, sc.cursor, counts);
     if (n <= 0) return 1;
+    if (k <= kLocalSortMaxK) {
+        const size_t sb = 2 * sizeof(int) * (size_t)k + (size_t)kChunkRows * (sizeof(int) + sizeof(short));
+        if (sb > 48 * 1024) cudaFuncSetAttribute(k_label_scatter_local, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sb);
+        const int sblocks = num_sms * 2;
+        const long long srpb = (n + sblocks - 1) / sblocks;
+        k_label_scatter_local<<<sblocks, kScatterThreads, sb, s>>>(labels, n, k, sc.cursor, sc.perm, srpb);
+        return 3;
+    }
     const long long rpb = (n + blocks - 1) / blocks;
     if (smem) k_label_scatter<true><<<blocks, 512, hb, s>>>(labels, n, k, sc.cursor, sc.perm, rpb);
     else k_label_scatter<false><<<blocks, 512, 0, s>>>(labels, n, k, sc.cursor, sc.perm, rpb);
+    return 3;                             /* hist, scan, scatter */
+}
+
+int launch_update_sum(const float* P, long long n, int d, int k, DevParams* prm, long long* sums, UpdateScratch sc,
+                      int num_sms, cudaStream_t s) {
+    if (n <= 0) return 0;
     const bool vec = (d % 4 == 0) && ((reinterpret_cast<uintptr_t>(P) & 15) == 0);
     /* eight warps a block, about eight blocks per SM over all feature slices; at least 32
      * rows a warp, so that a small problem does not pay a bin search and a flush of atomics
@@ -233,8 +362,25 @@ int launch_update_sorted(const float* P, long long n, int d, const int* labels, 
     const dim3 grid((unsigned)std::max<long long>(1, std::min<long long>(want, (n + 255) / 256)), (unsigned)ny);
     if (vec) k_segsum<4><<<grid, 256, 0, s>>>(P, d, sc.perm, sc.bin_start, k, prm, sums);
     else k_segsum<1><<<grid, 256, 0, s>>>(P, d, sc.perm, sc.bin_start, k, prm, sums);
-    const int seg = 1;
-    return 3 + seg;                       /* hist, scan, scatter, segmented sums */
+    return 1;
+}
+
+int launch_update_sorted(const float* P, long long n, int d, const int* labels, int k, DevParams* prm,
+                         long long* sums, long long* counts, UpdateScratch sc, int num_sms, cudaStream_t s) {
+    const int a = launch_update_sort(n, labels, k, prm, counts, sc, num_sms, s);
+    return a + launch_update_sum(P, n, d, k, prm, sums, sc, num_sms, s);
+}
+
+int launch_refine_snapshot(const RefineEntry* list, const DevParams* prm, const int* labels, int* old, long long cap,
+                           int num_sms, cudaStream_t s) {
+    k_refine_snapshot<<<num_sms * 2, 256, 0, s>>>(list, prm, labels, old, cap);
+    return 1;
+}
+
+int launch_refine_correct(const float* P, int d, const RefineEntry* list, const DevParams* prm, const int* labels,
+                          const int* old, long long cap, int k, long long* sums, int num_sms, cudaStream_t s) {
+    k_refine_correct<<<num_sms * 4, 256, 0, s>>>(P, d, list, prm, labels, old, cap, k, sums);
+    return 1;
 }
 
 }  /* namespace mpk */

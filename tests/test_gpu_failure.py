@@ -111,7 +111,8 @@ def test_allocation_failures_unwind(cuda):
 
 def test_mg_async_error_aborts_and_recovers(cuda):
     """mpkMeansMixedMG never blocks on a device: a (host-injected)
-    asynchronous NCCL error found at its final wait aborts the communicators
+    asynchronous NCCL error found at its next wait on the devices (the one
+    after the communicators' first, warm-up allreduce) aborts the communicators
     and returns MPK_ERR_CUDA; the next call builds new ones and matches the
     single-GPU driver."""
     import ctypes

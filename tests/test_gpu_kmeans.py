@@ -283,7 +283,9 @@ def test_assign_rejects_invalid(cuda):
 # ---------------------------------------------------------------- update ----
 
 @pytest.mark.parametrize("n,d,k", [(1000, 16, 10), (20000, 128, 1024), (3000, 33, 64), (777, 256, 5000),
-                                   (70000, 8, 60000)])  # k past the shared-memory histogram
+                                   (70000, 8, 60000),   # k past the shared-memory histogram
+                                   # several 8192-row chunks per block of the coalesced scatter; its largest k
+                                   (5_000_000, 4, 3000), (400_000, 32, 4096)])
 def test_update_bit_exact(cuda, n, d, k):
     P, C = make_problem(max(n, k), d, k, seed=k)
     P = P[:n] if n >= k else P
@@ -458,7 +460,9 @@ def test_engine_iterate_graphs_equal_steps(cuda):
             l1 = e.launches()
             e.iterate(C_b, lab_b, sums_b, 1)
             e.iterate(C_b, lab_b, sums_b, 5)
-            assert e.launches() - l1 == 6 * per_iter
+            # the replays run the refinement beside the update: two kernels more an
+            # iteration (the snapshot of the listed rows' labels and the moves)
+            assert e.launches() - l1 == 6 * (per_iter + 2)
             C_c = dev(C)
             lab_c = torch.empty_like(lab_a)
             e.iterate(C_c, lab_c, sums_b, 6)
@@ -481,7 +485,7 @@ def test_engine_step_graphs_equal_calls(cuda):
     replayed from CUDA graphs, no finalisation) followed by Finalize equals
     Assign + Accumulate + Finalize called in turn, bit for bit, over six
     iterations on a capturable stream, k = 512 (the wide path is in the graphs);
-    its replays launch the same kernels as the calls."""
+    its replays launch the calls' kernels and the overlap's two."""
     P, C = make_problem(40000, 48, 512, seed=14)
     dP = dev(P)
     pmax = float(max(np.abs(P).max(), np.abs(C).max()))
@@ -504,10 +508,59 @@ def test_engine_step_graphs_equal_calls(cuda):
             for _ in range(6):
                 e.step(C_b, lab_b, sums_b)
                 e.finalize(sums_b, C_b)
-            assert e.launches() - l1 == calls
+            assert e.launches() - l1 == calls + 6 * 2     # + snapshot and moves (refinement beside the update)
             side.synchronize()
             assert e.counters()["status"] == 0
     assert torch.equal(C_b, C_a) and torch.equal(lab_b, lab_a) and torch.equal(sums_b, sums_a)
+
+
+@pytest.mark.parametrize("kind", ["gaussian", "offset"])
+def test_refine_overlap_equals_sequential(cuda, kind):
+    """The refinement on a second stream beside the update's segmented sum (the
+    update sums the assignment's labels, then the rows the refinement moved
+    change clusters) equals refining first and updating after, bit for bit:
+    labels, int64 sums and centroids after six iterations, through
+    mpkEngineIterate (graphs), mpkEngineStep (graphs) and direct launches on
+    the legacy default stream.  "offset" is the cancellation geometry (k = 4096,
+    offset 1e3): most listed rows change label and many take the wide path."""
+    rng = np.random.default_rng(21)
+    if kind == "gaussian":
+        P, C = make_problem(50000, 64, 600, seed=22)
+        k = 600
+    else:
+        n, d, k = 40000, 64, 4096
+        o = rng.standard_normal(d)
+        o = o / np.linalg.norm(o) * 1e3
+        means = o + 2.0 * rng.standard_normal((k, d))
+        P = (means[rng.integers(0, k, n)] + rng.standard_normal((n, d))).astype(np.float32)
+        C = P[np.sort(rng.choice(n, size=k, replace=False))].copy()
+    n = P.shape[0]
+    dP = dev(P)
+    pmax = float(max(np.abs(P).max(), np.abs(C).max()))
+    side = torch.cuda.Stream()
+    out = {}
+    for mode in (0, 1):
+        for api in ("iterate", "step", "legacy"):
+            stream = side if api != "legacy" else torch.cuda.default_stream()
+            with torch.cuda.stream(stream):
+                with M.Engine(dP, k, pmax_global=pmax, stream=side.cuda_stream if api != "legacy" else None) as e:
+                    e.overlap_refine(mode)
+                    lab = torch.empty(n, dtype=torch.int32, device="cuda")
+                    sums = torch.empty(e.sums_length, dtype=torch.int64, device="cuda")
+                    Cd = dev(C)
+                    for _ in range(6):
+                        if api == "step":
+                            e.step(Cd, lab, sums)
+                            e.finalize(sums, Cd)
+                        else:
+                            e.iterate(Cd, lab, sums, 1)
+                    stream.synchronize()
+                    assert e.counters()["status"] == 0
+            out[(mode, api)] = (lab.cpu(), sums.cpu(), Cd.cpu())
+    ref = out[(0, "iterate")]
+    for key, got in out.items():
+        for a, b in zip(got, ref):
+            assert torch.equal(a, b), key
 
 
 def test_tiled_full_scan_bit_exact_shifted_offset(cuda):
