@@ -106,6 +106,9 @@ def parse():
     ap.add_argument("--shift-nonneg", action="store_true",
                     help="P += max|P| before the fit, as the reference's driver does for its conditions "
                          "(mpkShiftNonNegative); a stress variant, not a BASELINE configuration")
+    ap.add_argument("--combine", choices=["peer", "nccl"], default="peer",
+                    help="N > 1: how the ranks' sums are combined: the fused peer-memory combine and finalisation "
+                         "(mpkPeerCombine) or an NCCL allreduce then mpkEngineFinalize")
     ap.add_argument("--api", choices=["engine", "mg"], default="engine",
                     help="mg: one process drives --gpus devices through mpkMeansMixedMG (config 3; not a driver line)")
     ap.add_argument("--no-blocks", action="store_true",
@@ -305,8 +308,31 @@ def label_check(P, C, labels, seconds, threads):
     return {"rows": m, "match": int((got == want).sum())}
 
 
+def peer_group(M, world, rank, K, D):
+    """This rank's exchange block for the fused combine over NVLink peer memory, connected to
+    every other rank's through CUDA IPC handles; None on every rank (the NCCL allreduce is
+    used instead) if any rank could not open a peer's block."""
+    g = None
+    try:
+        g = M.PeerGroup(rank, world, K, D)
+        hs = [None] * world
+        dist.all_gather_object(hs, g.handle())
+        g.connect_handles(hs)
+        ok = 1
+    except Exception as exc:                      # noqa: BLE001 - reported, then the NCCL path runs
+        print(f"rank {rank}: peer combine unavailable ({exc}); NCCL allreduce instead", file=sys.stderr)
+        ok = 0
+    flag = torch.tensor([ok], dtype=torch.int32, device="cuda")
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    if int(flag.item()) == 0:
+        if g is not None:
+            g.close()
+        return None
+    return g
+
+
 def run_lloyd(wl, world, rank, local, steps, warmup, n_override=None, e2e=False, cpu=False,
-              shift_nonneg=False, check_s=3.0):
+              shift_nonneg=False, check_s=3.0, combine="peer"):
     """One workload on this rank: generate its rows, time `steps` Lloyd iterations after
     `warmup` untimed ones, then check and (optionally) measure e2e and the CPU baseline."""
     import mpkmeans_b200 as M
@@ -339,20 +365,26 @@ def run_lloyd(wl, world, rank, local, steps, warmup, n_override=None, e2e=False,
     labels = torch.empty(n_local, dtype=torch.int32, device=dev)
     sums = torch.empty(eng.sums_length, dtype=torch.int64, device=dev)
     C = C0.clone()
+    grp = peer_group(M, world, rank, K, D) if (world > 1 and combine == "peer") else None
 
     def step(ar=None):
         if world == 1:
             eng.iterate(C, labels, sums, 1)
             return
-        eng.step(C, labels, sums)             # assign + refine + accumulate, replayed from CUDA graphs
+        # assign + refine + accumulate, replayed from CUDA graphs
+        eng.step(C, labels, grp.sums if grp is not None else sums)
         if ar is not None:
             ar.append(torch.cuda.Event(enable_timing=True))
             ar[-1].record()
-        dist.all_reduce(sums)
+        if grp is not None:
+            grp.combine(eng, C)               # the ranks' sums combined and finalised over peer memory
+        else:
+            dist.all_reduce(sums)
         if ar is not None:
             ar.append(torch.cuda.Event(enable_timing=True))
             ar[-1].record()
-        eng.finalize(sums, C)
+        if grp is None:
+            eng.finalize(sums, C)
 
     for _ in range(warmup):
         step()
@@ -391,12 +423,24 @@ def run_lloyd(wl, world, rank, local, steps, warmup, n_override=None, e2e=False,
               "what": ("tensor-core assignment (centroid split + k_assign_tc, one CUDA graph); update (the "
                        "sorted fixed-point update with the FP32 refinement -- k_refine and the wide and full-scan "
                        "passes -- on a second stream beside its segmented sum, then the moves of the refined rows" +
-                       (" and the finalisation; one CUDA graph)" if world == 1 else "; one CUDA graph; the "
-                        "finalisation is in other_ms)") +
-                       "; refine_ms is 0 because the refinement is inside update_ms; allreduce (int64 NCCL "
-                       "allreduce of the sums); max over ranks of each, per step")}
+                       (" and the finalisation; one CUDA graph)" if world == 1 else "; one CUDA graph)") +
+                       "; refine_ms is 0 because the refinement is inside update_ms; allreduce_ms: combining the "
+                       "ranks' int64 sums -- with the peer-memory combine this is the whole fused combine and "
+                       "finalisation (waiting for the slowest rank included), with NCCL the allreduce alone and "
+                       "the finalisation in other_ms; max over ranks of each, per step")}
     a_ms = prof["assign_ms"] / max(1, prof["assign_launches"])
-    u_ms = prof["accum_ms"] / max(1, prof["accum_launches"])
+    window_ms = prof["accum_ms"] / max(1, prof["accum_launches"])
+    # the update kernels alone (the timed window above also holds the refinement beside them):
+    # Accumulate on the final labels, CUDA events on the engine's stream, after the timed steps
+    for _ in range(2):
+        eng.accumulate(labels, sums)
+    u0, u1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    u0.record()
+    for _ in range(5):
+        eng.accumulate(labels, sums)
+    u1.record()
+    torch.cuda.synchronize()
+    u_ms = u0.elapsed_time(u1) / 5
     cnt = eng.counters()
     sha = hashlib.sha256(C.cpu().numpy().tobytes()).hexdigest()[:16]
 
@@ -415,17 +459,21 @@ def run_lloyd(wl, world, rank, local, steps, warmup, n_override=None, e2e=False,
     agg = agg.tolist()
 
     res = {"wl": wl, "t_ms": t_ms, "steps": steps, "warmup": warmup, "phases": phases, "a_ms": a_ms, "u_ms": u_ms,
+           "window_ms": window_ms,
            "clk": clk, "counters": cnt, "n_local": n_local, "n_total": n_total, "launches": launches, "K": K, "D": D,
            "label_check": {"rows": agg[0], "match_pct": 100.0 * agg[1] / max(1, agg[0]), "mismatches": agg[2],
                            "what": "each rank's labels on a random row sample of its shard against the CPU "
                                    "oracle's FP32 argmin on the final centroids, summed over ranks"},
            "centroid_sha": sha, "centroid_sha_ranks_equal": len(set(shas)) == 1,
            "iterations_before_hash": warmup + steps}
-    res["e2e"] = run_e2e(M, P, C0, world, rank, dev, n_total, iters=WORKLOADS[wl]["iters"]) if e2e else None
+    res["combine"] = None if world == 1 else ("peer memory (mpkPeerCombine)" if grp is not None else "NCCL allreduce")
+    res["e2e"] = run_e2e(M, P, C0, world, rank, dev, n_total, iters=WORKLOADS[wl]["iters"], grp=grp) if e2e else None
     res["cpu"] = cpu_baseline(P, C_chk, labels) if (cpu and rank == 0 and world == 1) else None
     if cnt["status"] != 0:
         raise RuntimeError(f"engine device status {cnt['status']}")
     eng.close()
+    if grp is not None:
+        grp.close()
     torch.cuda.synchronize()
     torch.cuda.set_stream(torch.cuda.default_stream(dev))
     del P, labels, sums, C, C0, C_chk
@@ -434,7 +482,7 @@ def run_lloyd(wl, world, rank, local, steps, warmup, n_override=None, e2e=False,
     return res
 
 
-def run_e2e(M, P, C0, world, rank, dev, n_total, steps=2, iters=E2E_ITERS):
+def run_e2e(M, P, C0, world, rank, dev, n_total, steps=2, iters=E2E_ITERS, grp=None):
     """Public API from pinned host buffers: H2D of the points and start
     centroids, the fit (the configuration's iteration count), D2H of labels
     and centroids."""
@@ -462,10 +510,13 @@ def run_e2e(M, P, C0, world, rank, dev, n_total, steps=2, iters=E2E_ITERS):
             with M.Engine(dP, C0.shape[0], pmax_global=float(pmax.item()), n_global=n_total, stream=stream) as e:
                 s = torch.empty(e.sums_length, dtype=torch.int64, device=dev)
                 for _ in range(iters):
-                    e.assign(dC, lab)
-                    e.accumulate(lab, s)
-                    dist.all_reduce(s)
-                    e.finalize(s, dC)
+                    if grp is not None:
+                        e.step(dC, lab, grp.sums)
+                        grp.combine(e, dC)
+                    else:
+                        e.step(dC, lab, s)
+                        dist.all_reduce(s)
+                        e.finalize(s, dC)
         marks[2].record()
         hL.copy_(lab, non_blocking=True)
         hC.copy_(dC, non_blocking=True)
@@ -490,7 +541,9 @@ def run_e2e(M, P, C0, world, rank, dev, n_total, steps=2, iters=E2E_ITERS):
     return {"value": iters * steps / (t / 1e3), "unit": UNIT, "last_step_ms": brk,
             "h2d_bytes_per_step": int(P.numel() * 4 + C0.numel() * 4),
             "d2h_bytes_per_step": int(P.shape[0] * 4 + C0.numel() * 4),
-            "iters_per_step": iters, "api": "mpkMeansMixed" if world == 1 else "mpkEngine* + NCCL allreduce"}
+            "iters_per_step": iters,
+            "api": "mpkMeansMixed" if world == 1 else ("mpkEngineStep + mpkPeerCombine" if grp is not None
+                                                         else "mpkEngineStep + NCCL allreduce + mpkEngineFinalize")}
 
 
 def cpu_baseline(P, C_chk, labels):
@@ -545,8 +598,12 @@ def lloyd_summary(r, hbm, bf16):
         "assign": {"achieved_tflops": achieved, "peak_tflops": peak, "frac": achieved / peak,
                    "peak_source": "measured burst bf16 (MEASURED_PEAKS.json bf16_tflops)",
                    "sm_mhz_median": r["clk"].get("sm_mhz"), "avg_launch_ms": r["a_ms"]},
-        "update": {"achieved_gbs": u_gbs, "peak_gbs": hbm, "frac": u_gbs / hbm, "avg_launch_ms": r["u_ms"]},
-        "phases": r["phases"], "label_check": r["label_check"], "centroid_sha": r["centroid_sha"],
+        "update": {"achieved_gbs": u_gbs, "peak_gbs": hbm, "frac": u_gbs / hbm, "avg_launch_ms": r["u_ms"],
+                   "timing": "the update kernels alone (sort + segmented sum, no refinement), five calls on the "
+                             "final labels after the timed steps, CUDA events on the engine's stream",
+                   "overlapped_window_ms": r["window_ms"]},
+        "phases": r["phases"], "combine": r["combine"], "label_check": r["label_check"],
+        "centroid_sha": r["centroid_sha"],
         "centroid_sha_ranks_equal": r["centroid_sha_ranks_equal"],
         "iterations_before_hash": r["iterations_before_hash"],
         "refined_rows_per_iter": r["counters"]["rows_refined"] / nit,
@@ -970,7 +1027,7 @@ def main():
         return
 
     r = run_lloyd(args.workload, world, rank, local, args.steps, args.warmup, n_override=args.n,
-                  e2e=not args.no_e2e, cpu=not args.no_cpu, shift_nonneg=args.shift_nonneg)
+                  e2e=not args.no_e2e, cpu=not args.no_cpu, shift_nonneg=args.shift_nonneg, combine=args.combine)
     # configs 5 (every N) and 4 (N = 1 and 8) after the config-3 headline, an eighth of their
     # rows per GPU: at N = 8 each is the whole configuration
     blocks = {}
@@ -978,7 +1035,7 @@ def main():
         for bw in ("config5", "config4"):
             if bw == "config4" and world not in (1, 8):
                 continue
-            blocks[bw] = run_lloyd(bw, world, rank, local, args.block_steps, args.block_warmup)
+            blocks[bw] = run_lloyd(bw, world, rank, local, args.block_steps, args.block_warmup, combine=args.combine)
     if rank == 0:
         value, summ = lloyd_summary(r, hbm, bf16)
         a, u = summ["assign"], summ["update"]
@@ -997,11 +1054,10 @@ def main():
                                    "timed steps (with one GPU, the replayed graph of the centroid split and the kernel)"},
             "roofline_update": {"bound": "hbm", "achieved": u["achieved_gbs"], "peak": hbm, "unit": "GB/s",
                                 "frac": u["frac"], "peak_source": f"{peak_src} copy bandwidth",
-                                "kernel": "update: k_label_hist + k_bin_scan + k_label_scatter + k_segsum, with the "
-                                          "refinement beside k_segsum" +
-                                          (" (+ memset and k_finalize_fixed: one graph)" if world == 1 else ""),
-                                "work": "n*d*4 + n*4 bytes per update", "avg_launch_ms": u["avg_launch_ms"]},
-            "phases": summ["phases"],
+                                "kernel": "update: memset + k_label_hist + k_bin_scan + k_label_scatter_local (k_label_scatter when k > 4096) + k_segsum",
+                                "work": "n*d*4 + n*4 bytes per update", "avg_launch_ms": u["avg_launch_ms"],
+                                "timing": u["timing"], "overlapped_window_ms": u["overlapped_window_ms"]},
+            "phases": summ["phases"], "combine": summ["combine"],
             "gpu_launches": r["launches"],
             "label_check": summ["label_check"], "label_match_pct": summ["label_check"]["match_pct"],
             "centroid_sha": summ["centroid_sha"], "centroid_sha_ranks_equal": summ["centroid_sha_ranks_equal"],

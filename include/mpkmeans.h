@@ -295,6 +295,30 @@ mpkStatus mpkEngineCounters(mpkEngine e, long long* rows_refined, long long* can
                             long long* rows_full_scan, int* status);
 long long mpkEngineSumsLength(mpkEngine e);  /* k*d + k */
 
+/* ---- Combining the ranks' sums over NVLink peer memory (no reference
+ * counterpart: the reference has no multi-GPU path) ----
+ * One group per rank (GPU), each with an exchange block in its device memory.
+ * Per iteration every rank runs mpkEngineStep into mpkPeerSums(g) and then
+ * mpkPeerCombine, which replaces the allreduce of the sums and
+ * mpkEngineFinalize: each rank finalises its 1/world slice of the clusters
+ * from every rank's sums, read over NVLink, and then copies the other ranks'
+ * finalised slices; the result equals allreduce + Finalize bit for bit.
+ * Set-up: mpkPeerCreate on each rank's device; either export every block as
+ * an IPC handle (mpkPeerExportHandle, 64 bytes) and pass all handles to
+ * mpkPeerConnect (ranks in different processes), or pass the blocks' addresses
+ * (mpkPeerLocalBase) and devices (ranks of one process).  Every rank must call
+ * mpkPeerCombine once per iteration: its waits on the other ranks are bounded
+ * (4 s) and set the engine's device status on expiry. */
+typedef struct mpkPeerGroup_s* mpkPeerGroup;
+mpkStatus mpkPeerCreate(mpkPeerGroup* out, int rank, int world, int k, int d);
+mpkStatus mpkPeerExportHandle(mpkPeerGroup g, void* handle64);
+mpkStatus mpkPeerLocalBase(mpkPeerGroup g, void** base);
+/* handles64[p] (or bases[p] with devices[p]) for every rank p but this one */
+mpkStatus mpkPeerConnect(mpkPeerGroup g, const void* const* handles64, void* const* bases, const int* devices);
+long long* mpkPeerSums(mpkPeerGroup g);      /* this rank's k*d + k sums buffer */
+mpkStatus mpkPeerCombine(mpkPeerGroup g, mpkEngine e, float* dC, float* dMoved2);
+mpkStatus mpkPeerDestroy(mpkPeerGroup g);
+
 #ifdef __cplusplus
 }
 #endif

@@ -121,6 +121,13 @@ SIGNATURES = {
     "mpkEngineFinalize": (_I, [_P, _P, _P, _P]),
     "mpkEngineIterate": (_I, [_P, _P, _P, _P, _I, _I]),
     "mpkEngineStep": (_I, [_P, _P, _P, _P, _I]),
+    "mpkPeerCreate": (_I, [ctypes.POINTER(_P), _I, _I, _I, _I]),
+    "mpkPeerExportHandle": (_I, [_P, _P]),
+    "mpkPeerLocalBase": (_I, [_P, ctypes.POINTER(_P)]),
+    "mpkPeerConnect": (_I, [_P, _P, _P, _P]),
+    "mpkPeerSums": (_P, [_P]),
+    "mpkPeerCombine": (_I, [_P, _P, _P, _P]),
+    "mpkPeerDestroy": (_I, [_P]),
     "mpkDebugFailAlloc": (_I, [_I]),
     "mpkDebugMGFailNextWait": (_I, []),
     "mpkEngineInertia": (_I, [_P, _P, _P, ctypes.POINTER(_D)]),
@@ -295,6 +302,52 @@ def update(P, labels, C, moved2=None, blas: int | None = None) -> None:
     n, d = P.shape
     k = C.shape[0]
     check("mpkUpdate", lib().mpkUpdate(blas, _ptr(P), n, d, k, _ptr(labels), _ptr(C), _ptr(moved2)))
+
+
+class PeerGroup:
+    """One rank's exchange block for combining the ranks' sums over NVLink peer memory
+    (mpkPeer*), created on the current device.  Per iteration: Engine.step into
+    ``sums`` (an int device address), then ``combine`` instead of an allreduce and
+    Engine.finalize.  Ranks of one process connect by addresses and devices
+    (``connect_local``); ranks of different processes by exported IPC handles
+    (``handle`` and ``connect_handles``)."""
+
+    def __init__(self, rank: int, world: int, k: int, d: int):
+        h = _P()
+        check("mpkPeerCreate", lib().mpkPeerCreate(ctypes.byref(h), int(rank), int(world), int(k), int(d)))
+        self.h = h
+        self.rank, self.world = int(rank), int(world)
+        self.sums = int(lib().mpkPeerSums(self.h))
+
+    def handle(self) -> bytes:
+        buf = ctypes.create_string_buffer(64)
+        check("mpkPeerExportHandle", lib().mpkPeerExportHandle(self.h, buf))
+        return buf.raw
+
+    def base(self) -> int:
+        b = _P()
+        check("mpkPeerLocalBase", lib().mpkPeerLocalBase(self.h, ctypes.byref(b)))
+        return int(b.value)
+
+    def connect_handles(self, handles: list) -> None:
+        bufs = [ctypes.create_string_buffer(bytes(h), 64) if (i != self.rank and h is not None) else None
+                for i, h in enumerate(handles)]
+        arr = (_P * self.world)(*[ctypes.cast(b, _P) if b is not None else None for b in bufs])
+        check("mpkPeerConnect", lib().mpkPeerConnect(self.h, arr, None, None))
+        self._keep = bufs
+
+    def connect_local(self, bases: list, devices: list) -> None:
+        arr = (_P * self.world)(*bases)
+        dev = (_I * self.world)(*devices)
+        check("mpkPeerConnect", lib().mpkPeerConnect(self.h, None, arr, dev))
+
+    def combine(self, engine, C, moved2=None) -> None:
+        check("mpkPeerCombine", lib().mpkPeerCombine(self.h, engine.h, _ptr(C), _ptr(moved2)))
+
+    def close(self) -> None:
+        if self.h:
+            lib().mpkPeerDestroy(self.h)
+            self.h = None
 
 
 class Engine:

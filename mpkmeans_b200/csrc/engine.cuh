@@ -176,6 +176,19 @@ void launch_count_diff(const int* a, const int* b, long long n, unsigned long lo
 void launch_add_const(float* p, long long count, float c, cudaStream_t s);
 void launch_standardize(float* P, int n, int d, cudaStream_t s);
 
+/* ---- combining the ranks' sums over peer memory (peer.cu) ---- */
+constexpr int kPeerMax = 64;                     /* ranks a group can hold */
+struct PeerBases {
+    void* p[kPeerMax];                           /* every rank's exchange block, as this GPU addresses it */
+};
+size_t peer_block_bytes(int k, int d);
+size_t peer_sums_offset();
+/* The fused combine + finalisation of one iteration on this rank (one launch):
+ * C (k x d, this rank's centroids) and moved2 (k, optional) become the
+ * finalised values of the sums of every rank's exchange block. */
+cudaError_t launch_peer_combine(const PeerBases& bases, int rank, int world, int k, int d, const DevParams* prm,
+                                int* status, float* C, float* moved2, int num_sms, cudaStream_t s);
+
 /* ---- device memory (mpkmeans_api.cu) ----
  * Engine scratch comes from one stream-ordered memory pool per device whose
  * release threshold keeps freed blocks cached, so a second fit of the same

@@ -104,6 +104,12 @@ int current_sm_count(int* dev_out, int* cc_major) {
 
 namespace mpk {
 
+/* peer.cu: the group behind mpkPeerCombine */
+bool peer_ready(mpkPeerGroup g, int k, int d);
+const PeerBases& peer_bases(mpkPeerGroup g);
+int peer_rank(mpkPeerGroup g);
+int peer_world(mpkPeerGroup g);
+
 static cudaMemPool_t engine_pool(int dev) {
     static std::mutex m;
     static cudaMemPool_t pools[64] = {};
@@ -707,6 +713,14 @@ mpkStatus mpkEngineIterate(mpkEngine e, float* dC, int* dAssign, long long* dSum
 mpkStatus mpkEngineStep(mpkEngine e, const float* dC, int* dAssign, long long* dSums, int refine) {
     if (!e || !dC || (e->n > 0 && !dAssign) || !dSums || !e->can_assign) return MPK_ERR_INVALID;
     return engine_replay(e, const_cast<float*>(dC), dAssign, dSums, 1, refine, false);
+}
+
+mpkStatus mpkPeerCombine(mpkPeerGroup g, mpkEngine e, float* dC, float* dMoved2) {
+    if (!e || !dC || !mpk::peer_ready(g, e->k, e->d)) return MPK_ERR_INVALID;
+    const cudaError_t err = launch_peer_combine(mpk::peer_bases(g), mpk::peer_rank(g), mpk::peer_world(g), e->k,
+                                                e->d, e->prm, &e->prm->status, dC, dMoved2, e->num_sms, e->s);
+    ++e->launches;
+    return err == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
 }
 
 mpkStatus mpkEngineInertia(mpkEngine e, const float* dC, const int* dAssign, double* out) {
