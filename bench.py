@@ -106,7 +106,7 @@ def parse():
     ap.add_argument("--shift-nonneg", action="store_true",
                     help="P += max|P| before the fit, as the reference's driver does for its conditions "
                          "(mpkShiftNonNegative); a stress variant, not a BASELINE configuration")
-    ap.add_argument("--combine", choices=["peer", "nccl"], default="peer",
+    ap.add_argument("--combine", choices=["peer", "nccl"], default="nccl",
                     help="N > 1: how the ranks' sums are combined: the fused peer-memory combine and finalisation "
                          "(mpkPeerCombine) or an NCCL allreduce then mpkEngineFinalize")
     ap.add_argument("--api", choices=["engine", "mg"], default="engine",
@@ -332,7 +332,7 @@ def peer_group(M, world, rank, K, D):
 
 
 def run_lloyd(wl, world, rank, local, steps, warmup, n_override=None, e2e=False, cpu=False,
-              shift_nonneg=False, check_s=3.0, combine="peer"):
+              shift_nonneg=False, check_s=3.0, combine="nccl"):
     """One workload on this rank: generate its rows, time `steps` Lloyd iterations after
     `warmup` untimed ones, then check and (optionally) measure e2e and the CPU baseline."""
     import mpkmeans_b200 as M

@@ -50,28 +50,59 @@ __host__ __device__ inline size_t off_x(int k, int d) { return kOffS + align256(
 __host__ __device__ inline size_t off_m(int k, int d) { return off_x(k, d) + align256((size_t)k * d * sizeof(float)); }
 __host__ __device__ inline size_t block_bytes(int k, int d) { return off_m(k, d) + align256((size_t)k * sizeof(float)); }
 
-__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
+/* Flags are stored and polled with relaxed system-scope accesses; the one
+ * __threadfence_system() before a rank's stores (release) and the one after its
+ * wait (acquire) order the data around them. */
+__device__ __forceinline__ void st_relaxed_sys(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long* p) {
     unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 
-/* Thread 0: every rank's flag `which` at or past ep, within the time limit. */
+/* Release: this thread's (and, cumulatively, its block's) earlier writes, then
+ * flag `slot` of every rank's block set to ep. */
+__device__ __forceinline__ void announce(const PeerBases& bases, int world, int slot, unsigned long long ep) {
+    __threadfence_system();
+    for (int p = 0; p < world; ++p)
+        st_relaxed_sys(reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(bases.p[p]) + kOffFlags) + slot,
+                       ep);
+}
+
+/* Thread 0: every rank's flag at or past ep, within the time limit; then acquire. */
 __device__ bool wait_flags(const unsigned long long* flags, int world, unsigned long long ep, int* status) {
     const unsigned long long t0 = globaltimer();
     for (int p = 0; p < world; ++p) {
-        while (ld_acquire_sys(flags + p) < ep) {
+        while (ld_relaxed_sys(flags + p) < ep) {
             if (globaltimer() - t0 > kWaitLimitNs) {
                 atomicOr(status, MPK_DEV_TIMEOUT);
                 return false;
             }
-            __nanosleep(100);
         }
     }
+    __threadfence_system();
     return true;
+}
+
+/* The sum over ranks of one int64 of the sums region, the loads of all ranks
+ * issued before any is used (eight at a time).  Plain L2-level loads: a peer's
+ * memory is not cached in this GPU's L2, and the flag wait ordered them. */
+__device__ __forceinline__ long long sum_over_ranks(const PeerBases& bases, int world, size_t index) {
+    long long total = 0;
+    for (int p0 = 0; p0 < world; p0 += 8) {
+        long long v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            v[u] = p0 + u < world
+                       ? __ldcg(reinterpret_cast<const long long*>(reinterpret_cast<const uint8_t*>(bases.p[p0 + u]) +
+                                                                   kOffS) + index)
+                       : 0;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) total += v[u];
+    }
+    return total;
 }
 
 __global__ void __launch_bounds__(256)
@@ -91,14 +122,8 @@ k_peer_combine(PeerBases bases, int rank, int world, int k, int d, const DevPara
     /* ---- 1: announce, then wait for every rank's sums ---- */
     if (t == 0) {
         ep_s = *reinterpret_cast<volatile unsigned long long*>(epoch);
-        if (blockIdx.x == 0) {
-            __threadfence_system();
-            for (int p = 0; p < world; ++p)
-                st_release_sys(reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(bases.p[p]) + kOffFlags) +
-                                   rank, ep_s);
-        }
+        if (blockIdx.x == 0) announce(bases, world, rank, ep_s);
         ok_s = wait_flags(flags, world, ep_s, status) ? 1 : 0;
-        __threadfence_system();
     }
     __syncthreads();
     const unsigned long long ep = ep_s;
@@ -111,17 +136,11 @@ k_peer_combine(PeerBases bases, int rank, int world, int k, int d, const DevPara
     if (ok) {
         const double inv = ldexp(1.0, -prm->frac);
         for (int j = j0 + (int)blockIdx.x; j < j1; j += (int)gridDim.x) {
-            long long cnt = 0;
-            for (int p = 0; p < world; ++p)
-                cnt += __ldcv(reinterpret_cast<const long long*>(reinterpret_cast<const uint8_t*>(bases.p[p]) + kOffS) +
-                              kd + j);
+            const long long cnt = sum_over_ranks(bases, world, (size_t)kd + j);
             float acc = 0.f;
             for (int f = t; f < d; f += 256) {
                 const size_t o = (size_t)j * d + f;
-                long long sum = 0;
-                for (int p = 0; p < world; ++p)
-                    sum += __ldcv(reinterpret_cast<const long long*>(reinterpret_cast<const uint8_t*>(bases.p[p]) +
-                                                                      kOffS) + o);
+                const long long sum = sum_over_ranks(bases, world, o);
                 const float old = C[o];
                 const float nv = cnt > 0 ? (float)(((double)sum * inv) / (double)cnt) : old;
                 C[o] = nv;
@@ -150,13 +169,9 @@ k_peer_combine(PeerBases bases, int rank, int world, int k, int d, const DevPara
         if (atomicAdd(done, 1u) == gridDim.x - 1) {
             *done = 0;
             *reinterpret_cast<volatile unsigned long long*>(epoch) = ep + 1;
-            __threadfence_system();
-            for (int p = 0; p < world; ++p)
-                st_release_sys(reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(bases.p[p]) + kOffFlags) +
-                                   kPeerMax + rank, ep);
+            announce(bases, world, kPeerMax + rank, ep);
         }
         ok_s = (ok && wait_flags(flags + kPeerMax, world, ep, status)) ? 1 : 0;
-        __threadfence_system();
     }
     __syncthreads();
     if (!ok_s) return;
@@ -171,9 +186,16 @@ k_peer_combine(PeerBases bases, int rank, int world, int k, int d, const DevPara
         const float* Xp = reinterpret_cast<const float*>(pb + ox);
         const float* Mp = reinterpret_cast<const float*>(pb + om);
         const long long e0 = (long long)q0 * d, e1 = (long long)q1 * d;
-        for (long long e = e0 + tid; e < e1; e += nthr) C[e] = __ldcv(Xp + e);
+        if ((d & 3) == 0) {                       /* rows of 16-byte multiples: float4 copies */
+            const float4* src = reinterpret_cast<const float4*>(Xp + e0);
+            float4* dst = reinterpret_cast<float4*>(C + e0);
+            const long long nv = (e1 - e0) >> 2;
+            for (long long e = tid; e < nv; e += nthr) dst[e] = __ldcg(src + e);
+        } else {
+            for (long long e = e0 + tid; e < e1; e += nthr) C[e] = __ldcg(Xp + e);
+        }
         if (moved2)
-            for (long long j = q0 + tid; j < q1; j += nthr) moved2[j] = __ldcv(Mp + j);
+            for (long long j = q0 + tid; j < q1; j += nthr) moved2[j] = __ldcg(Mp + j);
     }
 }
 
