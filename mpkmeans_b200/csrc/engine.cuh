@@ -127,7 +127,7 @@ cudaError_t launch_assign(const AssignArgs& a, cudaStream_t s);
 void launch_refine(const float* P, const float* C, const float* cn, int d, int k, int bn,
                    const RefineEntry* list, DevParams* prm, int* labels, long long n_cap,
                    unsigned long long* hist, int hist_cap, const __half* Xs, long long n, int dp,
-                   const WideScratch& w, int num_sms, cudaStream_t s);
+                   const WideScratch& w, int num_sms, cudaStream_t s, int blocks_per_sm = 4);
 void launch_wide_gather(const RefineEntry* list, const __half* Xs, long long n, int dp, const WideScratch& w,
                         long long base, const DevParams* prm, int num_sms, cudaStream_t s);
 void launch_refine_wide(const float* P, const float* C, const float* cn, int d, int k, const RefineEntry* list,
@@ -151,7 +151,7 @@ int launch_update_sorted(const float* P, long long n, int d, const int* labels, 
 int launch_update_sort(long long n, const int* labels, int k, DevParams* prm, long long* counts, UpdateScratch sc,
                        int num_sms, cudaStream_t s);
 int launch_update_sum(const float* P, long long n, int d, int k, DevParams* prm, long long* sums, UpdateScratch sc,
-                      int num_sms, cudaStream_t s);
+                      int num_sms, cudaStream_t s, bool leave_room);
 /* Overlapping the refinement with the segmented sum: snapshot the listed
  * rows' labels before the refinement (old, capacity cap entries); after it,
  * move every row whose label changed between the clusters' sums and counts

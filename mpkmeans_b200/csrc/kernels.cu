@@ -773,13 +773,15 @@ void launch_refine_wide(const float* P, const float* C, const float* cn, int d, 
 
 void launch_refine(const float* P, const float* C, const float* cn, int d, int k, int bn, const RefineEntry* list,
                    DevParams* prm, int* labels, long long n_cap, unsigned long long* hist, int hist_cap,
-                   const __half* Xs, long long n, int dp, const WideScratch& w, int num_sms, cudaStream_t s) {
+                   const __half* Xs, long long n, int dp, const WideScratch& w, int num_sms, cudaStream_t s,
+                   int blocks_per_sm) {
+    /* grid-stride over the entries: any grid works; four blocks a SM fill the register file,
+     * one leaves the rest of each SM to a kernel running beside it */
+    const int grid = num_sms * (blocks_per_sm > 0 ? blocks_per_sm : 4);
     if (d <= 256)
-        k_refine<8><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, bn, list, prm, labels, n_cap, hist, hist_cap, Xs, n,
-                                                 dp, w);
+        k_refine<8><<<grid, 256, 0, s>>>(P, C, cn, d, k, bn, list, prm, labels, n_cap, hist, hist_cap, Xs, n, dp, w);
     else
-        k_refine<0><<<num_sms * 4, 256, 0, s>>>(P, C, cn, d, k, bn, list, prm, labels, n_cap, hist, hist_cap, Xs, n,
-                                                 dp, w);
+        k_refine<0><<<grid, 256, 0, s>>>(P, C, cn, d, k, bn, list, prm, labels, n_cap, hist, hist_cap, Xs, n, dp, w);
 }
 
 void launch_finalize_fixed(const long long* sums, const long long* counts, int k, int d, const DevParams* prm,

@@ -460,15 +460,30 @@ static mpkStatus engine_assign_tc(mpkEngine e, const float* dC, int* dAssign, in
 /* The FP32 refinement of the rows the last engine_assign_tc listed.
  * record_hist: the refinement writes its entry count to the next slot of the
  * engine's survivor history (prm->hist_next counts the slots used). */
+/* Which part of the refinement to launch: all of it; the per-row FP32 pass
+ * (k_refine: small blocks that can run beside other kernels); or the wide
+ * rounds and the tiled full scan that follow it (tensor-core and shared-memory
+ * heavy kernels that occupy whole SMs). */
+enum RefinePart { REFINE_ALL, REFINE_ROWS, REFINE_WIDE };
+
 static mpkStatus engine_refine(mpkEngine e, const float* dC, int* dAssign, bool record_hist,
-                               cudaStream_t rs = nullptr) {
+                               cudaStream_t rs = nullptr, RefinePart part = REFINE_ALL) {
     if (e->n == 0) return MPK_OK;
     if (!rs) rs = e->s;
-    prof_mark(e, e->ev_refine, rs);
-    launch_refine(e->P, dC, e->cn, e->d, e->k, assign_bn_for(e->k), e->list, e->prm, dAssign, e->n,
-                  record_hist ? e->hist : nullptr, MPK_MAX_HIST, e->Xs, e->n, e->dp,
-                  e->wide, e->num_sms, rs);
-    ++e->launches;
+    if (part != REFINE_WIDE) prof_mark(e, e->ev_refine, rs);
+    if (part != REFINE_WIDE) {
+        /* beside the segmented sum (REFINE_ROWS), the sum's one wave keeps three block slots a
+         * SM and the refinement's first blocks take the fourth; the rest start as the sum's
+         * blocks retire (a heavy refinement, as at config 5, then still gets the whole GPU) */
+        launch_refine(e->P, dC, e->cn, e->d, e->k, assign_bn_for(e->k), e->list, e->prm, dAssign, e->n,
+                      record_hist ? e->hist : nullptr, MPK_MAX_HIST, e->Xs, e->n, e->dp,
+                      e->wide, e->num_sms, rs);
+        ++e->launches;
+    }
+    if (part == REFINE_ROWS) {
+        prof_mark(e, e->ev_refine, rs);
+        return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
+    }
     /* rows the refinement queued: per round, a tensor-core pass that lists their
      * candidates, then the FP32 evaluation of just those (every launch sizes itself from
      * prm->nwide; rounds past the queue exit at once) */
@@ -496,7 +511,7 @@ static mpkStatus engine_refine(mpkEngine e, const float* dC, int* dAssign, bool 
         launch_full_scan(e->P, dC, e->cn, e->d, e->k, e->wide.scan, e->prm, dAssign, e->num_sms, rs);
         ++e->launches;
     }
-    prof_mark(e, e->ev_refine, rs);
+    if (part != REFINE_WIDE) prof_mark(e, e->ev_refine, rs);
     return cudaGetLastError() == cudaSuccess ? MPK_OK : MPK_ERR_CUDA;
 }
 
@@ -548,11 +563,13 @@ static mpkStatus engine_finalize(mpkEngine e, const long long* dSums, float* dC,
 /* The refinement of the rows the last engine_assign_tc listed and the update,
  * overlapped (finalize: then the finalisation too, into dMoved2 if given).
  * The counting sort reads the assignment's labels; then the latency-bound
- * refinement runs on the second stream beside the bandwidth-bound segmented
- * sum of those labels: it snapshots the listed rows' labels, refines them,
- * and moves every row whose label changed from its old cluster's sums and
- * count to the new one's.  The integer sums come out exactly as an update
- * of the refined labels would give them. */
+ * per-row refinement runs on the second stream beside the bandwidth-bound
+ * segmented sum of those labels (which leaves each SM room for it), after
+ * snapshotting the listed rows' labels.  After the join come the wide rounds
+ * and the full scan (kernels that need whole SMs; they exit at once when no row
+ * needs them), and then every listed row whose label changed moves from its old
+ * cluster's sums and count to the new one's.  The integer sums come out
+ * exactly as an update of the refined labels would give them. */
 static mpkStatus engine_refine_update(mpkEngine e, float* dC, int* dAssign, long long* dSums, bool record_hist,
                                       bool finalize, float* dMoved2) {
     const long long kd = (long long)e->k * e->d;
@@ -562,12 +579,13 @@ static mpkStatus engine_refine_update(mpkEngine e, float* dC, int* dAssign, long
     cudaEventRecord(e->ev_fork, e->s);
     cudaStreamWaitEvent(e->s2, e->ev_fork, 0);
     e->launches += launch_refine_snapshot(e->list, e->prm, dAssign, e->old_lab, e->n, e->num_sms, e->s2);
-    mpkStatus st = engine_refine(e, dC, dAssign, record_hist, e->s2);
-    e->launches += launch_refine_correct(e->P, e->d, e->list, e->prm, dAssign, e->old_lab, e->n, e->k, dSums,
-                                         e->num_sms, e->s2);
-    e->launches += launch_update_sum(e->P, e->n, e->d, e->k, e->prm, dSums, e->us, e->num_sms, e->s);
+    mpkStatus st = engine_refine(e, dC, dAssign, record_hist, e->s2, REFINE_ROWS);
+    e->launches += launch_update_sum(e->P, e->n, e->d, e->k, e->prm, dSums, e->us, e->num_sms, e->s, true);
     cudaEventRecord(e->ev_join2, e->s2);
     cudaStreamWaitEvent(e->s, e->ev_join2, 0);       /* always joined, so a capture can end */
+    if (st == MPK_OK) st = engine_refine(e, dC, dAssign, record_hist, e->s, REFINE_WIDE);
+    e->launches += launch_refine_correct(e->P, e->d, e->list, e->prm, dAssign, e->old_lab, e->n, e->k, dSums,
+                                         e->num_sms, e->s);
     prof_mark(e, e->ev_accum);
     if (st == MPK_OK && finalize) st = engine_finalize(e, dSums, dC, dMoved2);
     if (st != MPK_OK) return st;

@@ -351,14 +351,16 @@ int launch_update_sort(long long n, const int* labels, int k, DevParams* prm, lo
 }
 
 int launch_update_sum(const float* P, long long n, int d, int k, DevParams* prm, long long* sums, UpdateScratch sc,
-                      int num_sms, cudaStream_t s) {
+                      int num_sms, cudaStream_t s, bool leave_room) {
     if (n <= 0) return 0;
     const bool vec = (d % 4 == 0) && ((reinterpret_cast<uintptr_t>(P) & 15) == 0);
-    /* eight warps a block, about eight blocks per SM over all feature slices; at least 32
-     * rows a warp, so that a small problem does not pay a bin search and a flush of atomics
-     * for every handful of rows */
+    /* eight warps a block, over all feature slices about eight blocks per SM (two waves of
+     * four, which fill the register file); leave_room: one wave of three blocks per SM, so
+     * that a kernel running beside it (the refinement) keeps a block's worth of each SM.
+     * At least 32 rows a warp, so that a small problem does not pay a bin search and a
+     * flush of atomics for every handful of rows. */
     const int ny = ceil_div(d, vec ? 128 : 32);
-    const long long want = std::max<long long>(1, (long long)num_sms * 8 / ny);   /* whole waves */
+    const long long want = std::max<long long>(1, (long long)num_sms * (leave_room ? 3 : 8) / ny);   /* whole waves */
     const dim3 grid((unsigned)std::max<long long>(1, std::min<long long>(want, (n + 255) / 256)), (unsigned)ny);
     if (vec) k_segsum<4><<<grid, 256, 0, s>>>(P, d, sc.perm, sc.bin_start, k, prm, sums);
     else k_segsum<1><<<grid, 256, 0, s>>>(P, d, sc.perm, sc.bin_start, k, prm, sums);
@@ -368,7 +370,7 @@ int launch_update_sum(const float* P, long long n, int d, int k, DevParams* prm,
 int launch_update_sorted(const float* P, long long n, int d, const int* labels, int k, DevParams* prm,
                          long long* sums, long long* counts, UpdateScratch sc, int num_sms, cudaStream_t s) {
     const int a = launch_update_sort(n, labels, k, prm, counts, sc, num_sms, s);
-    return a + launch_update_sum(P, n, d, k, prm, sums, sc, num_sms, s);
+    return a + launch_update_sum(P, n, d, k, prm, sums, sc, num_sms, s, false);
 }
 
 int launch_refine_snapshot(const RefineEntry* list, const DevParams* prm, const int* labels, int* old, long long cap,
