@@ -339,7 +339,8 @@ int launch_update_sort(long long n, const int* labels, int k, DevParams* prm, lo
     if (k <= kLocalSortMaxK) {
         const size_t sb = 2 * sizeof(int) * (size_t)k + (size_t)kChunkRows * (sizeof(int) + sizeof(short));
         if (sb > 48 * 1024) cudaFuncSetAttribute(k_label_scatter_local, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sb);
-        const int sblocks = num_sms * 2;
+        /* as many blocks as fit a SM (four at k = 1024), each chunk's phases latency-bound */
+        const int sblocks = num_sms * std::max(1, std::min(4, (int)((227 * 1024) / (sb + 1024))));
         const long long srpb = (n + sblocks - 1) / sblocks;
         k_label_scatter_local<<<sblocks, kScatterThreads, sb, s>>>(labels, n, k, sc.cursor, sc.perm, srpb);
         return 3;
