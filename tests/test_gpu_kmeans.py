@@ -563,6 +563,45 @@ def test_refine_overlap_equals_sequential(cuda, kind):
             assert torch.equal(a, b), key
 
 
+def test_engine_step_empty_and_tiny_shards(cuda):
+    """mpkEngineStep (graphs, the refinement beside the update) on shards with no
+    rows, fewer rows than centroids and a few thousand rows: the shards' sums
+    add up to one engine's over all rows, and Finalize then gives its
+    centroids, for three iterations."""
+    P, C = make_problem(6000, 40, 300, seed=15)
+    dP = dev(P)
+    pmax = float(max(np.abs(P).max(), np.abs(C).max()))
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        whole = M.Engine(dP, 300, pmax_global=pmax, n_global=6000, stream=side.cuda_stream)
+        cuts = [(0, 0), (0, 3), (3, 3), (3, 6000)]
+        shards = [M.Engine(dP[a:b], 300, pmax_global=pmax, n_global=6000, stream=side.cuda_stream) for a, b in cuts]
+        try:
+            Cw, Cs = dev(C), dev(C)
+            lab_w = torch.empty(6000, dtype=torch.int32, device="cuda")
+            sums_w = torch.empty(whole.sums_length, dtype=torch.int64, device="cuda")
+            labs = [torch.empty(b - a, dtype=torch.int32, device="cuda") for a, b in cuts]
+            sums = [torch.empty(whole.sums_length, dtype=torch.int64, device="cuda") for _ in cuts]
+            for _ in range(3):
+                whole.step(Cw, lab_w, sums_w)
+                whole.finalize(sums_w, Cw)
+                for e, lab, sm in zip(shards, labs, sums):
+                    e.step(Cs, lab, sm)
+                tot = sums[0] + sums[1] + sums[2] + sums[3]
+                shards[3].finalize(tot, Cs)
+                side.synchronize()
+                assert torch.equal(tot, sums_w)
+                assert torch.equal(torch.cat(labs), lab_w)
+                assert torch.equal(Cs, Cw)
+            for e in [whole] + shards:
+                assert e.counters()["status"] == 0
+        finally:
+            side.synchronize()
+            whole.close()
+            for e in shards:
+                e.close()
+
+
 def test_tiled_full_scan_bit_exact_shifted_offset(cuda):
     """Cancellation stress with the reference driver's non-negativity shift
     (P += max|P|) and few points per cluster: most wide rows overflow their
