@@ -719,7 +719,7 @@ int assign_supported(int d) { return d >= 1 && d <= kMaxDim; }
 cudaError_t launch_assign(const AssignArgs& a, cudaStream_t s) {
     if (a.n <= 0) return cudaSuccess;
     if (a.emit) {
-        /* the wide path exists only for k > kWideRescan, where the tiles are 256 wide */
+        /* the wide path exists only for k > kWideMinK, where the tiles are 256 wide */
         if (assign_bn_for(a.k) != 256 || !a.wide) return cudaErrorInvalidValue;
         return launch_bn<256, true>(a, s);
     }

@@ -55,7 +55,7 @@ struct RefineEntry {
 static_assert(sizeof(RefineEntry) == 80, "refinement entry layout");
 
 /* Wide refinement.  A flagged row whose overflowing classes hold more than
- * kWideRescan columns in all is not rescanned class by class: it is queued
+ * rescan_limit columns in all is not rescanned class by class: it is queued
  * (went), and in rounds of `cap` rows its split planes are copied to Xw, a
  * second tensor-core pass over those rows emits every column within the
  * row's bound (up to kWideCand / 2 per tile half), and the FP32 evaluation
@@ -63,7 +63,16 @@ static_assert(sizeof(RefineEntry) == 80, "refinement entry layout");
  * sizes itself from prm->nwide on the device; rounds past the queue exit at
  * once. */
 constexpr int kWideCand = 512;
-constexpr int kWideRescan = 256;
+/* the wide path's tensor-core pass runs on 256-wide centroid tiles: k > 128 */
+constexpr int kWideMinK = 128;
+/* Class-rescan columns above which a row goes wide.  The wide pass costs a
+ * fixed ~20 us (a tensor-core launch over whole SMs, after the update's
+ * join); class rescans cost FP32 dots in the refinement, which runs beside
+ * the update's segmented sum and hides there on small shards.  Measured at
+ * k = 1024: at 1e7 rows sending every rescan row wide (32 columns) takes
+ * 0.09 ms off an iteration; at 1.25e6 rows it adds 0.02 ms, so small shards
+ * keep 256.  Either way the labels are the same, bit for bit. */
+inline int wide_rescan_limit(long long n) { return n >= (1LL << 22) ? 32 : 256; }
 struct WideScratch {
     __half* Xw;          /* 2 planes x cap x dp FP16: one round's rows */
     int* went;           /* n: refinement-entry index of each queued row */
@@ -73,6 +82,7 @@ struct WideScratch {
     long long cap;       /* rows Xw holds (its plane stride); 0: no wide path (small k) */
     long long per_round; /* rows per round, <= cap */
     int rounds;          /* rounds per assignment; queued rows past them rescan their classes */
+    int rescan_limit;    /* class-rescan columns above which a row goes wide (wide_rescan_limit) */
 };
 
 /* Widest row the tiled full scan (k_full_scan) stages in shared memory. */

@@ -226,7 +226,7 @@ __global__ void k_refine(const float* __restrict__ P, const float* __restrict__ 
         const RefineEntry E = list[e];
         if (w.cap > 0 && (E.ovf[0] | E.ovf[1])) {
             const int classes = __popc((unsigned)E.ovf[0]) + __popc((unsigned)E.ovf[1]);
-            if ((long long)classes * ((k + 15) / 16) > kWideRescan) {
+            if ((long long)classes * ((k + 15) / 16) > w.rescan_limit) {
                 unsigned slot = 0;
                 if (lane == 0) {
                     slot = atomicAdd(&prm->nwide, 1u);

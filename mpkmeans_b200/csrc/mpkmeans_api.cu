@@ -190,7 +190,7 @@ struct mpkEngine_s {
     unsigned long long* hist = nullptr;   /* MPK_MAX_HIST slots */
     UpdateScratch us{nullptr, nullptr, nullptr, nullptr};
     CUtensorMap tmX, tmC, tmCh, tmXw;   /* tmCh: centroid planes in 128-row halves (CTA pairs) */
-    WideScratch wide{nullptr, nullptr, nullptr, nullptr, nullptr, 0, 0, 0};
+    WideScratch wide{nullptr, nullptr, nullptr, nullptr, nullptr, 0, 0, 0, 256};
     BoundConsts bc;
     float4* dbg = nullptr;                /* test hook, set by mpkDebugSetAssignTrace */
     int stall = -1;                       /* test hook, set by mpkDebugInjectStall */
@@ -326,15 +326,17 @@ static mpkStatus engine_create(mpkEngine* out, const float* dP, long long n, int
         ALLOC(e->cn, (size_t)e->kpad * sizeof(float));
         ALLOC(e->list, (size_t)(n > 0 ? n : 1) * sizeof(RefineEntry));
         ALLOC(e->old_lab, (size_t)(n > 0 ? n : 1) * sizeof(int));
-        /* the wide path: only when some row could need more than kWideRescan
-         * class-rescan columns (16 classes of k/16) */
-        if (k > kWideRescan && n > 0) {
+        /* the wide path (rows whose class rescans would visit more than
+         * wide.rescan_limit columns): its tensor-core pass needs 256-wide centroid
+         * tiles, k > kWideMinK */
+        if (k > kWideMinK && n > 0) {
             const long long cap = std::min<long long>(n, std::max<long long>(65536, (n + 7) / 8));
             e->wide.cap = cap;
             e->wide.per_round = cap;
             /* every queued row gets a round when classes are wide (k >= 4096: 256+ columns a
              * class); below that one round, and rows past it rescan their classes */
             e->wide.rounds = k >= 4096 ? (int)((n + cap - 1) / cap) : 1;
+            e->wide.rescan_limit = wide_rescan_limit(n);
             ALLOC(e->wide.Xw, (size_t)2 * cap * e->dp * sizeof(__half));
             ALLOC(e->wide.went, (size_t)n * sizeof(int));
             ALLOC(e->wide.cand, (size_t)cap * kWideCand * sizeof(int));
