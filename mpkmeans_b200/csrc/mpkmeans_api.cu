@@ -329,7 +329,8 @@ static mpkStatus engine_create(mpkEngine* out, const float* dP, long long n, int
         /* the wide path (rows whose class rescans would visit more than
          * wide.rescan_limit columns): its tensor-core pass needs 256-wide centroid
          * tiles, k > kWideMinK */
-        if (k > kWideMinK && n > 0) {
+        /* (16 classes of ceil(k/16) columns: a row can exceed the limit only when they do) */
+        if (k > kWideMinK && n > 0 && 16LL * ((k + 15) / 16) > wide_rescan_limit(n)) {
             const long long cap = std::min<long long>(n, std::max<long long>(65536, (n + 7) / 8));
             e->wide.cap = cap;
             e->wide.per_round = cap;
