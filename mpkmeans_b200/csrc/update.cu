@@ -6,7 +6,10 @@
  *
  *   k_label_hist     labels -> per-cluster counts (shared-memory histogram)
  *   k_bin_scan       counts -> bin starts; counts written to the sums buffer
- *   k_label_scatter  row indices grouped by label (perm)
+ *   k_label_scatter_local   row indices grouped by label (perm): each block
+ *                    sorts 8192-row chunks in shared memory and writes every
+ *                    label's run contiguously (k <= 4096; k_label_scatter,
+ *                    row by row, above)
  *   k_segsum         each warp walks a contiguous run of perm over one
  *                    128-feature slice of the rows (coalesced, 16 B per lane),
  *                    quantising every coordinate once to q = rint(x * 2^frac)
@@ -16,7 +19,11 @@
  *
  * Integer sums are exact, so the result does not depend on the order of the
  * rows within a cluster, on the split of the work, or on the number of GPUs
- * whose buffers are later summed; the points are read from HBM once.
+ * whose buffers are later summed; the points are read from HBM once.  The
+ * same exactness lets the refinement run beside the segmented sum:
+ * k_refine_snapshot keeps the listed rows' labels before it, and
+ * k_refine_correct moves every row it relabelled between the clusters'
+ * sums and counts afterwards.
  */
 #include "engine.cuh"
 
