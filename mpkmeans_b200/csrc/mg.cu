@@ -297,6 +297,20 @@ extern "C" mpkStatus mpkMeansMixedMG(int ngpu, const int* devices, const float* 
         if (refine) mpk::fill_exclusions(S, P, rows_all, S->hp_update);
     }
 done:
+    /* Invariant before the synchronisations below: no stream holds a collective that
+     * could wait for ever.  On success every collective has completed (mg_wait).  On
+     * an error a collective may be in flight (a group launch that failed part way, or
+     * a step that failed after others' allreduces were enqueued), so any communicator
+     * still alive is aborted first, which ends its kernels; mg_wait's own failures
+     * have aborted theirs already (comm[g] is then null). */
+    if (rc != MPK_OK)
+        for (int g = 0; g < ngpu; ++g)
+            if (comm[g]) {
+                cudaSetDevice(devices[g]);
+                if (N.abort) N.abort(comm[g]);
+                else N.commDestroy(comm[g]);
+                comm[g] = nullptr;
+            }
     for (int g = 0; g < ngpu; ++g) {
         cudaSetDevice(devices[g]);
         if (st[g]) cudaStreamSynchronize(st[g]);
