@@ -293,32 +293,46 @@ __global__ void k_refine_snapshot(const RefineEntry* __restrict__ list, const De
 
 /* After the refinement: every listed row whose label it changed from a to b
  * moves its fixed-point coordinates from cluster a's sums to b's and one count
- * with them (one warp per entry).  Integer adds commute, so this may run
- * beside the segmented sum of the same update, and the result equals an
- * update from the refined labels exactly. */
+ * with them.  One thread checks each entry; the warp then moves its changed
+ * rows one at a time, its lanes over the row's features.  Integer adds
+ * commute, so this may run beside the segmented sum of the same update, and
+ * the result equals an update from the refined labels exactly. */
 __global__ void k_refine_correct(const float* __restrict__ P, int d, const RefineEntry* __restrict__ list,
                                  const DevParams* __restrict__ prm, const int* __restrict__ labels,
                                  const int* __restrict__ old, long long cap, int k, long long* __restrict__ sums) {
     const long long nf = min((long long)prm->nflag, cap);
     const int lane = threadIdx.x & 31;
-    const long long nw = (long long)gridDim.x * (blockDim.x >> 5);
+    const long long nthr = (long long)gridDim.x * blockDim.x;
     const float sc = ldexpf(1.0f, prm->frac);
     long long* counts = sums + (size_t)k * d;
-    for (long long e = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); e < nf; e += nw) {
-        const int row = list[e].row;
-        const int a = old[e], b = labels[row];
-        if (a == b || (unsigned)a >= (unsigned)k || (unsigned)b >= (unsigned)k) continue;   /* warp-uniform */
-        const float* p = P + (size_t)row * d;
-        for (int f = lane; f < d; f += 32) {
-            const long long q = quantise(p[f], sc);
-            if (q) {
-                atomicAdd(reinterpret_cast<unsigned long long*>(&sums[(size_t)b * d + f]), (unsigned long long)q);
-                atomicAdd(reinterpret_cast<unsigned long long*>(&sums[(size_t)a * d + f]), (unsigned long long)(-q));
-            }
+    /* warp-uniform trip count: every lane of a warp runs the same bases */
+    for (long long base = (long long)blockIdx.x * blockDim.x + (threadIdx.x & ~31); base < nf; base += nthr) {
+        const long long e = base + lane;
+        int row = 0, a = 0, b = 0;
+        bool moved = false;
+        if (e < nf) {
+            row = list[e].row;
+            a = old[e];
+            b = labels[row];
+            moved = a != b && (unsigned)a < (unsigned)k && (unsigned)b < (unsigned)k;
         }
-        if (lane == 0) {
-            atomicAdd(reinterpret_cast<unsigned long long*>(&counts[b]), 1ull);
-            atomicAdd(reinterpret_cast<unsigned long long*>(&counts[a]), ~0ull);   /* -1 */
+        unsigned m = __ballot_sync(FULL, moved);
+        while (m) {
+            const int src = __ffs(m) - 1;
+            m &= m - 1;
+            const int r = __shfl_sync(FULL, row, src), ra = __shfl_sync(FULL, a, src), rb = __shfl_sync(FULL, b, src);
+            const float* p = P + (size_t)r * d;
+            for (int f = lane; f < d; f += 32) {
+                const long long q = quantise(p[f], sc);
+                if (q) {
+                    atomicAdd(reinterpret_cast<unsigned long long*>(&sums[(size_t)rb * d + f]), (unsigned long long)q);
+                    atomicAdd(reinterpret_cast<unsigned long long*>(&sums[(size_t)ra * d + f]), (unsigned long long)(-q));
+                }
+            }
+            if (lane == 0) {
+                atomicAdd(reinterpret_cast<unsigned long long*>(&counts[rb]), 1ull);
+                atomicAdd(reinterpret_cast<unsigned long long*>(&counts[ra]), ~0ull);   /* -1 */
+            }
         }
     }
 }
@@ -389,7 +403,7 @@ int launch_refine_snapshot(const RefineEntry* list, const DevParams* prm, const 
 
 int launch_refine_correct(const float* P, int d, const RefineEntry* list, const DevParams* prm, const int* labels,
                           const int* old, long long cap, int k, long long* sums, int num_sms, cudaStream_t s) {
-    k_refine_correct<<<num_sms * 4, 256, 0, s>>>(P, d, list, prm, labels, old, cap, k, sums);
+    k_refine_correct<<<num_sms * 2, 256, 0, s>>>(P, d, list, prm, labels, old, cap, k, sums);
     return 1;
 }
 
