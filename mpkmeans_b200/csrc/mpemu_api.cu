@@ -39,20 +39,46 @@ __device__ __forceinline__ float from_word(__nv_bfloat16 w) { return __bfloat162
 __device__ __forceinline__ float from_word(__half w) { return __half2float(w); }
 
 /* Every element of a column-major rows x cols matrix: a = scale * A(r, c);
- * word s = round(a), a -= word (exact), for s = 0..nsplits-1. */
-template <typename W>
+ * word s = round(a), a -= word (exact), for s = 0..nsplits-1.  Columns go to
+ * blockIdx.y, four consecutive rows to a thread: VEC (A 16-byte aligned with
+ * lda % 4 == 0, S 8-byte aligned with lds and stride % 4 == 0) loads the four
+ * with one float4 and stores each plane's four words with one 8-byte store;
+ * the arithmetic per element is the same either way. */
+template <typename W, bool VEC>
 __global__ void k_split(const float* __restrict__ A, long long lda, long long rows, long long cols, int nsplits,
                         float scale, W* __restrict__ S, long long lds, long long stride) {
-    const long long total = rows * cols;
-    const long long step = (long long)gridDim.x * blockDim.x;
-    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += step) {
-        const long long c = e / rows, r = e - c * rows;
-        float a = A[c * lda + r] * scale;
-        W* dst = S + c * lds + r;
-        for (int s = 0; s < nsplits; ++s) {
-            const W w = to_word<W>(a);
-            dst[(long long)s * stride] = w;
-            a = a - from_word(w);
+    const long long rstep = (long long)gridDim.x * blockDim.x * 4;
+    for (long long c = blockIdx.y; c < cols; c += gridDim.y) {
+        const float* a_col = A + c * lda;
+        W* s_col = S + c * lds;
+        for (long long r0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4; r0 < rows; r0 += rstep) {
+            const bool full = r0 + 3 < rows;
+            float v[4];
+            if (VEC && full) {
+                const float4 t = *reinterpret_cast<const float4*>(a_col + r0);
+                v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+            } else {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) v[u] = r0 + u < rows ? a_col[r0 + u] : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = v[u] * scale;
+            for (int sp = 0; sp < nsplits; ++sp) {
+                W w[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    w[u] = to_word<W>(v[u]);
+                    v[u] = v[u] - from_word(w[u]);
+                }
+                W* dst = s_col + (long long)sp * stride + r0;
+                if (VEC && full) {
+                    *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(w);
+                } else {
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        if (r0 + u < rows) dst[u] = w[u];
+                }
+            }
         }
     }
 }
@@ -323,7 +349,15 @@ mpemuStatus_t split_impl(const float* dA, int64_t lda, int64_t rows, int64_t col
     if (lda < rows || lds < rows) return MPEMU_STATUS_INVALID_VALUE;
     if (stride < lds * cols) return MPEMU_STATUS_INVALID_VALUE;
     if (rows == 0 || cols == 0) return MPEMU_STATUS_SUCCESS;
-    k_split<W><<<grid_for(rows * cols), kBlock, 0, s>>>(dA, lda, rows, cols, nsplits, scale, dS, lds, stride);
+    /* blocks over the rows of a column (four rows a thread), columns on y; about 16 blocks
+     * a SM in all */
+    const long long xb = std::max<long long>(1, std::min<long long>((rows + 4 * kBlock - 1) / (4 * kBlock), 148 * 16));
+    const long long yb = std::max<long long>(1, std::min<long long>(cols, std::max<long long>(1, 148 * 16 / xb)));
+    const dim3 grid((unsigned)xb, (unsigned)std::min<long long>(yb, 65535));
+    const bool vec = (reinterpret_cast<uintptr_t>(dA) % 16 == 0) && lda % 4 == 0 &&
+                     (reinterpret_cast<uintptr_t>(dS) % 8 == 0) && lds % 4 == 0 && stride % 4 == 0;
+    if (vec) k_split<W, true><<<grid, kBlock, 0, s>>>(dA, lda, rows, cols, nsplits, scale, dS, lds, stride);
+    else k_split<W, false><<<grid, kBlock, 0, s>>>(dA, lda, rows, cols, nsplits, scale, dS, lds, stride);
     return cudaGetLastError() == cudaSuccess ? MPEMU_STATUS_SUCCESS : MPEMU_STATUS_CUDA_ERROR;
 }
 
