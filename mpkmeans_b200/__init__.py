@@ -345,9 +345,21 @@ class PeerGroup:
         check("mpkPeerCombine", lib().mpkPeerCombine(self.h, engine.h, _ptr(C), _ptr(moved2)))
 
     def close(self) -> None:
-        if self.h:
+        if getattr(self, "h", None):
             lib().mpkPeerDestroy(self.h)
             self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:                        # noqa: BLE001 - interpreter shutdown
+            pass
 
 
 class Engine:

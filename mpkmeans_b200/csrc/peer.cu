@@ -225,6 +225,17 @@ struct mpkPeerGroup_s {
     bool connected = false;
 };
 
+/* Runs `fn` with the group's device current, then restores the caller's. */
+template <typename F>
+static mpkStatus on_device(int dev, F&& fn) {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != dev && cudaSetDevice(dev) != cudaSuccess) return MPK_ERR_CUDA;
+    const mpkStatus st = fn();
+    if (prev != dev) cudaSetDevice(prev);
+    return st;
+}
+
 extern "C" {
 
 mpkStatus mpkPeerCreate(mpkPeerGroup* out, int rank, int world, int k, int d) {
@@ -273,6 +284,8 @@ mpkStatus mpkPeerLocalBase(mpkPeerGroup g, void** base) {
 
 mpkStatus mpkPeerConnect(mpkPeerGroup g, const void* const* handles64, void* const* bases, const int* devices) {
     if (!g || g->connected || (!handles64 && !bases)) return MPK_ERR_INVALID;
+    /* peer access and IPC mappings belong to the context of the group's device */
+    return on_device(g->dev, [&]() -> mpkStatus {
     for (int p = 0; p < g->world; ++p) {
         if (p == g->rank) continue;
         if (bases && bases[p]) {
@@ -304,6 +317,7 @@ mpkStatus mpkPeerConnect(mpkPeerGroup g, const void* const* handles64, void* con
     }
     g->connected = true;
     return MPK_OK;
+    });
 }
 
 long long* mpkPeerSums(mpkPeerGroup g) {
@@ -312,12 +326,16 @@ long long* mpkPeerSums(mpkPeerGroup g) {
 
 mpkStatus mpkPeerDestroy(mpkPeerGroup g) {
     if (!g) return MPK_ERR_INVALID;
-    cudaDeviceSynchronize();
-    for (int p = 0; p < g->world; ++p)
-        if (g->imported[p]) cudaIpcCloseMemHandle(g->bases.p[p]);
-    cudaFree(g->base);
+    const mpkStatus st = on_device(g->dev, [&]() -> mpkStatus {
+        /* no combine of this rank may still read the peers' blocks or its own */
+        cudaDeviceSynchronize();
+        for (int p = 0; p < g->world; ++p)
+            if (g->imported[p]) cudaIpcCloseMemHandle(g->bases.p[p]);
+        cudaFree(g->base);
+        return MPK_OK;
+    });
     delete g;
-    return MPK_OK;
+    return st;
 }
 
 }  /* extern "C" */
