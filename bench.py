@@ -244,6 +244,19 @@ class Clocks:
         except OSError:
             self.p = None
 
+    def wait_ready(self, limit_s=5.0):
+        """Return once nvidia-smi has written its first sample (or after limit_s): from then on
+        a sample falls every 50 ms, so even a timed region shorter than that has one within the
+        25 ms kept on either side of it."""
+        t0 = time.time()
+        while self.p is not None and time.time() - t0 < limit_s:
+            try:
+                if any(l.count(",") >= 9 for l in Path(self.f.name).read_text().splitlines()):
+                    return
+            except OSError:
+                pass
+            time.sleep(0.02)
+
     def stop(self, window=None):
         if self.p is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
@@ -392,7 +405,7 @@ def run_lloyd(wl, world, rank, local, steps, warmup, n_override=None, e2e=False,
     if world > 1:
         dist.barrier()
     clocks = Clocks(local)
-    time.sleep(0.3)
+    clocks.wait_ready()
     eng.profile(True)
     launches0 = eng.launches()
     ar = []
